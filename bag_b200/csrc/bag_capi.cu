@@ -1,0 +1,888 @@
+// C ABI and host plan builder of the B200-native BAG FP32 matmul.
+//
+// The builder turns one call into (a) at most a few materialisation stages and
+// (b) grouped leaf launches.  It walks the recursion of the reference
+// (bag.cuh:152-245): at each level an operand that is a sum of several blocks
+// is first rounded into the workspace, exactly where the reference's
+// prepare_child (bag.cuh:124-135) rounds it, the Full basis materialises its
+// transformed quadrants where prepare<true> does (bag.cuh:66-68), and the
+// seven products' operand combinations at the deepest level are fused into the
+// GEMM prologue.  Outputs skip the reference's T workspace: each leaf product
+// carries the signed list of C blocks the composed inverse transforms send it
+// to (bag.py:530-533 for one level), so there is no decode kernel.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdint>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/bag_capi.h"
+#include "bag_kernels.h"
+
+struct bag_workspace {
+  int m, n, k, depth, basis, batch;
+  int device;
+  float* data;
+  size_t elements;
+};
+
+namespace bag_b200 {
+namespace {
+
+thread_local std::string g_last_error;
+thread_local cudaEvent_t g_prof_start = nullptr;
+thread_local cudaEvent_t g_prof_end = nullptr;
+std::atomic<unsigned long long> g_launches{0};
+
+struct Error : std::runtime_error {
+  bag_status status;
+  Error(bag_status s, const std::string& what) : std::runtime_error(what), status(s) {}
+};
+
+[[noreturn]] void fail(bag_status s, const std::string& what) { throw Error(s, what); }
+
+void cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail(BAG_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int sm_count_for_current_device() {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  int dev = 0;
+  cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int count = 0;
+  cuda_check(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev),
+             "cudaDeviceGetAttribute");
+  cache[dev] = count;
+  return count;
+}
+
+// ---------------------------------------------------------------------------
+// Plan builder.
+// ---------------------------------------------------------------------------
+
+struct View {
+  const float* p;
+  long long ld;
+  long long bstride;
+  bool operator==(const View& o) const { return p == o.p && ld == o.ld && bstride == o.bstride; }
+};
+
+struct STerm {
+  View v;
+  float coef;
+};
+using Expr = std::vector<STerm>;
+
+struct Target {
+  View v;
+  float coef;
+  int mode;
+};
+
+struct HostLeaf {
+  int m, n, k;
+  Expr left, right;
+  std::vector<Target> out;
+};
+
+struct HostJob {
+  int rows, cols;
+  std::vector<View> in;
+  std::vector<View> out;
+  std::vector<std::vector<int>> expr;   // signed (input index + 1)
+};
+
+enum BasisKind { kMinimal = BAG_BASIS_MINIMAL, kFull = BAG_BASIS_FULL, kClassic = BAG_BASIS_CLASSIC };
+
+// One level of each algorithm: operand combinations over quadrants
+// (0=X11, 1=X12, 2=X21, 3=X22) as ordered signed terms, and the signed C
+// quadrants the product is added to.
+struct Combo {
+  int n;
+  int q[4];
+  int s[4];
+};
+struct LevelProduct {
+  Combo left, right;
+  int out[4];   // coefficient per C quadrant
+};
+
+// Minimal basis: operand sums in the order the reference evaluates them
+// (SA = A12 - A21 + A22 as in bag.cuh:72; SA - A11 as x + delta*y with
+// x = SA, bag.cuh:118), outputs from the composed inverse transform
+// C11=M4+M5, C12=M3+M5-M6-M2, C21=M1-M3-M5-M7, C22=M1+M2-M3-M5 (bag.py:530-533).
+const LevelProduct kMinimal7[7] = {
+    {{2, {1, 3}, {1, 1}}, {2, {1, 3}, {1, 1}}, {0, 0, 1, 1}},                     // M1
+    {{2, {3, 2}, {1, -1}}, {2, {3, 2}, {1, -1}}, {0, -1, 0, 1}},                  // M2
+    {{3, {1, 2, 3}, {1, -1, 1}}, {3, {1, 2, 3}, {1, -1, 1}}, {0, 1, -1, -1}},     // M3
+    {{1, {0}, {1}}, {1, {0}, {1}}, {1, 0, 0, 0}},                                 // M4
+    {{1, {1}, {1}}, {1, {2}, {1}}, {1, 1, -1, -1}},                               // M5
+    {{4, {1, 2, 3, 0}, {1, -1, 1, -1}}, {1, {1}, {1}}, {0, -1, 0, 0}},            // M6
+    {{1, {2}, {1}}, {4, {1, 2, 3, 0}, {1, -1, 1, -1}}, {0, 0, -1, 0}},            // M7
+};
+
+// Full basis: operands are x + delta*y over the transformed quadrants
+// T11=X11, T12=X12-X21+X22, T21=X22-X21, T22=X12+X22 (bag.cuh:101-110, 171-189).
+const LevelProduct kFull7[7] = {
+    {{1, {3}, {1}}, {1, {3}, {1}}, {0, 0, 1, 1}},
+    {{1, {2}, {1}}, {1, {2}, {1}}, {0, -1, 0, 1}},
+    {{1, {1}, {1}}, {1, {1}, {1}}, {0, 1, -1, -1}},
+    {{1, {0}, {1}}, {1, {0}, {1}}, {1, 0, 0, 0}},
+    {{2, {1, 2}, {1, -1}}, {2, {3, 1}, {1, -1}}, {1, 1, -1, -1}},
+    {{2, {1, 0}, {1, -1}}, {2, {1, 2}, {1, -1}}, {0, -1, 0, 0}},
+    {{2, {3, 1}, {1, -1}}, {2, {1, 0}, {1, -1}}, {0, 0, -1, 0}},
+};
+
+// Classic Strassen-1969, strassen.cuh:131-153 (x + delta*y, v + eps*w order).
+const LevelProduct kClassic7[7] = {
+    {{2, {2, 3}, {1, 1}}, {1, {0}, {1}}, {0, 0, 1, -1}},
+    {{2, {0, 1}, {1, 1}}, {1, {3}, {1}}, {-1, 1, 0, 0}},
+    {{2, {2, 0}, {1, -1}}, {2, {0, 1}, {1, 1}}, {0, 0, 0, 1}},
+    {{2, {1, 3}, {1, -1}}, {2, {2, 3}, {1, 1}}, {1, 0, 0, 0}},
+    {{1, {0}, {1}}, {2, {1, 3}, {1, -1}}, {0, 1, 0, 1}},
+    {{1, {3}, {1}}, {2, {2, 0}, {1, -1}}, {1, 0, 1, 0}},
+    {{2, {0, 3}, {1, 1}}, {2, {0, 3}, {1, 1}}, {1, 0, 0, 1}},
+};
+
+struct Builder {
+  int basis;
+  float* ws = nullptr;      // workspace base (may be a fake base for dumps)
+  size_t ws_used = 0;       // elements per batch entry
+  long long ws_bstride = 0; // elements between batch entries' workspaces
+  struct Buf {
+    const float* begin;
+    const float* end;
+    int stage;
+  };
+  std::vector<Buf> bufs;
+  std::vector<std::vector<HostJob>> stages;   // stages[s-1]: jobs of stage s
+  std::vector<HostLeaf> leaves;
+
+  int stage_of(const View& v) const {
+    for (const Buf& b : bufs)
+      if (v.p >= b.begin && v.p < b.end) return b.stage;
+    return 0;
+  }
+
+  View alloc(int rows, int cols, int stage) {
+    const long long ld = std::max<long long>(4, (rows + 3) / 4 * 4);
+    const size_t count = size_t(ld) * cols;
+    const size_t begin = (ws_used + 63) / 64 * 64;   // 256-byte aligned
+    ws_used = begin + count;
+    const float* p = ws + begin;
+    bufs.push_back({p, p + std::max<size_t>(count, 1), stage});
+    return {p, ld, ws_bstride};
+  }
+
+  // Round a signed sum of blocks into the workspace (one job output).
+  View materialize(const Expr& e, int rows, int cols) {
+    int stage = 1;
+    for (const STerm& t : e) stage = std::max(stage, stage_of(t.v) + 1);
+    if ((int)stages.size() < stage) stages.resize(stage);
+    const View out = alloc(rows, cols, stage);
+    auto& jobs = stages[stage - 1];
+    // Join the job that already reads most of these blocks, so one pass over
+    // a quadrant set writes all of its combinations.
+    HostJob* best = nullptr;
+    int best_overlap = 0;
+    for (HostJob& j : jobs) {
+      if (j.rows != rows || j.cols != cols || (int)j.out.size() >= kMaxJobOutputs) continue;
+      int overlap = 0;
+      size_t fresh = 0;
+      for (const STerm& t : e) {
+        if (std::find(j.in.begin(), j.in.end(), t.v) != j.in.end()) ++overlap;
+        else ++fresh;
+      }
+      if (overlap > best_overlap && j.in.size() + fresh <= size_t(kMaxJobInputs)) {
+        best = &j;
+        best_overlap = overlap;
+      }
+    }
+    if (best) {
+      HostJob& j = *best;
+      std::vector<View>& in = j.in;
+      for (const STerm& t : e)
+        if (std::find(in.begin(), in.end(), t.v) == in.end()) in.push_back(t.v);
+      std::vector<int> code;
+      for (const STerm& t : e) {
+        const int idx = int(std::find(in.begin(), in.end(), t.v) - in.begin()) + 1;
+        code.push_back(t.coef > 0 ? idx : -idx);
+      }
+      j.out.push_back(out);
+      j.expr.push_back(code);
+      return out;
+    }
+    HostJob j;
+    j.rows = rows;
+    j.cols = cols;
+    std::vector<int> code;
+    for (const STerm& t : e) {
+      j.in.push_back(t.v);
+      code.push_back(t.coef > 0 ? int(j.in.size()) : -int(j.in.size()));
+    }
+    j.out.push_back(out);
+    j.expr.push_back(code);
+    jobs.push_back(j);
+    return out;
+  }
+
+  // Reduce an operand to a single unit-coefficient block.  A lone negated
+  // block keeps its data; the sign moves to the outputs (exact).
+  View single(const Expr& e, int rows, int cols, float* sign) {
+    if (e.size() == 1) {
+      *sign = e[0].coef;
+      return e[0].v;
+    }
+    *sign = 1.f;
+    return materialize(e, rows, cols);
+  }
+
+  static void quads(const View& v, int rows, int cols, View q[4]) {
+    const long long h = rows / 2, w = (long long)(cols / 2) * v.ld;
+    q[0] = {v.p, v.ld, v.bstride};
+    q[1] = {v.p + w, v.ld, v.bstride};
+    q[2] = {v.p + h, v.ld, v.bstride};
+    q[3] = {v.p + h + w, v.ld, v.bstride};
+  }
+
+  // Full-basis transform of one operand's quadrants (bag.cuh:66-68):
+  // T11 = X11 (a view), T12 = X12 - X21 + X22, T21 = X22 - X21, T22 = X12 + X22.
+  void full_transform(const View q[4], int rows, int cols, View t[4]) {
+    t[0] = q[0];
+    t[1] = materialize({{q[1], 1.f}, {q[2], -1.f}, {q[3], 1.f}}, rows, cols);
+    t[2] = materialize({{q[3], 1.f}, {q[2], -1.f}}, rows, cols);
+    t[3] = materialize({{q[1], 1.f}, {q[3], 1.f}}, rows, cols);
+  }
+
+  void expand(const Expr& L, const Expr& R, const std::vector<Target>& T, int m, int k, int n,
+              int depth) {
+    if (depth == 0) {
+      leaves.push_back({m, n, k, L, R, T});
+      return;
+    }
+    float ls = 1.f, rs = 1.f;
+    const View lv = single(L, m, k, &ls);
+    const View rv = single(R, k, n, &rs);
+    View lq[4], rq[4];
+    quads(lv, m, k, lq);
+    quads(rv, k, n, rq);
+    const int h = m / 2, kk = k / 2, w = n / 2;
+    const LevelProduct* table = basis == kFull ? kFull7 : basis == kClassic ? kClassic7 : kMinimal7;
+    if (basis == kFull) {
+      View lt[4], rt[4];
+      full_transform(lq, h, kk, lt);
+      full_transform(rq, kk, w, rt);
+      std::copy(lt, lt + 4, lq);
+      std::copy(rt, rt + 4, rq);
+    }
+    for (int p = 0; p < 7; ++p) {
+      const LevelProduct& lp = table[p];
+      Expr l, r;
+      for (int i = 0; i < lp.left.n; ++i) l.push_back({lq[lp.left.q[i]], float(lp.left.s[i])});
+      for (int i = 0; i < lp.right.n; ++i) r.push_back({rq[lp.right.q[i]], float(lp.right.s[i])});
+      std::vector<Target> t;
+      for (const Target& tg : T) {
+        View cq[4];
+        quads(tg.v, m, n, cq);
+        for (int q = 0; q < 4; ++q)
+          if (lp.out[q]) t.push_back({cq[q], tg.coef * ls * rs * float(lp.out[q]), tg.mode});
+      }
+      expand(l, r, t, h, kk, w, depth - 1);
+    }
+  }
+};
+
+struct GemmDesc {
+  int m, n, k;                 // column-major C(m x n) += A(m x k) B(k x n)
+  const float* a;
+  long long lda, sa;
+  const float* b;
+  long long ldb, sb;
+  float* c;
+  long long ldc, sc;
+  int batch;
+  int depth, basis;
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Build the plan; ws may be a fake base when only sizes are wanted.
+void build_plan(const GemmDesc& g, float* ws, long long ws_bstride, Builder& B) {
+  B.basis = g.basis;
+  B.ws = ws;
+  B.ws_bstride = ws_bstride;
+  const View A{g.a, g.lda, g.sa}, Bv{g.b, g.ldb, g.sb}, C{g.c, g.ldc, g.sc};
+  if (g.m == 0 || g.n == 0) return;
+  int depth = g.depth;
+  // Peel so every level halves exactly and block offsets stay 16-byte aligned.
+  const int align = 4 << depth;
+  int mc = g.m - g.m % align, kc = g.k - g.k % align, nc = g.n - g.n % align;
+  if (depth == 0 || mc == 0 || kc == 0 || nc == 0) {
+    B.leaves.push_back({g.m, g.n, g.k, {{A, 1.f}}, {{Bv, 1.f}}, {{C, 1.f, kOutAtomic}}});
+    return;
+  }
+  B.expand({{A, 1.f}}, {{Bv, 1.f}}, {{C, 1.f, kOutAtomic}}, mc, kc, nc, depth);
+  if (kc < g.k)
+    B.leaves.push_back({mc, nc, g.k - kc, {{{A.p + (long long)kc * A.ld, A.ld, A.bstride}, 1.f}},
+                        {{{Bv.p + kc, Bv.ld, Bv.bstride}, 1.f}}, {{C, 1.f, kOutAtomic}}});
+  if (mc < g.m)
+    B.leaves.push_back({g.m - mc, g.n, g.k, {{{A.p + mc, A.ld, A.bstride}, 1.f}}, {{Bv, 1.f}},
+                        {{{C.p + mc, C.ld, C.bstride}, 1.f, kOutAtomic}}});
+  if (nc < g.n)
+    B.leaves.push_back({mc, g.n - nc, g.k, {{A, 1.f}},
+                        {{{Bv.p + (long long)nc * Bv.ld, Bv.ld, Bv.bstride}, 1.f}},
+                        {{{C.p + (long long)nc * C.ld, C.ld, C.bstride}, 1.f, kOutAtomic}}});
+}
+
+// Workspace elements per batch entry (dry run with a fake base).
+size_t plan_workspace_elements(GemmDesc g) {
+  static float fake;
+  Builder B;
+  g.a = g.b = &fake;
+  g.c = &fake;
+  build_plan(g, reinterpret_cast<float*>(uintptr_t(1) << 44), 0, B);
+  return B.ws_used;
+}
+
+int choose_tile(const std::vector<HostLeaf>& leaves, int sm_count) {
+  long long tiles = 0;
+  const TileShape big = leaf_tile_shape(kTileLarge);
+  for (const HostLeaf& l : leaves)
+    tiles += (long long)((l.m + big.bm - 1) / big.bm) * ((l.n + big.bn - 1) / big.bn);
+  return tiles < 2LL * sm_count ? kTileSmall : kTileLarge;
+}
+
+void check_ld(long long ld) {
+  if (ld <= 0 || ld > INT32_MAX) fail(BAG_ERR_INVALID, "leading dimension out of range");
+}
+
+Term make_term(const View& v, float coef, int mode) {
+  check_ld(v.ld);
+  Term t{};
+  t.p = v.p;
+  t.bstride = v.bstride;
+  t.ld = int(v.ld);
+  t.coef = coef;
+  t.mode = mode;
+  return t;
+}
+
+bool view_vec_ok(const View& v) { return aligned16(v.p) && v.ld % 4 == 0 && v.bstride % 4 == 0; }
+
+void execute_plan(Builder& B, int batch, cudaStream_t stream) {
+  const int sms = sm_count_for_current_device();
+  // Materialisation stages.
+  for (const auto& jobs : B.stages) {
+    for (size_t j0 = 0; j0 < jobs.size(); j0 += kMaxJobs) {
+      MatPlan mp{};
+      long long chunks = 0;
+      for (size_t j = j0; j < std::min(jobs.size(), j0 + kMaxJobs); ++j) {
+        const HostJob& hj = jobs[j];
+        MatJob& J = mp.job[mp.njobs];
+        J.rows = hj.rows;
+        J.cols = hj.cols;
+        J.nin = int(hj.in.size());
+        J.nout = int(hj.out.size());
+        for (int i = 0; i < J.nin; ++i) J.in[i] = make_term(hj.in[i], 1.f, 0);
+        for (int o = 0; o < J.nout; ++o) {
+          J.out[o] = make_term(hj.out[o], 1.f, 0);
+          for (size_t t = 0; t < hj.expr[o].size(); ++t) J.expr[o][t] = (signed char)hj.expr[o][t];
+        }
+        mp.chunk_begin[mp.njobs] = chunks;
+        chunks += (long long)((hj.rows + 3) / 4) * hj.cols;
+        ++mp.njobs;
+      }
+      mp.chunk_begin[mp.njobs] = chunks;
+      cuda_check(launch_materialize(mp, batch, stream, sms), "materialize launch");
+      ++g_launches;
+    }
+  }
+  if (g_prof_start) cuda_check(cudaEventRecord(g_prof_start, stream), "cudaEventRecord");
+  // Leaf products, grouped into as few launches as the parameter block allows.
+  const int cfg = choose_tile(B.leaves, sms);
+  const TileShape ts = leaf_tile_shape(cfg);
+  bool vec = true;
+  for (const HostLeaf& l : B.leaves) {
+    for (const STerm& t : l.left) vec = vec && view_vec_ok(t.v);
+    for (const STerm& t : l.right) vec = vec && view_vec_ok(t.v);
+    for (const Target& t : l.out) vec = vec && view_vec_ok(t.v);
+  }
+  size_t i = 0;
+  while (i < B.leaves.size()) {
+    LeafPlan lp;
+    lp.nprod = 0;
+    lp.ntiles = 0;
+    int nterms = 0;
+    while (i < B.leaves.size() && lp.nprod < kMaxProducts) {
+      const HostLeaf& l = B.leaves[i];
+      const int need = int(l.left.size() + l.right.size() + l.out.size());
+      if (nterms + need > kMaxTerms) break;
+      if ((int)l.left.size() > kMaxOperandTerms || (int)l.right.size() > kMaxOperandTerms)
+        fail(BAG_ERR_INTERNAL, "operand has more fused terms than the kernel takes");
+      Prod& P = lp.prod[lp.nprod];
+      P.m = l.m;
+      P.n = l.n;
+      P.k = l.k;
+      P.tiles_m = (l.m + ts.bm - 1) / ts.bm;
+      P.tiles_n = (l.n + ts.bn - 1) / ts.bn;
+      P.tile_begin = lp.ntiles;
+      P.l0 = short(nterms);
+      P.nl = short(l.left.size());
+      for (const STerm& t : l.left) lp.terms[nterms++] = make_term(t.v, t.coef, 0);
+      P.r0 = short(nterms);
+      P.nr = short(l.right.size());
+      for (const STerm& t : l.right) lp.terms[nterms++] = make_term(t.v, t.coef, 0);
+      P.o0 = short(nterms);
+      P.no = short(l.out.size());
+      for (const Target& t : l.out) lp.terms[nterms++] = make_term(t.v, t.coef, t.mode);
+      const long long tiles = (long long)P.tiles_m * P.tiles_n;
+      if (tiles > 0) {
+        if ((long long)lp.ntiles + tiles > INT32_MAX) fail(BAG_ERR_SHAPE, "problem too large");
+        lp.ntiles += int(tiles);
+        ++lp.nprod;
+      }
+      ++i;
+    }
+    if (lp.nprod == 0 && i < B.leaves.size()) fail(BAG_ERR_INTERNAL, "plan chunking failed");
+    cuda_check(launch_leaf(lp, cfg, vec, batch, stream), "leaf launch");
+    if (lp.nprod) ++g_launches;
+  }
+  if (g_prof_end) cuda_check(cudaEventRecord(g_prof_end, stream), "cudaEventRecord");
+}
+
+void check_device_workspace(const bag_workspace* ws) {
+  int dev = 0;
+  cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (ws->device != dev) fail(BAG_ERR_WORKSPACE, "workspace belongs to another device");
+}
+
+void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
+  if (g.m < 0 || g.n < 0 || g.k < 0) fail(BAG_ERR_SHAPE, "negative extent");
+  if (g.depth < 0 || g.depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8");
+  if (g.basis != kMinimal && g.basis != kFull && g.basis != kClassic)
+    fail(BAG_ERR_INVALID, "unknown basis");
+  if (beta != 0.f && beta != 1.f) fail(BAG_ERR_UNSUPPORTED, "beta must be 0 or 1");
+  if (g.batch < 0) fail(BAG_ERR_INVALID, "negative batch");
+  if (g.m == 0 || g.n == 0 || g.batch == 0) return;
+  if (!g.a || !g.b || !g.c) fail(BAG_ERR_INVALID, "null matrix pointer");
+  if (g.lda < std::max(1, g.m) || g.ldb < std::max(1, g.k) || g.ldc < std::max(1, g.m))
+    fail(BAG_ERR_INVALID, "leading dimension smaller than the row count");
+  if (beta == 0.f) {
+    for (int i = 0; i < g.batch; ++i)
+      cuda_check(cudaMemset2DAsync(g.c + (long long)i * g.sc, size_t(g.ldc) * sizeof(float), 0,
+                                   size_t(g.m) * sizeof(float), size_t(g.n), stream),
+                 "cudaMemset2DAsync");
+  }
+  if (g.k == 0) return;
+  const size_t need = plan_workspace_elements(g);
+  float* base = nullptr;
+  if (need) {
+    if (!ws) fail(BAG_ERR_WORKSPACE, "this plan needs a workspace");
+    check_device_workspace(ws);
+    if (need * size_t(g.batch) > ws->elements)
+      fail(BAG_ERR_WORKSPACE, "workspace too small for this problem");
+    base = ws->data;
+  }
+  Builder B;
+  build_plan(g, base ? base : reinterpret_cast<float*>(uintptr_t(1) << 44), (long long)need, B);
+  if (B.ws_used != need) fail(BAG_ERR_INTERNAL, "plan size changed between passes");
+  execute_plan(B, g.batch, stream);
+}
+
+GemmDesc make_desc(int layout, int m, int n, int k, const float* a, long long lda, long long sa,
+                   const float* b, long long ldb, long long sb, float* c, long long ldc,
+                   long long sc, int batch, int depth, int basis) {
+  if (layout != BAG_LAYOUT_COL_MAJOR && layout != BAG_LAYOUT_ROW_MAJOR)
+    fail(BAG_ERR_INVALID, "unknown layout");
+  GemmDesc g{};
+  if (layout == BAG_LAYOUT_COL_MAJOR) {
+    g = {m, n, k, a, lda, sa, b, ldb, sb, c, ldc, sc, batch, depth, basis};
+  } else {
+    // Row-major C = A B is column-major C^T = B^T A^T: swap the operands.
+    g = {n, m, k, b, ldb, sb, a, lda, sa, c, ldc, sc, batch, depth, basis};
+  }
+  return g;
+}
+
+bool valid_shape_impl(int backend, int s) {
+  if (s <= 0 || s % 4) return false;
+  switch (backend) {
+    case BAG_BACKEND_LEGACY:
+      return s % ((s <= 384) ? 16 : (s <= 1024 && s != 1024) ? 32 : (s <= 4096) ? 64 : 128) == 0;
+    case BAG_BACKEND_LARGE: return s % 64 == 0;
+    case BAG_BACKEND_MEDIUM: return s % 32 == 0;
+    case BAG_BACKEND_HUGE: return s % 128 == 0;
+    default: return true;
+  }
+}
+
+bool paired_backend(int backend) {
+  return backend == BAG_BACKEND_COLUMN_TILE8 || backend == BAG_BACKEND_HUGE ||
+         backend == BAG_BACKEND_PIPE64X32 || backend == BAG_BACKEND_DEFERRED_SWIZZLE64;
+}
+
+void check_backend(int backend) {
+  if (backend < 0 || backend >= BAG_BACKEND_COUNT) fail(BAG_ERR_INVALID, "unknown backend");
+}
+
+size_t local_elements_impl(int n, int depth, int basis) {
+  if (depth < 1) fail(BAG_ERR_SHAPE, "BAG depth must be positive");
+  int size = n;
+  for (int level = 0; level < depth; ++level, size /= 2)
+    if (size <= 0 || size % 8) fail(BAG_ERR_SHAPE, "each BAG level requires N divisible by 8");
+  const size_t count = size_t(n) * n;
+  return basis == BAG_BASIS_FULL ? 3 * count : count + count / 2;
+}
+
+template <class F>
+bag_status guarded(F&& f) {
+  try {
+    f();
+    return BAG_OK;
+  } catch (const Error& e) {
+    g_last_error = e.what();
+    return e.status;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return BAG_ERR_INTERNAL;
+  } catch (...) {
+    g_last_error = "unknown error";
+    return BAG_ERR_INTERNAL;
+  }
+}
+
+// JSON dump of a plan built against fake, far-apart base pointers.
+std::string dump_plan(int m, int n, int k, long long lda, long long ldb, long long ldc, int depth,
+                      int basis) {
+  const uintptr_t unit = uintptr_t(1) << 40;
+  GemmDesc g{m, n, k, reinterpret_cast<const float*>(unit), lda, 0,
+             reinterpret_cast<const float*>(2 * unit), ldb, 0,
+             reinterpret_cast<float*>(3 * unit), ldc, 0, 1, depth, basis};
+  Builder B;
+  build_plan(g, reinterpret_cast<float*>(4 * unit), 0, B);
+  auto ref = [&](const View& v) {
+    const uintptr_t p = reinterpret_cast<uintptr_t>(v.p);
+    const uintptr_t base = p / unit;
+    const long long off = (long long)((p - base * unit) / sizeof(float));
+    return "[" + std::to_string(int(base) - 1) + "," + std::to_string(off) + "," +
+           std::to_string(v.ld) + "]";
+  };
+  std::string s = "{\"workspace_elements\":" + std::to_string(B.ws_used) + ",\"stages\":[";
+  for (size_t si = 0; si < B.stages.size(); ++si) {
+    s += si ? ",[" : "[";
+    for (size_t j = 0; j < B.stages[si].size(); ++j) {
+      const HostJob& hj = B.stages[si][j];
+      s += j ? "," : "";
+      s += "{\"rows\":" + std::to_string(hj.rows) + ",\"cols\":" + std::to_string(hj.cols) +
+           ",\"in\":[";
+      for (size_t i = 0; i < hj.in.size(); ++i) s += (i ? "," : "") + ref(hj.in[i]);
+      s += "],\"out\":[";
+      for (size_t o = 0; o < hj.out.size(); ++o) s += (o ? "," : "") + ref(hj.out[o]);
+      s += "],\"expr\":[";
+      for (size_t o = 0; o < hj.expr.size(); ++o) {
+        s += o ? ",[" : "[";
+        for (size_t t = 0; t < hj.expr[o].size(); ++t)
+          s += (t ? "," : "") + std::to_string(hj.expr[o][t]);
+        s += "]";
+      }
+      s += "]}";
+    }
+    s += "]";
+  }
+  s += "],\"leaves\":[";
+  for (size_t i = 0; i < B.leaves.size(); ++i) {
+    const HostLeaf& l = B.leaves[i];
+    s += i ? "," : "";
+    s += "{\"m\":" + std::to_string(l.m) + ",\"n\":" + std::to_string(l.n) +
+         ",\"k\":" + std::to_string(l.k) + ",\"left\":[";
+    for (size_t t = 0; t < l.left.size(); ++t)
+      s += std::string(t ? "," : "") + "[" + ref(l.left[t].v) + "," +
+           std::to_string(int(l.left[t].coef)) + "]";
+    s += "],\"right\":[";
+    for (size_t t = 0; t < l.right.size(); ++t)
+      s += std::string(t ? "," : "") + "[" + ref(l.right[t].v) + "," +
+           std::to_string(int(l.right[t].coef)) + "]";
+    s += "],\"out\":[";
+    for (size_t t = 0; t < l.out.size(); ++t)
+      s += std::string(t ? "," : "") + "[" + ref(l.out[t].v) + "," +
+           std::to_string(int(l.out[t].coef)) + "]";
+    s += "]}";
+  }
+  s += "]}";
+  return s;
+}
+
+}  // namespace
+}  // namespace bag_b200
+
+using namespace bag_b200;
+
+extern "C" {
+
+const char* bag_last_error(void) { return g_last_error.c_str(); }
+
+const char* bag_version(void) { return "bag_b200 0.1.0 (sm_100a)"; }
+
+bag_status bag_local_elements(int n, int depth, int basis, size_t* elements) {
+  return guarded([&] {
+    if (!elements) fail(BAG_ERR_INVALID, "null output pointer");
+    *elements = 0;
+    *elements = local_elements_impl(n, depth, basis);
+  });
+}
+
+bag_status bag_workspace_create_ex(int m, int n, int k, int depth, int basis, int batch,
+                                   bag_workspace** out) {
+  return guarded([&] {
+    if (!out) fail(BAG_ERR_INVALID, "null output pointer");
+    *out = nullptr;
+    if (m < 0 || n < 0 || k < 0 || batch < 0) fail(BAG_ERR_SHAPE, "negative extent");
+    if (depth < 0 || depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8");
+    if (basis != kMinimal && basis != kFull && basis != kClassic) fail(BAG_ERR_INVALID, "unknown basis");
+    GemmDesc g{m, n, k, nullptr, std::max(1, m), 0, nullptr, std::max(1, k), 0, nullptr,
+               std::max(1, m), 0, std::max(batch, 1), depth, basis};
+    const size_t per = plan_workspace_elements(g);
+    const size_t total = per * size_t(std::max(batch, 1));
+    auto* ws = new bag_workspace{m, n, k, depth, basis, batch, 0, nullptr, total};
+    cudaError_t e = cudaGetDevice(&ws->device);
+    if (e == cudaSuccess && total) e = cudaMalloc(&ws->data, total * sizeof(float));
+    if (e != cudaSuccess) {
+      delete ws;
+      cuda_check(e, "workspace allocation");
+    }
+    *out = ws;
+  });
+}
+
+bag_status bag_workspace_create(int n, int depth, int basis, bag_workspace** out) {
+  return guarded([&] {
+    if (!out) fail(BAG_ERR_INVALID, "null output pointer");
+    *out = nullptr;
+    if (basis != kMinimal && basis != kFull) fail(BAG_ERR_INVALID, "unknown basis");
+    local_elements_impl(n, depth, basis);   // the reference's shape rules (bag.cuh:23-30)
+    const bag_status s = bag_workspace_create_ex(n, n, n, depth, basis, 1, out);
+    if (s != BAG_OK) fail(s, g_last_error);
+  });
+}
+
+bag_status bag_workspace_destroy(bag_workspace* ws) {
+  return guarded([&] {
+    if (!ws) return;
+    if (ws->data) cudaFree(ws->data);
+    delete ws;
+  });
+}
+
+size_t bag_workspace_bytes(const bag_workspace* ws) {
+  return ws ? ws->elements * sizeof(float) : 0;
+}
+
+bag_status bag_matmul(const float* a, const float* b, float* c, int n, bag_stream_t stream,
+                      bag_workspace* ws, int backend, int schedule) {
+  return guarded([&] {
+    if (!ws) fail(BAG_ERR_WORKSPACE, "null workspace");
+    check_backend(backend);
+    if (schedule < BAG_SCHEDULE_SERIAL || schedule > BAG_SCHEDULE_BATCHED)
+      fail(BAG_ERR_INVALID, "unknown schedule");
+    if (n != ws->n || ws->m != ws->n || ws->k != ws->n) fail(BAG_ERR_WORKSPACE, "BAG workspace size mismatch");
+    int leaf = n;
+    for (int level = 0; level < ws->depth; ++level) leaf /= 2;
+    if (!valid_shape_impl(backend, leaf))
+      fail(BAG_ERR_SHAPE, "BAG leaf violates backend tile constraints");
+    if (schedule == BAG_SCHEDULE_BATCHED && !paired_backend(backend))
+      fail(BAG_ERR_UNSUPPORTED, "BAG batched schedule requires a paired backend");
+    run_gemm(make_desc(BAG_LAYOUT_COL_MAJOR, n, n, n, a, n, 0, b, n, 0, c, n, 0, 1, ws->depth,
+                       ws->basis),
+             1.f, reinterpret_cast<cudaStream_t>(stream), ws);
+  });
+}
+
+bag_status bag_sgemm_ex(int layout, int m, int n, int k, const float* a, long long lda,
+                        const float* b, long long ldb, float* c, long long ldc, float beta,
+                        int depth, int basis, bag_stream_t stream, bag_workspace* ws) {
+  return guarded([&] {
+    run_gemm(make_desc(layout, m, n, k, a, lda, 0, b, ldb, 0, c, ldc, 0, 1, depth, basis), beta,
+             reinterpret_cast<cudaStream_t>(stream), ws);
+  });
+}
+
+bag_status bag_sgemm_batched(int layout, int m, int n, int k, const float* a, long long lda,
+                             long long stride_a, const float* b, long long ldb, long long stride_b,
+                             float* c, long long ldc, long long stride_c, int batch, float beta,
+                             int depth, int basis, bag_stream_t stream, bag_workspace* ws) {
+  return guarded([&] {
+    if (batch > 65535) fail(BAG_ERR_SHAPE, "batch must be at most 65535");
+    run_gemm(make_desc(layout, m, n, k, a, lda, stride_a, b, ldb, stride_b, c, ldc, stride_c,
+                       batch, depth, basis),
+             beta, reinterpret_cast<cudaStream_t>(stream), ws);
+  });
+}
+
+}  // extern "C"
+
+namespace bag_b200 {
+namespace {
+
+void check_coeffs(int delta, int eps, int gd, int ge) {
+  if (delta < -1 || delta > 1) fail(BAG_ERR_INVALID, "delta must be -1, 0 or 1");
+  if (eps < -1 || eps > 1) fail(BAG_ERR_INVALID, "epsilon must be -1, 0 or 1");
+  if (gd < -2 || gd > 2) fail(BAG_ERR_INVALID, "gamma_d must be in -2..2");
+  if (ge < -2 || ge > 2) fail(BAG_ERR_INVALID, "gamma_e must be in -2..2");
+}
+
+HostLeaf primitive_leaf(int delta, int eps, int gd, int ge, int atomic, const float* x,
+                        const float* y, const float* v, const float* w, float* d, float* e, int m,
+                        int n, int k, long long ldx, long long ldy, long long ldv, long long ldw,
+                        long long ldd, long long lde) {
+  HostLeaf l;
+  l.m = m;
+  l.n = n;
+  l.k = k;
+  if (!x || !v) fail(BAG_ERR_INVALID, "x and v are required");
+  if (delta && !y) fail(BAG_ERR_INVALID, "y may be null only when delta == 0");
+  if (eps && !w) fail(BAG_ERR_INVALID, "w may be null only when epsilon == 0");
+  if (gd && !d) fail(BAG_ERR_INVALID, "d may be null only when gamma_d == 0");
+  if (ge && !e) fail(BAG_ERR_INVALID, "e may be null only when gamma_e == 0");
+  l.left.push_back({{x, ldx, 0}, 1.f});
+  if (delta) l.left.push_back({{y, ldy, 0}, float(delta)});
+  l.right.push_back({{v, ldv, 0}, 1.f});
+  if (eps) l.right.push_back({{w, ldw, 0}, float(eps)});
+  auto mode_of = [&](int g) {
+    return (g == 2 || g == -2) ? kOutOverwrite : (atomic ? kOutAtomic : kOutAdd);
+  };
+  auto coef_of = [](int g) { return g > 0 ? 1.f : -1.f; };
+  if (gd) l.out.push_back({{d, ldd, 0}, coef_of(gd), mode_of(gd)});
+  if (ge) l.out.push_back({{e, lde, 0}, coef_of(ge), mode_of(ge)});
+  return l;
+}
+
+void run_leaves(std::vector<HostLeaf> leaves, cudaStream_t stream) {
+  Builder B;
+  B.leaves = std::move(leaves);
+  execute_plan(B, 1, stream);
+}
+
+}  // namespace
+}  // namespace bag_b200
+
+extern "C" {
+
+bag_status bag_primitive(int delta, int eps, int gamma_d, int gamma_e, int atomic,
+                         const float* x, const float* y, const float* v, const float* w, float* d,
+                         float* e, int m, int n, int k, long long ldx, long long ldy, long long ldv,
+                         long long ldw, long long ldd, long long lde, bag_stream_t stream) {
+  return guarded([&] {
+    check_coeffs(delta, eps, gamma_d, gamma_e);
+    if (m < 0 || n < 0 || k < 0) fail(BAG_ERR_SHAPE, "negative extent");
+    if ((gamma_d == 0 && gamma_e == 0) || m == 0 || n == 0) return;
+    if (gamma_d && gamma_e && d == e && (gamma_d == 2 || gamma_d == -2 || gamma_e == 2 || gamma_e == -2))
+      fail(BAG_ERR_INVALID, "overwrite modes need distinct outputs");
+    auto ld_ok = [&](long long ld, int rows) { return ld >= std::max(1, rows); };
+    if (!ld_ok(ldx, m) || (delta && !ld_ok(ldy, m)) || !ld_ok(ldv, k) || (eps && !ld_ok(ldw, k)) ||
+        (gamma_d && !ld_ok(ldd, m)) || (gamma_e && !ld_ok(lde, m)))
+      fail(BAG_ERR_INVALID, "leading dimension smaller than the row count");
+    run_leaves({primitive_leaf(delta, eps, gamma_d, gamma_e, atomic, x, y, v, w, d, e, m, n, k,
+                               std::max(ldx, 1LL), std::max(ldy, 1LL), std::max(ldv, 1LL),
+                               std::max(ldw, 1LL), std::max(ldd, 1LL), std::max(lde, 1LL))},
+               reinterpret_cast<cudaStream_t>(stream));
+  });
+}
+
+bag_status bag_primitive_pair(int delta, int eps, int gamma_d, int gamma_e, int atomic,
+                              const float* const operands[8], float* const outputs[4], int s,
+                              long long ld, bag_stream_t stream) {
+  return guarded([&] {
+    check_coeffs(delta, eps, gamma_d, gamma_e);
+    if (!operands || !outputs) fail(BAG_ERR_INVALID, "null operand table");
+    if (s < 0) fail(BAG_ERR_SHAPE, "negative extent");
+    if (s == 0 || (gamma_d == 0 && gamma_e == 0)) return;
+    if (ld < s) fail(BAG_ERR_INVALID, "leading dimension smaller than the row count");
+    std::vector<HostLeaf> leaves;
+    for (int p = 0; p < 2; ++p)
+      leaves.push_back(primitive_leaf(delta, eps, gamma_d, gamma_e, atomic, operands[4 * p],
+                                      operands[4 * p + 1], operands[4 * p + 2],
+                                      operands[4 * p + 3], outputs[2 * p], outputs[2 * p + 1], s,
+                                      s, s, ld, ld, ld, ld, ld, ld));
+    run_leaves(std::move(leaves), reinterpret_cast<cudaStream_t>(stream));
+  });
+}
+
+bag_status bag_strassen_one_level(int backend, int schedule, const float* a, const float* b,
+                                  float* c, int n, bag_stream_t stream) {
+  return guarded([&] {
+    check_backend(backend);
+    if (schedule < BAG_STRASSEN_SERIAL_ATOMIC || schedule > BAG_STRASSEN_FOUR_BATCHED_ATOMIC)
+      fail(BAG_ERR_INVALID, "unknown schedule");
+    if (n <= 0 || n % 8) fail(BAG_ERR_SHAPE, "one_level currently requires N divisible by 8");
+    if (!valid_shape_impl(backend, n / 2))
+      fail(BAG_ERR_SHAPE, "shape violates original kernel tile constraints");
+    const bool normal = schedule == BAG_STRASSEN_SERIAL_NORMAL ||
+                        schedule == BAG_STRASSEN_DEPENDENCY_NORMAL ||
+                        schedule == BAG_STRASSEN_PAIRED_NORMAL;
+    if (normal && (backend == BAG_BACKEND_LEGACY || backend == BAG_BACKEND_MEDIUM ||
+                   backend == BAG_BACKEND_HUGE))
+      fail(BAG_ERR_UNSUPPORTED, "selected backend requires atomic updates");
+    if (schedule == BAG_STRASSEN_FOUR_BATCHED_ATOMIC && !paired_backend(backend))
+      fail(BAG_ERR_UNSUPPORTED, "four-variant batching requires a paired backend");
+    run_gemm(make_desc(BAG_LAYOUT_COL_MAJOR, n, n, n, a, n, 0, b, n, 0, c, n, 0, 1, 1, kClassic),
+             1.f, reinterpret_cast<cudaStream_t>(stream), nullptr);
+  });
+}
+
+bag_status bag_valid_shape(int backend, int s, int* valid) {
+  return guarded([&] {
+    if (!valid) fail(BAG_ERR_INVALID, "null output pointer");
+    check_backend(backend);
+    *valid = valid_shape_impl(backend, s) ? 1 : 0;
+  });
+}
+
+bag_status bag_profile_set_events(void* start_event, void* end_event) {
+  return guarded([&] {
+    if ((start_event == nullptr) != (end_event == nullptr))
+      fail(BAG_ERR_INVALID, "set both profiling events or neither");
+    g_prof_start = static_cast<cudaEvent_t>(start_event);
+    g_prof_end = static_cast<cudaEvent_t>(end_event);
+  });
+}
+
+unsigned long long bag_launch_count(void) { return g_launches.load(); }
+
+bag_status bag_ffma_probe(float* sink, int iterations, bag_stream_t stream, double* flops) {
+  return guarded([&] {
+    if (!sink || !flops || iterations <= 0) fail(BAG_ERR_INVALID, "bad probe arguments");
+    const int blocks = 4 * sm_count_for_current_device();
+    cuda_check(launch_ffma_probe(sink, blocks, iterations, reinterpret_cast<cudaStream_t>(stream),
+                                 flops),
+               "probe launch");
+  });
+}
+
+bag_status bag_plan_dump(int m, int n, int k, long long lda, long long ldb, long long ldc,
+                         int depth, int basis, char* buf, size_t buflen, size_t* needed) {
+  return guarded([&] {
+    if (m < 0 || n < 0 || k < 0) fail(BAG_ERR_SHAPE, "negative extent");
+    if (depth < 0 || depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8");
+    if (basis != kMinimal && basis != kFull && basis != kClassic) fail(BAG_ERR_INVALID, "unknown basis");
+    const std::string s = dump_plan(m, n, k, lda, ldb, ldc, depth, basis);
+    if (needed) *needed = s.size() + 1;
+    if (buf && buflen) {
+      const size_t len = std::min(buflen - 1, s.size());
+      std::memcpy(buf, s.data(), len);
+      buf[len] = 0;
+    }
+  });
+}
+
+}  // extern "C"

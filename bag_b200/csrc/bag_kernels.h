@@ -1,0 +1,34 @@
+// Host-side entry points of the sm_100a kernels (bag_kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "bag_plan.h"
+
+namespace bag_b200 {
+
+enum : int {
+  kTileLarge = 0,   // 128 x 128 CTA tile, 256 threads, 8 x 8 FFMA per thread
+  kTileSmall = 1,   // 64 x 64 CTA tile, 64 threads, for grids too small to fill 148 SMs
+};
+
+struct TileShape {
+  int bm, bn;
+};
+
+TileShape leaf_tile_shape(int config);
+
+// One grouped launch of every product in `plan`; grid = (plan.ntiles, batch).
+// `vec` selects 128-bit loads/stores and requires every term pointer 16-byte
+// aligned with ld % 4 == 0 and every block offset a multiple of 4 rows.
+cudaError_t launch_leaf(const LeafPlan& plan, int config, bool vec, int batch, cudaStream_t stream);
+
+// FP32 FFMA throughput probe over `blocks` CTAs of 256 threads; `sink` holds
+// blocks*256 floats.  *flops receives the FLOPs the launch performs.
+cudaError_t launch_ffma_probe(float* sink, int blocks, int iters, cudaStream_t stream,
+                              double* flops);
+
+// One launch of every materialisation job in `plan`.
+cudaError_t launch_materialize(const MatPlan& plan, int batch, cudaStream_t stream, int sm_count);
+
+}  // namespace bag_b200

@@ -1,0 +1,85 @@
+// Launch descriptors shared by the host plan builder and the sm_100a kernels.
+//
+// A BAG call is compiled on the host into two kinds of work:
+//
+//  * materialisation jobs ("MatPlan"): elementwise signed sums of up to four
+//    input blocks, written to workspace blocks.  Only operands that the
+//    reference itself rounds before recursing (bag.cuh:124-135 prepare_child,
+//    bag.cuh:66-68 the Full-basis transform) are materialised; everything at
+//    the deepest level is fused into the GEMM prologue.
+//  * leaf products ("LeafPlan"): every one of the 7^depth sub-products (plus
+//    peeling strips for ragged shapes) as one grouped launch.  A product is a
+//    list of signed left terms, signed right terms and signed output targets;
+//    the kernel sums the terms while staging tiles into shared memory and adds
+//    +-M into every C block the inverse transform sends it to.
+//
+// Both plans travel by value as __grid_constant__ kernel parameters, so a call
+// needs no device-side table, no upload and no allocation.
+#pragma once
+
+#include <cstdint>
+
+namespace bag_b200 {
+
+// One signed operand or output reference: p + batch*bstride is the block's
+// first element, column-major with leading dimension ld (elements).
+struct Term {
+  const float* p;
+  long long bstride;
+  int ld;
+  float coef;   // +1 / -1 for operand terms; the gamma sign for outputs
+  int mode;     // outputs only: kOutAtomic / kOutAdd / kOutOverwrite
+  int pad_;
+};
+
+// Output update modes of a product target.
+enum : int {
+  kOutAtomic = 0,     // atomicAdd (red.global) -- safe for concurrent writers
+  kOutAdd = 1,        // plain read-modify-write -- single writer only
+  kOutOverwrite = 2,  // store coef*M -- single writer only (gamma = +-2)
+};
+
+struct Prod {
+  int m, n, k;          // extents: left is m x k, right is k x n, output m x n
+  int tiles_m, tiles_n; // CTA tiles covering the output
+  int tile_begin;       // first work item of this product within the launch
+  short l0, nl;         // left terms  [l0, l0+nl) in LeafPlan::terms
+  short r0, nr;         // right terms
+  short o0, no;         // outputs
+};
+
+constexpr int kMaxProducts = 64;
+constexpr int kMaxTerms = 416;
+constexpr int kMaxOperandTerms = 4;   // per operand per product (fused transform)
+
+struct LeafPlan {
+  int nprod;
+  int ntiles;           // total work items (grid.x)
+  Prod prod[kMaxProducts];
+  Term terms[kMaxTerms];
+};
+
+constexpr int kMaxJobs = 24;
+constexpr int kMaxJobInputs = 4;
+constexpr int kMaxJobOutputs = 4;
+
+struct MatJob {
+  int rows, cols;
+  int nin, nout;
+  Term in[kMaxJobInputs];     // coef unused
+  Term out[kMaxJobOutputs];   // coef unused
+  // expr[o][t]: signed (input index + 1) of the t-th term of output o,
+  // evaluated left to right; 0 ends the list.
+  signed char expr[kMaxJobOutputs][kMaxJobInputs];
+};
+
+struct MatPlan {
+  int njobs;
+  long long chunk_begin[kMaxJobs + 1];   // prefix sums of float4 chunks per job
+  MatJob job[kMaxJobs];
+};
+
+static_assert(sizeof(LeafPlan) < 32000, "kernel parameter limit");
+static_assert(sizeof(MatPlan) < 32000, "kernel parameter limit");
+
+}  // namespace bag_b200

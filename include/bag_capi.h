@@ -1,0 +1,140 @@
+/*
+ * bag_capi.h -- C ABI of the B200-native BAG FP32 matrix multiply.
+ *
+ * Plain pointers, sizes and status codes; no C++ or torch types.  Every entry
+ * point is asynchronous on the given stream, allocates nothing (workspaces are
+ * created up front) and never throws: failures return a status and leave a
+ * message in bag_last_error() (thread-local).
+ *
+ * Reference interfaces replaced (liuyao0322/bag, path:line):
+ *   bag_workspace_create/_destroy/_bytes  bag_cuda::Workspace, include/bag/cuda/bag.cuh:34-55
+ *   bag_local_elements                    bag_cuda::local_elements, bag.cuh:23-30
+ *   bag_matmul                            bag_cuda::matmul, bag.cuh:247-260
+ *   bag_valid_shape                       strassen_cuda::valid_shape, include/bag/cuda/strassen.cuh:57-66
+ *   bag_primitive                         strassen_cuda::primitive, strassen.cuh:68-70 (CUDA) and
+ *                                         bag_primitive, src/bag_triton/primitive.py:256-272 (gamma +-2)
+ *   bag_primitive_pair                    strassen_cuda::pair, strassen.cuh:167-197
+ *   bag_strassen_one_level                strassen_cuda::one_level, strassen.cuh:223-276
+ *   bag_sgemm_ex / bag_sgemm_batched      new: rectangular, ragged, row-major and batched problems
+ *                                         (BASELINE configs 4 and 5); no reference counterpart
+ *   bag_plan_dump                         new: the host plan as JSON, for tests of the plan builder
+ */
+#ifndef BAG_CAPI_H
+#define BAG_CAPI_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t; 0 is the legacy default stream. */
+typedef struct CUstream_st* bag_stream_t;
+typedef struct bag_workspace bag_workspace;
+
+typedef enum bag_status {
+  BAG_OK = 0,
+  BAG_ERR_INVALID = 1,     /* bad argument (null pointer, bad enum, bad coefficient) */
+  BAG_ERR_SHAPE = 2,       /* shape the algorithm or backend cannot take */
+  BAG_ERR_WORKSPACE = 3,   /* workspace missing, too small or for another shape */
+  BAG_ERR_UNSUPPORTED = 4, /* valid request this build does not implement */
+  BAG_ERR_CUDA = 5,        /* a CUDA runtime call failed */
+  BAG_ERR_INTERNAL = 6
+} bag_status;
+
+/* Basis descriptors, bag.cuh:7 (Minimal, Full); CLASSIC is Strassen-1969
+ * (strassen.cuh:131-153) run through the same recursion. */
+enum { BAG_BASIS_MINIMAL = 0, BAG_BASIS_FULL = 1, BAG_BASIS_CLASSIC = 2 };
+/* bag_cuda::Schedule, bag.cuh:8.  Every schedule runs as one grouped launch on
+ * the caller stream here; the value is validated and otherwise a hint. */
+enum { BAG_SCHEDULE_SERIAL = 0, BAG_SCHEDULE_SEVEN_STREAM = 1, BAG_SCHEDULE_BATCHED = 2 };
+/* strassen_cuda::Schedule, strassen.cuh:165. */
+enum {
+  BAG_STRASSEN_SERIAL_ATOMIC = 0, BAG_STRASSEN_SERIAL_NORMAL = 1, BAG_STRASSEN_SEVEN_ATOMIC = 2,
+  BAG_STRASSEN_DEPENDENCY_NORMAL = 3, BAG_STRASSEN_PAIRED_ATOMIC = 4,
+  BAG_STRASSEN_PAIRED_NORMAL = 5, BAG_STRASSEN_FOUR_BATCHED_ATOMIC = 6
+};
+enum { BAG_LAYOUT_COL_MAJOR = 0, BAG_LAYOUT_ROW_MAJOR = 1 };
+/* Backend ids are the positions of strassen_cuda::Backend (strassen.cuh:11-16);
+ * every id runs this library's kernel, valid_shape keeps its constraints. */
+enum { BAG_BACKEND_LEGACY = 0, BAG_BACKEND_LARGE = 1, BAG_BACKEND_MEDIUM = 2, BAG_BACKEND_HUGE = 3,
+       BAG_BACKEND_PIPE64X32 = 8, BAG_BACKEND_DEFERRED_SWIZZLE64 = 23,
+       BAG_BACKEND_COLUMN_TILE8 = 37, BAG_BACKEND_COUNT = 42 };
+
+const char* bag_last_error(void);
+const char* bag_version(void);
+
+/* Elements the reference's workspace holds (bag.cuh:23-30): throws there, returns
+ * 0 and sets BAG_ERR_SHAPE here when depth < 1 or a level's size is not a multiple of 8. */
+bag_status bag_local_elements(int n, int depth, int basis, size_t* elements);
+
+/* Workspace for square n x n products at `depth` levels (bag.cuh:40-44). */
+bag_status bag_workspace_create(int n, int depth, int basis, bag_workspace** out);
+/* Workspace for C(m x n) += A(m x k) B(k x n), `batch` problems at once. */
+bag_status bag_workspace_create_ex(int m, int n, int k, int depth, int basis, int batch,
+                                   bag_workspace** out);
+bag_status bag_workspace_destroy(bag_workspace* ws);
+size_t bag_workspace_bytes(const bag_workspace* ws);
+
+/* C <- A B + C; A, B, C distinct column-major n x n, ld = n (bag.cuh:247-260).
+ * Checks n == the workspace's n, the leaf against `backend`'s valid_shape, and
+ * that BATCHED uses a paired backend, with the reference's error texts. */
+bag_status bag_matmul(const float* a, const float* b, float* c, int n, bag_stream_t stream,
+                      bag_workspace* ws, int backend, int schedule);
+
+/* C <- A B + beta C (beta 0 or 1) for any m, n, k >= 0.  depth 0 is a plain
+ * GEMM through the same kernel; ragged extents are peeled into plain strips.
+ * ws may be NULL when the plan needs no workspace (Minimal basis, depth <= 1). */
+bag_status bag_sgemm_ex(int layout, int m, int n, int k, const float* a, long long lda,
+                        const float* b, long long ldb, float* c, long long ldc, float beta,
+                        int depth, int basis, bag_stream_t stream, bag_workspace* ws);
+
+/* `batch` independent problems, operand i at base + i*stride (one launch). */
+bag_status bag_sgemm_batched(int layout, int m, int n, int k, const float* a, long long lda,
+                             long long stride_a, const float* b, long long ldb, long long stride_b,
+                             float* c, long long ldc, long long stride_c, int batch, float beta,
+                             int depth, int basis, bag_stream_t stream, bag_workspace* ws);
+
+/* d (+)= gamma_d (x + delta y)(v + eps w), e likewise; column-major, x,y: m x k,
+ * v,w: k x n, d,e: m x n.  delta, eps in {-1,0,1}; gamma in {-2..2}: +-1
+ * accumulates (atomically when `atomic` != 0), +-2 overwrites, 0 skips. */
+bag_status bag_primitive(int delta, int eps, int gamma_d, int gamma_e, int atomic,
+                         const float* x, const float* y, const float* v, const float* w, float* d,
+                         float* e, int m, int n, int k, long long ldx, long long ldy, long long ldv,
+                         long long ldw, long long ldd, long long lde, bag_stream_t stream);
+
+/* Two primitives with shared coefficients in one launch (strassen.cuh:167-197);
+ * operand arrays are {x,y,v,w} and {d,e} for product 0 then product 1. */
+bag_status bag_primitive_pair(int delta, int eps, int gamma_d, int gamma_e, int atomic,
+                              const float* const operands[8], float* const outputs[4], int s,
+                              long long ld, bag_stream_t stream);
+
+/* Classic Strassen one level, C <- A B + C, column-major n x n (strassen.cuh:225-276). */
+bag_status bag_strassen_one_level(int backend, int schedule, const float* a, const float* b,
+                                  float* c, int n, bag_stream_t stream);
+
+/* 1 when `s` satisfies `backend`'s tile constraint (strassen.cuh:57-66). */
+bag_status bag_valid_shape(int backend, int s, int* valid);
+
+/* Measurement hooks (new; no reference counterpart).  When set, the leaf
+ * launches of later calls on this host thread are bracketed by
+ * cudaEventRecord(start) / cudaEventRecord(end) on the call's stream, so a
+ * caller can time the product kernel alone; NULL, NULL turns it off.
+ * bag_launch_count returns how many kernels this process has launched. */
+bag_status bag_profile_set_events(void* start_event, void* end_event);
+unsigned long long bag_launch_count(void);
+/* FP32 FFMA throughput probe (a roofline denominator): one launch of
+ * 4 x SM-count CTAs x 256 threads of register-only fmaf chains; `sink` must
+ * hold 1024 x SM-count floats.  *flops receives the launch's FLOP count. */
+bag_status bag_ffma_probe(float* sink, int iterations, bag_stream_t stream, double* flops);
+
+/* Describe the plan for a column-major problem as JSON (no GPU needed).
+ * Pointers are reported as {base, offset}: base 0=A, 1=B, 2=C, 3=workspace.
+ * Writes at most buflen bytes; *needed receives the full length + 1. */
+bag_status bag_plan_dump(int m, int n, int k, long long lda, long long ldb, long long ldc,
+                         int depth, int basis, char* buf, size_t buflen, size_t* needed);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BAG_CAPI_H */

@@ -1,0 +1,112 @@
+"""CPU tests of the C ABI: the library loads, exports every declared symbol,
+and its host-side validation matches the reference's rules and errors.
+No kernel is launched here."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "bag_capi.h")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(bag_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for expected in ("bag_matmul", "bag_sgemm_ex", "bag_sgemm_batched", "bag_primitive",
+                     "bag_strassen_one_level", "bag_workspace_create", "bag_last_error"):
+        assert expected in names
+
+
+def test_library_exports_every_declared_symbol(built_lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", built_lib], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\bT (bag_[a-z0-9_]+)$", out, flags=re.M))
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_python_signatures_cover_header(bag):
+    assert set(bag.SIGNATURES) == set(declared_functions())
+    for name in bag.SIGNATURES:
+        assert getattr(bag.lib(), name) is not None
+
+
+def test_version(bag):
+    assert b"sm_100a" in bag.lib().bag_version()
+
+
+@pytest.mark.parametrize("n,depth,basis,expected", [
+    (16, 1, "minimal", 16 * 16 + 16 * 16 // 2),
+    (16, 1, "full", 3 * 16 * 16),
+    (64, 3, "minimal", 64 * 64 * 3 // 2),
+])
+def test_local_elements_matches_reference(bag, n, depth, basis, expected):
+    # bag.cuh:23-30
+    assert bag.local_elements(n, depth, basis) == expected
+
+
+@pytest.mark.parametrize("n,depth", [(12, 1), (24, 2), (16, 0), (0, 1)])
+def test_local_elements_rejects_like_reference(bag, n, depth):
+    with pytest.raises(ValueError):
+        bag.local_elements(n, depth)
+
+
+@pytest.mark.parametrize("backend,s,valid", [
+    ("huge", 128, True), ("huge", 192, False), ("large", 64, True), ("large", 96, False),
+    ("medium", 96, True), ("column_tile64_k16_r4x8", 12, True), ("column_tile64_k16_r4x8", 6, False),
+    ("legacy", 384, True), ("legacy", 400, False), ("legacy", 2048, True),
+])
+def test_valid_shape_matches_reference(bag, backend, s, valid):
+    # strassen.cuh:57-66
+    assert bag.valid_shape(backend, s) is valid
+
+
+def test_errors_are_status_codes_not_exceptions(bag):
+    lib = bag.lib()
+    # Null workspace, bad backend, bad schedule: BAG_ERR_WORKSPACE / INVALID.
+    assert lib.bag_matmul(None, None, None, 16, None, None, 37, 2) == 3
+    assert b"workspace" in lib.bag_last_error()
+    assert lib.bag_primitive(2, 0, 1, 0, 1, None, None, None, None, None, None, 4, 4, 4,
+                             4, 4, 4, 4, 4, 4, None) == 1
+    assert b"delta" in lib.bag_last_error()
+    assert lib.bag_sgemm_ex(7, 4, 4, 4, None, 4, None, 4, None, 4, 1.0, 1, 0, None, None) == 1
+    assert lib.bag_sgemm_ex(0, 4, 4, 4, None, 4, None, 4, None, 4, 0.5, 1, 0, None, None) == 4
+    assert lib.bag_strassen_one_level(37, 6, None, None, None, 12, None) == 2
+    # strassen.cuh:228-231: shape first, then "selected backend requires atomic updates".
+    assert lib.bag_strassen_one_level(0, 1, None, None, None, 16, None) == 2
+    assert lib.bag_strassen_one_level(0, 1, None, None, None, 64, None) == 4
+    valid = ctypes.c_int()
+    assert lib.bag_valid_shape(99, 16, ctypes.byref(valid)) == 1
+
+
+def test_empty_problems_are_no_ops(bag):
+    lib = bag.lib()
+    # m == 0 or n == 0 returns before touching the device.
+    assert lib.bag_sgemm_ex(0, 0, 8, 8, None, 1, None, 8, None, 1, 1.0, 1, 0, None, None) == 0
+    assert lib.bag_primitive(0, 0, 1, 0, 1, None, None, None, None, None, None, 0, 4, 4,
+                             1, 1, 4, 4, 1, 1, None) == 0
+
+
+def test_plan_dump_without_gpu(bag):
+    plan = bag.plan_dump(16, 16, 16, 16, 16, 16, 1, "minimal")
+    assert len(plan["leaves"]) == 7
+
+
+def test_workspace_sizes(bag):
+    # Depth-1 Minimal fuses every transform: no workspace; deeper plans round
+    # the outer operands into 8 quarter-size blocks (4 per operand).
+    plan1 = bag.plan_dump(1024, 1024, 1024, 1024, 1024, 1024, 1, "minimal")
+    plan2 = bag.plan_dump(1024, 1024, 1024, 1024, 1024, 1024, 2, "minimal")
+    assert plan1["workspace_elements"] == 0
+    assert plan2["workspace_elements"] == 8 * 512 * 512

@@ -1,0 +1,403 @@
+"""GPU parity tests: the sm_100a kernels, called through the C ABI, against the
+CPU oracle, the reference's golden outputs and the reference's own CUDA BAG.
+
+Bars:
+* bit-exact for single-writer primitive outputs (every output is the same
+  sequential fmaf chain as ``oracle/exact_gemm.c``);
+* the reference validator (``fp32_baseline.cu:121-192``): rel-L2 <= 3e-5,
+  max_abs/(1+max|ref|) <= 1e-4, after 1 and 3 accumulating calls;
+* the reference's Triton limits (``tests/triton/test_bag.py:60-61``,
+  ``test_primitive.py:89``) on its golden outputs;
+* relative Frobenius error vs FP64 <= 1.25x the reference CUDA BAG's error at
+  equal depth and <= 1e-4.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from oracle import bag_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libbagref.so")
+
+
+@pytest.fixture(scope="module")
+def torch_mod(cuda):
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    return torch
+
+
+def dev(torch, x, order="C"):
+    """Upload a numpy matrix; order='F' gives a column-major tensor."""
+    x = np.asfortranarray(x) if order == "F" else np.ascontiguousarray(x)
+    t = torch.from_numpy(x).cuda()
+    return t
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+# ---------------------------------------------------------------------------
+# Primitive: bit-exact against the sequential-fmaf oracle.
+# ---------------------------------------------------------------------------
+
+PRIM_SHAPES = [(1, 1, 1), (37, 29, 21), (63, 97, 35), (257, 65, 33), (128, 128, 128),
+               (130, 66, 260), (64, 257, 33), (512, 256, 129)]
+# The seven Minimal-basis coefficient sets plus the classic ones (bag.cuh:170-190,
+# strassen.cuh:143-153).
+COEFFS = [(1, 1), (-1, -1), (0, 0), (-1, 0), (0, -1), (1, 0), (-1, 1)]
+
+
+@pytest.mark.parametrize("shape", PRIM_SHAPES)
+@pytest.mark.parametrize("delta,eps", COEFFS)
+def test_primitive_bitexact(bag, torch_mod, shape, delta, eps):
+    torch = torch_mod
+    m, n, k = shape
+    rng = np.random.default_rng(m * 131 + n * 17 + k + 3 * delta + eps)
+    x, y = (rng.uniform(-1, 1, (m, k)).astype(np.float32) for _ in range(2))
+    v, w = (rng.uniform(-1, 1, (k, n)).astype(np.float32) for _ in range(2))
+    expect = O.exact_primitive(x, y if delta else None, v, w if eps else None, delta, eps)
+    tx, ty, tv, tw = (dev(torch, t, "F") for t in (x, y, v, w))
+    d = torch.full((n, m), 7.0, device="cuda").t()    # column-major, overwritten (gamma=2)
+    e = torch.zeros((n, m), device="cuda").t()        # accumulated once into zero (gamma=-1)
+    bag.bag_primitive(tx, ty if delta else None, tv, tw if eps else None, d, e, delta=delta,
+                      epsilon=eps, gamma_d=2, gamma_e=-1)
+    torch.cuda.synchronize()
+    assert np.array_equal(host(d), expect)
+    assert np.array_equal(host(e), -expect)
+
+
+def test_primitive_row_major_and_nonatomic(bag, torch_mod):
+    torch = torch_mod
+    m, n, k = 96, 80, 70
+    rng = np.random.default_rng(5)
+    x, y = (rng.uniform(-1, 1, (m, k)).astype(np.float32) for _ in range(2))
+    v, w = (rng.uniform(-1, 1, (k, n)).astype(np.float32) for _ in range(2))
+    d0 = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+    d = dev(torch, d0)
+    bag.bag_primitive(dev(torch, x), dev(torch, y), dev(torch, v), dev(torch, w), d, None,
+                      delta=-1, epsilon=1, gamma_d=1, gamma_e=0, _atomic_accumulate=False)
+    torch.cuda.synchronize()
+    ref = d0 + O.exact_primitive(x, y, v, w, -1, 1)
+    np.testing.assert_allclose(host(d), ref, atol=2e-4 + 2e-6 * k, rtol=2e-4)
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "prim_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[:-4])
+def test_primitive_reference_golden(bag, torch_mod, path):
+    torch = torch_mod
+    z = np.load(path)
+    delta, eps, gd, ge = [int(c) for c in z["coeffs"]]
+    d = dev(torch, z["d"]) if gd else None
+    e = dev(torch, z["e"]) if ge else None
+    bag.bag_primitive(dev(torch, z["x"]), dev(torch, z["y"]) if delta else None,
+                      dev(torch, z["v"]), dev(torch, z["w"]) if eps else None, d, e,
+                      delta=delta, epsilon=eps, gamma_d=gd, gamma_e=ge)
+    torch.cuda.synchronize()
+    k = z["x"].shape[1]
+    tol = dict(atol=2e-4 + 2e-6 * k, rtol=2e-4)      # test_primitive.py:89
+    if d is not None:
+        np.testing.assert_allclose(host(d), z["d_out"], **tol)
+    if e is not None:
+        np.testing.assert_allclose(host(e), z["e_out"], **tol)
+
+
+def test_primitive_concurrent_atomic_streams(bag, torch_mod):
+    """Two streams accumulate into one output (test_primitive.py:96-131)."""
+    torch = torch_mod
+    m, n, k = 73, 61, 47
+    rng = np.random.default_rng(11)
+    ops = [rng.uniform(-1, 1, s).astype(np.float32) for s in [(m, k), (m, k), (k, n), (k, n)] * 2]
+    t = [dev(torch, o) for o in ops]
+    out = torch.zeros((m, n), device="cuda")
+    s0, s1 = torch.cuda.Stream(), torch.cuda.Stream()
+    ready = torch.cuda.Event()
+    ready.record()
+    s0.wait_event(ready)
+    s1.wait_event(ready)
+    with torch.cuda.stream(s0):
+        bag.bag_primitive(t[0], t[1], t[2], t[3], out, None, delta=-1, epsilon=1, gamma_d=1,
+                          gamma_e=0)
+    with torch.cuda.stream(s1):
+        bag.bag_primitive(t[4], t[5], t[6], t[7], out, None, delta=-1, epsilon=1, gamma_d=1,
+                          gamma_e=0)
+    torch.cuda.synchronize()
+    expect = (O.exact_primitive(ops[0], ops[1], ops[2], ops[3], -1, 1)
+              + O.exact_primitive(ops[4], ops[5], ops[6], ops[7], -1, 1))
+    np.testing.assert_allclose(host(out), expect, atol=3e-4, rtol=2e-4)
+
+
+# ---------------------------------------------------------------------------
+# bag_matmul: the reference's Triton goldens and interface.
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "bag_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[:-4])
+def test_bag_matmul_reference_golden(bag, torch_mod, path):
+    torch = torch_mod
+    z = np.load(path)
+    order = "F" if str(z["layout"]) == "col" else "C"
+    a, b = dev(torch, z["a"], order), dev(torch, z["b"], order)
+    out = dev(torch, np.zeros_like(z["a"]), order)
+    ret = bag.bag_matmul(a, b, out=out)
+    torch.cuda.synchronize()
+    assert ret is out
+    got = host(out)
+    ref64 = O.fp64_matmul(z["a"], z["b"])
+    n = z["a"].shape[0]
+    assert O.rel_frobenius(got, ref64) <= 3e-4                  # test_bag.py:60
+    assert np.abs(got - ref64).max() <= 2e-3 + 2e-5 * n         # test_bag.py:61
+    assert O.rel_frobenius(got, z["out"]) <= 2e-6               # same algorithm as the reference
+    assert O.rel_frobenius(got, ref64) <= 1.25 * O.rel_frobenius(z["out"], ref64) + 2e-8
+
+
+def test_bag_matmul_interface_rejections(bag, torch_mod):
+    """test_bag.py:70-85: odd sizes are ValueError, non-FP32 is TypeError."""
+    torch = torch_mod
+    a = torch.rand(8, 8, device="cuda") - 0.5
+    b = torch.rand(8, 8, device="cuda") - 0.5
+    with pytest.raises(ValueError):
+        bag.bag_matmul(a[:7, :7], b[:7, :7])
+    with pytest.raises(TypeError):
+        bag.bag_matmul(a, b.to(torch.float16))
+
+
+@pytest.mark.parametrize("layout", ["row", "col", "sliced"])
+@pytest.mark.parametrize("size", [2, 6, 64, 510, 1024])
+def test_bag_matmul_layouts(bag, torch_mod, layout, size):
+    """test_bag.py:23-67 sizes and layouts against torch.mm (IEEE FP32)."""
+    torch = torch_mod
+    if layout == "sliced" and size > 510:
+        pytest.skip("reference skips large sliced cases")
+    gen = torch.Generator(device="cuda").manual_seed(20260831 + size)
+
+    def mat():
+        if layout == "row":
+            t = torch.empty((size, size), device="cuda")
+        elif layout == "col":
+            t = torch.empty_strided((size, size), (1, size), device="cuda")
+        else:
+            t = torch.empty((2 * size, 3 * size), device="cuda")[::2, ::3]
+        return t.uniform_(-0.5, 0.5, generator=gen)
+
+    a, b, out = mat(), mat(), mat()
+    ws = bag.allocate_bag_workspace(a, b, out)
+    ref = (a.double() @ b.double())
+    ret = bag.bag_matmul(a, b, out=out, workspace=ws)
+    torch.cuda.synchronize()
+    assert ret is out
+    diff = (out.double() - ref)
+    assert float(diff.norm() / ref.norm()) <= 3e-4
+    assert float(diff.abs().max()) <= 2e-3 + 2e-5 * size
+
+
+def test_non_default_stream_and_replay(bag, torch_mod):
+    """test_bag.py:88-136: calls from a non-default stream, run twice."""
+    torch = torch_mod
+    n = 128
+    a = torch.rand(n, n, device="cuda") - 0.5
+    b = torch.rand(n, n, device="cuda") - 0.5
+    out = torch.rand(n, n, device="cuda")
+    ws = bag.allocate_bag_workspace(a, b, out, depth=2)
+    caller = torch.cuda.Stream()
+    ready = torch.cuda.Event()
+    ready.record()
+    caller.wait_event(ready)
+    with torch.cuda.stream(caller):
+        bag.bag_matmul(a, b, out=out, workspace=ws)
+        bag.bag_matmul(a, b, out=out, workspace=ws)
+    caller.synchronize()
+    ref = a.double() @ b.double()
+    assert float((out.double() - ref).norm() / ref.norm()) <= 3e-4
+
+
+# ---------------------------------------------------------------------------
+# bag_cuda::matmul semantics: column-major C <- AB + C, validator of the
+# reference's CUDA benchmarks (CTest: sizes 24,128, depths 1,2, seed offset 1009).
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("n", [24, 128, 1024])
+@pytest.mark.parametrize("depth", [1, 2])
+@pytest.mark.parametrize("basis", ["minimal", "full"])
+@pytest.mark.parametrize("schedule", ["serial", "seven", "batched"])
+def test_matmul_reference_validator(bag, torch_mod, n, depth, basis, schedule):
+    torch = torch_mod
+    seed = 1009
+    a = O.hash_matrix(n, n, 11 + seed)
+    b = O.hash_matrix(n, n, 23 + seed)
+    c0 = O.hash_matrix(n, n, 37 + seed)
+    valid = all((n >> lv) % 8 == 0 for lv in range(depth))
+    if not valid:
+        with pytest.raises(ValueError):
+            bag.Workspace(n, depth, basis)
+        return
+    ws = bag.Workspace(n, depth, basis)
+    ta, tb = dev(torch, a, "F"), dev(torch, b, "F")
+    for repeats in (1, 3):
+        tc = dev(torch, c0, "F")
+        for _ in range(repeats):
+            bag.matmul(ta, tb, tc, n, ws, schedule=schedule)
+        torch.cuda.synchronize()
+        res = O.validate(host(tc), a, b, c0, repeats)
+        assert res.passed, res
+
+
+def test_matmul_workspace_mismatch(bag, torch_mod):
+    torch = torch_mod
+    ws = bag.Workspace(64, 1)
+    t = torch.zeros(128, 128, device="cuda")
+    with pytest.raises(ValueError, match="size mismatch"):
+        bag.matmul(t, t, t, 128, ws)
+    with pytest.raises(ValueError, match="tile constraints"):
+        bag.matmul(t, t, t, 64, bag.Workspace(64, 1), backend="huge")
+
+
+# ---------------------------------------------------------------------------
+# Rectangular, ragged, batched, classic.
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("m,k,n", [(256, 512, 128), (77, 53, 61), (511, 509, 513),
+                                   (1000, 1000, 1000), (8, 8, 8), (300, 2, 300)])
+@pytest.mark.parametrize("depth", [0, 1, 2])
+@pytest.mark.parametrize("layout", ["row", "col"])
+def test_sgemm_shapes(bag, torch_mod, m, k, n, depth, layout):
+    torch = torch_mod
+    rng = np.random.default_rng(m + 3 * k + 7 * n + depth)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    c = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+    order = "F" if layout == "col" else "C"
+    ta, tb, tc = dev(torch, a, order), dev(torch, b, order), dev(torch, c, order)
+    ws = bag.Workspace.for_problem(m, n, k, depth) if depth >= 2 else None
+    if layout == "row":
+        ws = bag.Workspace.for_problem(n, m, k, depth) if depth >= 2 else None
+    bag.sgemm(ta, tb, tc, depth=depth, workspace=ws)
+    torch.cuda.synchronize()
+    err = O.rel_frobenius(host(tc), O.fp64_matmul(a, b, c))
+    assert err < 2e-6 * (depth + 1)
+
+
+@pytest.mark.parametrize("basis", ["minimal", "full", "classic"])
+@pytest.mark.parametrize("depth", [1, 2, 3])
+def test_sgemm_bases_and_depths(bag, torch_mod, basis, depth):
+    torch = torch_mod
+    n = 512
+    rng = np.random.default_rng(depth * 10 + len(basis))
+    a = rng.standard_normal((n, n), dtype=np.float32)
+    b = rng.standard_normal((n, n), dtype=np.float32)
+    ta, tb = dev(torch, a), dev(torch, b)
+    tc = torch.full((n, n), 3.0, device="cuda")
+    ws = bag.Workspace.for_problem(n, n, n, depth, basis)
+    bag.sgemm(ta, tb, tc, beta=0.0, depth=depth, basis=basis, workspace=ws)
+    torch.cuda.synchronize()
+    got = host(tc)
+    ref = O.fp64_matmul(a, b)
+    assert O.rel_frobenius(got, ref) < 1e-6 * 2 ** depth
+    if basis != "classic":
+        orc = O.bag_matmul(a, b, depth=depth, basis=basis)
+        assert O.rel_frobenius(got, orc.astype(np.float64)) < 2e-6 * depth
+
+
+def test_sgemm_batched(bag, torch_mod):
+    torch = torch_mod
+    batch, n = 6, 256
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    a = torch.rand(batch, n, n, device="cuda", generator=gen)
+    b = torch.rand(batch, n, n, device="cuda", generator=gen)
+    c = torch.zeros(batch, n, n, device="cuda")
+    bag.sgemm_batched(a, b, c, depth=1)
+    ref = torch.bmm(a.double(), b.double())
+    torch.cuda.synchronize()
+    assert float((c.double() - ref).norm() / ref.norm()) < 2e-6
+    ws = bag.Workspace.for_problem(n, n, n, 2, "minimal", batch=batch)
+    c2 = torch.zeros_like(c)
+    bag.sgemm_batched(a, b, c2, depth=2, workspace=ws)
+    torch.cuda.synchronize()
+    assert float((c2.double() - ref).norm() / ref.norm()) < 4e-6
+
+
+def test_strassen_one_level(bag, torch_mod):
+    torch = torch_mod
+    n = 256
+    a = O.hash_matrix(n, n, 11)
+    b = O.hash_matrix(n, n, 23)
+    c0 = O.hash_matrix(n, n, 37)
+    tc = dev(torch, c0, "F")
+    bag.strassen_one_level(dev(torch, a, "F"), dev(torch, b, "F"), tc, n)
+    torch.cuda.synchronize()
+    assert O.validate(host(tc), a, b, c0, 1).passed
+    np.testing.assert_allclose(host(tc), O.strassen_one_level(a, b, c0), atol=1e-5, rtol=1e-5)
+
+
+# ---------------------------------------------------------------------------
+# Against the reference's own CUDA BAG, same inputs, same box.
+# ---------------------------------------------------------------------------
+
+def _ref_lib():
+    if not os.path.exists(REF_LIB):
+        pytest.skip("reference CUDA library not built (oracle/build_ref.py)")
+    lib = ctypes.CDLL(REF_LIB)
+    lib.ref_bag_matmul.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 5 + [ctypes.c_void_p]
+    lib.ref_strassen_one_level.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p]
+    lib.ref_last_error.restype = ctypes.c_char_p
+    return lib
+
+
+@pytest.mark.parametrize("n,depth,dist", [(1024, 1, "uniform_pm1"), (2048, 2, "uniform_pm1"),
+                                          (2048, 1, "normal"), (4096, 2, "normal")])
+@pytest.mark.parametrize("basis", ["minimal", "full"])
+def test_error_within_reference_bound(bag, torch_mod, n, depth, dist, basis):
+    """rel-F(mine) <= 1.25 x rel-F(reference CUDA BAG) and <= 1e-4, equal depth."""
+    torch = torch_mod
+    ref = _ref_lib()
+    a_rm, b_rm = O.config_inputs(n, n, n, 1, dist)
+    # Row-major inputs: the reference (column-major) computes C^T = B^T A^T.
+    ta, tb = torch.from_numpy(a_rm).cuda(), torch.from_numpy(b_rm).cuda()
+    exact = (ta.double() @ tb.double())
+    errs = []
+    for _ in range(3):
+        c = torch.zeros(n, n, device="cuda")
+        status = ref.ref_bag_matmul(tb.data_ptr(), ta.data_ptr(), c.data_ptr(), n, depth,
+                                    1 if basis == "full" else 0, 2, 0,
+                                    torch.cuda.current_stream().cuda_stream)
+        assert status == 0, ref.ref_last_error()
+        torch.cuda.synchronize()
+        errs.append(float((c.double() - exact).norm() / exact.norm()))
+    ref_err = float(np.median(errs))
+    ws = bag.Workspace.for_problem(n, n, n, depth, basis)
+    c = torch.zeros(n, n, device="cuda")
+    bag.sgemm(ta, tb, c, depth=depth, basis=basis, workspace=ws)
+    torch.cuda.synchronize()
+    mine = float((c.double() - exact).norm() / exact.norm())
+    assert mine <= 1e-4
+    assert mine <= 1.25 * ref_err, (mine, ref_err)
+
+
+def test_classic_matches_reference_strassen(bag, torch_mod):
+    torch = torch_mod
+    ref = _ref_lib()
+    n = 1024
+    a = torch.rand(n, n, device="cuda") - 0.5
+    b = torch.rand(n, n, device="cuda") - 0.5
+    c_ref = torch.zeros(n, n, device="cuda")
+    assert ref.ref_strassen_one_level(a.data_ptr(), b.data_ptr(), c_ref.data_ptr(), n,
+                                      torch.cuda.current_stream().cuda_stream) == 0
+    c = torch.zeros(n, n, device="cuda")
+    bag.strassen_one_level(a, b, c, n)
+    torch.cuda.synchronize()
+    exact = (a.t().double() @ b.t().double()).t()   # column-major view of the buffers
+    e_ref = float((c_ref.double() - exact).norm() / exact.norm())
+    e_mine = float((c.double() - exact).norm() / exact.norm())
+    assert e_mine <= 1.25 * e_ref and e_mine <= 1e-4

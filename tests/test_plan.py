@@ -1,0 +1,95 @@
+"""CPU tests of the host plan builder (no GPU): the dumped plan, executed in
+numpy by ``tests/plan_sim.py``, must compute C + A@B for every basis, depth
+and ragged or rectangular shape, and must round transformed operands where
+the reference does."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import bag_oracle as O
+from plan_sim import run_plan
+
+CASES = [
+    # m, k, n, depth, basis
+    (64, 64, 64, 1, "minimal"),
+    (64, 64, 64, 2, "minimal"),
+    (64, 64, 64, 3, "minimal"),
+    (64, 64, 64, 1, "full"),
+    (64, 64, 64, 2, "full"),
+    (64, 64, 64, 1, "classic"),
+    (64, 64, 64, 2, "classic"),
+    (72, 40, 56, 1, "minimal"),      # rectangular
+    (77, 53, 61, 2, "minimal"),      # ragged: peeled strips
+    (3, 5, 7, 1, "minimal"),         # smaller than one BAG block: plain GEMM
+    (128, 256, 64, 2, "full"),
+    (100, 100, 100, 1, "minimal"),   # 10000-style: halves to a non-multiple of 8
+    (40, 0, 24, 1, "minimal"),       # empty K
+    (48, 48, 48, 0, "minimal"),      # depth 0: plain GEMM
+]
+
+
+@pytest.mark.parametrize("m,k,n,depth,basis", CASES)
+def test_plan_computes_gemm(bag, m, k, n, depth, basis):
+    rng = np.random.default_rng(m * 7 + k * 3 + n + depth)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    c = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+    lda, ldb, ldc = m + 4, k + 8, m
+    plan = bag.plan_dump(m, n, k, lda, ldb, ldc, depth, basis)
+    got = run_plan(plan, a, b, c, lda, ldb, ldc)
+    assert O.rel_frobenius(got, O.fp64_matmul(a, b, c)) < 1e-6 * max(depth, 1) + 1e-7
+
+
+@pytest.mark.parametrize("depth", [1, 2])
+@pytest.mark.parametrize("basis", ["minimal", "full"])
+def test_plan_operands_round_like_reference(bag, depth, basis):
+    """Leaf products see bit-identical operands to the oracle's recursion.
+
+    With exactly representable inputs (multiples of 2^-16) every product of
+    two operands is exact in FP64, so comparing against the oracle run in the
+    same association order isolates the operand rounding.
+    """
+    n = 32
+    a = O.hash_matrix(n, n, 11)
+    b = O.hash_matrix(n, n, 23)
+    plan = bag.plan_dump(n, n, n, n, n, n, depth, basis)
+    got = run_plan(plan, a, b, np.zeros((n, n), np.float32), n, n, n)
+    ref = O.bag_product(a, b, depth, basis)
+    assert O.rel_frobenius(got, ref) < 1e-6
+
+
+def test_plan_shapes_and_counts(bag):
+    p1 = bag.plan_dump(64, 64, 64, 64, 64, 64, 1, "minimal")
+    assert len(p1["leaves"]) == 7 and p1["workspace_elements"] == 0 and p1["stages"] == []
+    # Direct decode: 14 output updates per level (M1:2 M2:2 M3:3 M4:1 M5:4 M6:1 M7:1).
+    assert sum(len(l["out"]) for l in p1["leaves"]) == 14
+    # Fused operand terms per level: 14 left and 14 right (max 4: SA - A11, SB - B11).
+    assert sum(len(l["left"]) for l in p1["leaves"]) == 14
+    assert max(len(l["left"]) for l in p1["leaves"]) == 4
+    p2 = bag.plan_dump(64, 64, 64, 64, 64, 64, 2, "minimal")
+    assert len(p2["leaves"]) == 49
+    assert sum(len(l["out"]) for l in p2["leaves"]) == 14 * 14
+    # One pass per operand rounds the four multi-term outer operands.
+    assert len(p2["stages"]) == 1 and len(p2["stages"][0]) == 2
+    assert all(len(j["out"]) == 4 for j in p2["stages"][0])
+    pf = bag.plan_dump(64, 64, 64, 64, 64, 64, 1, "full")
+    assert len(pf["stages"]) == 1 and len(pf["stages"][0]) == 2
+    assert max(len(l["left"]) for l in pf["leaves"]) == 2
+
+
+def test_plan_peels_ragged_edges(bag):
+    p = bag.plan_dump(77, 61, 53, 80, 56, 77, 2, "minimal")
+    # 49 BAG leaves on the 64x48x64 core plus the K, M and N strips.
+    assert len(p["leaves"]) == 52
+    strips = p["leaves"][49:]
+    assert [(s["m"], s["n"], s["k"]) for s in strips] == [(64, 48, 5), (13, 61, 53), (64, 13, 53)]
+
+
+def test_plan_workspace_alignment(bag):
+    p = bag.plan_dump(200, 200, 200, 200, 200, 200, 2, "full")
+    for stage in p["stages"]:
+        for job in stage:
+            for ref in job["out"]:
+                assert ref[0] == 3 and ref[1] % 64 == 0 and ref[2] % 4 == 0
