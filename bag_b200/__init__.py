@@ -63,6 +63,7 @@ SIGNATURES = {
     "bag_workspace_create_ex": (_I, [_I, _I, _I, _I, _I, _I, ctypes.POINTER(_VP)]),
     "bag_workspace_destroy": (_I, [_VP]),
     "bag_workspace_bytes": (_SZ, [_VP]),
+    "bag_workspace_data": (_VP, [_VP]),
     "bag_matmul": (_I, [_VP, _VP, _VP, _I, _VP, _VP, _I, _I]),
     "bag_sgemm_ex": (_I, [_I, _I, _I, _I, _VP, _LL, _VP, _LL, _VP, _LL, _F, _I, _I, _VP, _VP]),
     "bag_sgemm_batched": (_I, [_I, _I, _I, _I, _VP, _LL, _LL, _VP, _LL, _LL, _VP, _LL, _LL, _I,

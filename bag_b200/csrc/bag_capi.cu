@@ -16,6 +16,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -355,12 +356,45 @@ size_t plan_workspace_elements(GemmDesc g) {
   return B.ws_used;
 }
 
+// Tile configuration: the env var BAG_B200_TILE (a kTile* id) pins one for
+// tuning runs; otherwise the measured-fastest Tall tile, or small tiles when
+// the grid cannot fill the GPU.
 int choose_tile(const std::vector<HostLeaf>& leaves, int sm_count) {
+  static const int forced = [] {
+    const char* s = std::getenv("BAG_B200_TILE");
+    if (!s || !*s) return -1;
+    const int v = std::atoi(s);
+    return (v >= 0 && v < kTileCount) ? v : -1;
+  }();
+  if (forced >= 0) return forced;
   long long tiles = 0;
-  const TileShape big = leaf_tile_shape(kTileLarge);
+  const TileShape big = leaf_tile_shape(kTileTall);
   for (const HostLeaf& l : leaves)
     tiles += (long long)((l.m + big.bm - 1) / big.bm) * ((l.n + big.bn - 1) / big.bn);
-  return tiles < 2LL * sm_count ? kTileSmall : kTileLarge;
+  if (tiles >= 2LL * sm_count) return kTileTall;
+  tiles = 0;
+  const TileShape mid = leaf_tile_shape(kTileLarge);
+  for (const HostLeaf& l : leaves)
+    tiles += (long long)((l.m + mid.bm - 1) / mid.bm) * ((l.n + mid.bn - 1) / mid.bn);
+  return tiles >= 2LL * sm_count ? kTileLarge : kTileSmall;
+}
+
+// The compiled main loop for a product (kSigGeneric when none applies).
+int signature(const HostLeaf& l, bool vec) {
+  if (!vec || l.m < 4 || l.m % 4 || l.k % 4) return kSigGeneric;
+  for (const STerm& t : l.left)
+    if (t.v.ld != l.left[0].v.ld) return kSigGeneric;
+  for (const STerm& t : l.right)
+    if (t.v.ld != l.right[0].v.ld) return kSigGeneric;
+  const size_t nl = l.left.size(), nr = l.right.size();
+  if (nl == 1 && nr == 1) return kSig11;
+  if (nl == 1 && nr == 2) return kSig12;
+  if (nl == 2 && nr == 1) return kSig21;
+  if (nl == 2 && nr == 2) return kSig22;
+  if (nl == 3 && nr == 3) return kSig33;
+  if (nl == 4 && nr == 1) return kSig41;
+  if (nl == 1 && nr == 4) return kSig14;
+  return kSigGeneric;
 }
 
 void check_ld(long long ld) {
@@ -446,6 +480,7 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream) {
       P.o0 = short(nterms);
       P.no = short(l.out.size());
       for (const Target& t : l.out) lp.terms[nterms++] = make_term(t.v, t.coef, t.mode);
+      P.sig = signature(l, vec);
       const long long tiles = (long long)P.tiles_m * P.tiles_n;
       if (tiles > 0) {
         if ((long long)lp.ntiles + tiles > INT32_MAX) fail(BAG_ERR_SHAPE, "problem too large");
@@ -688,6 +723,8 @@ size_t bag_workspace_bytes(const bag_workspace* ws) {
   return ws ? ws->elements * sizeof(float) : 0;
 }
 
+float* bag_workspace_data(const bag_workspace* ws) { return ws ? ws->data : nullptr; }
+
 bag_status bag_matmul(const float* a, const float* b, float* c, int n, bag_stream_t stream,
                       bag_workspace* ws, int backend, int schedule) {
   return guarded([&] {
@@ -749,9 +786,10 @@ HostLeaf primitive_leaf(int delta, int eps, int gd, int ge, int atomic, const fl
   l.m = m;
   l.n = n;
   l.k = k;
-  if (!x || !v) fail(BAG_ERR_INVALID, "x and v are required");
-  if (delta && !y) fail(BAG_ERR_INVALID, "y may be null only when delta == 0");
-  if (eps && !w) fail(BAG_ERR_INVALID, "w may be null only when epsilon == 0");
+  // An empty reduction (k == 0) reads no operand, so they may be null.
+  if (k > 0 && (!x || !v)) fail(BAG_ERR_INVALID, "x and v are required");
+  if (k > 0 && delta && !y) fail(BAG_ERR_INVALID, "y may be null only when delta == 0");
+  if (k > 0 && eps && !w) fail(BAG_ERR_INVALID, "w may be null only when epsilon == 0");
   if (gd && !d) fail(BAG_ERR_INVALID, "d may be null only when gamma_d == 0");
   if (ge && !e) fail(BAG_ERR_INVALID, "e may be null only when gamma_e == 0");
   l.left.push_back({{x, ldx, 0}, 1.f});
@@ -789,7 +827,10 @@ bag_status bag_primitive(int delta, int eps, int gamma_d, int gamma_e, int atomi
     if (gamma_d && gamma_e && d == e && (gamma_d == 2 || gamma_d == -2 || gamma_e == 2 || gamma_e == -2))
       fail(BAG_ERR_INVALID, "overwrite modes need distinct outputs");
     auto ld_ok = [&](long long ld, int rows) { return ld >= std::max(1, rows); };
-    if (!ld_ok(ldx, m) || (delta && !ld_ok(ldy, m)) || !ld_ok(ldv, k) || (eps && !ld_ok(ldw, k)) ||
+    // An empty reduction reads no operand (k == 0 only writes 0 for +-2 codes).
+    const bool reads = k > 0;
+    if ((reads && (!ld_ok(ldx, m) || (delta && !ld_ok(ldy, m)) || !ld_ok(ldv, k) ||
+                   (eps && !ld_ok(ldw, k)))) ||
         (gamma_d && !ld_ok(ldd, m)) || (gamma_e && !ld_ok(lde, m)))
       fail(BAG_ERR_INVALID, "leading dimension smaller than the row count");
     run_leaves({primitive_leaf(delta, eps, gamma_d, gamma_e, atomic, x, y, v, w, d, e, m, n, k,

@@ -8,8 +8,14 @@
 namespace bag_b200 {
 
 enum : int {
-  kTileLarge = 0,   // 128 x 128 CTA tile, 256 threads, 8 x 8 FFMA per thread
+  kTileLarge = 0,   // 128 x 128 CTA tile, 256 threads, 8 x 8 FFMA per thread, 2 CTAs/SM
   kTileSmall = 1,   // 64 x 64 CTA tile, 64 threads, for grids too small to fill 148 SMs
+  kTileWide = 2,    // 128 x 256 CTA tile, 256 threads, 8 x 16 FFMA per thread, 1 CTA/SM
+  kTileTall = 3,    // 256 x 128 CTA tile, 256 threads, 16 x 8 FFMA per thread, 1 CTA/SM
+  kTileLarge1 = 4,  // 128 x 128 CTA tile, 256 threads, 8 x 8 per thread, 1 CTA/SM
+  kTileHalf = 5,    // 128 x 64 CTA tile, 128 threads, 8 x 8 per thread, 2 CTAs/SM
+  kTileTallS = 6,   // Tall with single-buffered register fragments
+  kTileCount = 7,
 };
 
 struct TileShape {

@@ -39,6 +39,12 @@ enum : int {
   kOutOverwrite = 2,  // store coef*M -- single writer only (gamma = +-2)
 };
 
+// Compiled main loops by (left terms, right terms); kSigGeneric runs the
+// runtime-count, element-masked loop.
+enum : int {
+  kSigGeneric = 0, kSig11, kSig12, kSig21, kSig22, kSig33, kSig41, kSig14,
+};
+
 struct Prod {
   int m, n, k;          // extents: left is m x k, right is k x n, output m x n
   int tiles_m, tiles_n; // CTA tiles covering the output
@@ -46,6 +52,7 @@ struct Prod {
   short l0, nl;         // left terms  [l0, l0+nl) in LeafPlan::terms
   short r0, nr;         // right terms
   short o0, no;         // outputs
+  int sig;              // kSig* main loop (fast paths need aligned, m % 4 == k % 4 == 0)
 };
 
 constexpr int kMaxProducts = 64;

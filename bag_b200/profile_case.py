@@ -1,0 +1,93 @@
+"""Profiling and tile-sweep driver for the BAG kernels.
+
+    python -m bag_b200.profile_case --n 4096 --depth 1          # one small case for ncu
+    python -m bag_b200.profile_case --sweep                      # time the current tile config
+
+The case mode builds N(0,1) FP32 operands on cuda:0 (torch generator, seed 0)
+and calls ``bag_b200.sgemm`` ``--calls`` times, so an ``ncu -k regex:leaf_gemm
+-c 1`` capture sees the first leaf launch.  The sweep mode prints one JSON line
+with effective and leaf-kernel TFLOP/s for a plain GEMM (depth 0, N=8192),
+BAG depth 1 (N=8192) and BAG depth 2 (N=16384); the tile configuration is
+the library default or the one pinned by ``BAG_B200_TILE``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+
+def _operands(n: int, depth: int, basis: str):
+    import torch
+
+    import bag_b200 as bag
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(n, n, device="cuda", generator=g)
+    b = torch.randn(n, n, device="cuda", generator=g)
+    c = torch.zeros(n, n, device="cuda")
+    ws = bag.Workspace.for_problem(n, n, n, depth, basis) if depth >= 2 or basis != "minimal" else None
+    return a, b, c, ws
+
+
+def run_case(n: int, depth: int, basis: str, calls: int) -> None:
+    import torch
+
+    import bag_b200 as bag
+    a, b, c, ws = _operands(n, depth, basis)
+    for _ in range(calls):
+        bag.sgemm(a, b, c, depth=depth, basis=basis, workspace=ws)
+    torch.cuda.synchronize()
+    print(f"ok n={n} depth={depth} basis={basis} calls={calls}")
+
+
+def run_sweep(reps: int = 3) -> dict:
+    import torch
+
+    import bag_b200 as bag
+    out = {"tile": os.environ.get("BAG_B200_TILE", "default")}
+    for name, n, depth in (("gemm8192_d0", 8192, 0), ("bag8192_d1", 8192, 1),
+                           ("bag16384_d2", 16384, 2)):
+        a, b, c, ws = _operands(n, depth, "minimal")
+        for _ in range(2):
+            bag.sgemm(a, b, c, depth=depth, workspace=ws)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(reps)]
+        for s, e in evs:
+            s.record()
+            e.record()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(reps):
+            bag.profile_events(*evs[i])
+            bag.sgemm(a, b, c, depth=depth, workspace=ws)
+        bag.profile_events(None, None)
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / reps
+        leaf = sum(s.elapsed_time(e) for s, e in evs) / reps
+        fexec = 7 ** depth * 2.0 * (n / 2 ** depth) ** 3
+        out[name] = {"ms": round(ms, 3), "eff_tflops": round(2.0 * n ** 3 / ms / 1e9, 2),
+                     "leaf_ms": round(leaf, 3), "leaf_tflops": round(fexec / leaf / 1e9, 2)}
+        del a, b, c, ws
+        torch.cuda.empty_cache()
+    return out
+
+
+def main() -> None:
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--n", type=int, default=4096)
+    p.add_argument("--depth", type=int, default=1)
+    p.add_argument("--basis", default="minimal")
+    p.add_argument("--calls", type=int, default=3)
+    p.add_argument("--sweep", action="store_true")
+    args = p.parse_args()
+    if args.sweep:
+        print(json.dumps(run_sweep()), flush=True)
+    else:
+        run_case(args.n, args.depth, args.basis, args.calls)
+
+
+if __name__ == "__main__":
+    main()

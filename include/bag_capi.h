@@ -75,6 +75,9 @@ bag_status bag_workspace_create_ex(int m, int n, int k, int depth, int basis, in
                                    bag_workspace** out);
 bag_status bag_workspace_destroy(bag_workspace* ws);
 size_t bag_workspace_bytes(const bag_workspace* ws);
+/* Device base of the workspace's rounded-operand blocks (NULL when the plan
+ * needs none: Minimal basis at depth 1 fuses every transform). */
+float* bag_workspace_data(const bag_workspace* ws);
 
 /* C <- A B + C; A, B, C distinct column-major n x n, ld = n (bag.cuh:247-260).
  * Checks n == the workspace's n, the leaf against `backend`'s valid_shape, and

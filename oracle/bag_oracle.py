@@ -156,8 +156,14 @@ def _decode(t: list[np.ndarray]) -> tuple[np.ndarray, ...]:
     return v11, v12, v21, v22
 
 
-def bag_product(a: np.ndarray, b: np.ndarray, depth: int, basis: str = "minimal") -> np.ndarray:
+def bag_product(a: np.ndarray, b: np.ndarray, depth: int, basis: str = "minimal",
+                leaf: str = "blas") -> np.ndarray:
     """Return A@B computed by ``depth`` BAG levels, reference evaluation order.
+
+    ``leaf="blas"`` computes leaf products with numpy's FP32 GEMM (fast);
+    ``leaf="fmaf"`` uses the sequential fmaf chain of ``oracle/exact_gemm.c``,
+    the summation order of the reference's CUDA kernels, so the result carries
+    the reference CUDA BAG's rounding error (small sizes only).
 
     This is ``bag_cuda::run<false>`` (``bag.cuh:241-245``): T is zeroed by
     prepare, products accumulate into T in product order 0..6, and decode
@@ -184,9 +190,10 @@ def bag_product(a: np.ndarray, b: np.ndarray, depth: int, basis: str = "minimal"
         left = _add(blocks[op.x], blocks[op.y], op.delta)
         right = _add(blocks[op.v], blocks[op.w], op.eps)
         if depth == 1:
-            prod = _mm32(left, right)
+            prod = (exact_primitive(left, None, right, None, 0, 0) if leaf == "fmaf"
+                    else _mm32(left, right))
         else:
-            prod = bag_product(left, right, depth - 1, basis)
+            prod = bag_product(left, right, depth - 1, basis, leaf)
         if op.gd:
             t[op.d] = (t[op.d] + F32(op.gd) * prod).astype(F32)
         if op.ge:

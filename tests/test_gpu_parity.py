@@ -160,7 +160,11 @@ def test_bag_matmul_reference_golden(bag, torch_mod, path):
     assert O.rel_frobenius(got, ref64) <= 3e-4                  # test_bag.py:60
     assert np.abs(got - ref64).max() <= 2e-3 + 2e-5 * n         # test_bag.py:61
     assert O.rel_frobenius(got, z["out"]) <= 2e-6               # same algorithm as the reference
-    assert O.rel_frobenius(got, ref64) <= 1.25 * O.rel_frobenius(z["out"], ref64) + 2e-8
+    # The reference's CUDA BAG sums each leaf product as a sequential fmaf chain
+    # (simt.cuh:136-159); its error, restated on CPU, bounds ours (the Triton
+    # interpreter's blocked numpy dot is more accurate than either).
+    ref_cuda = O.bag_product(z["a"], z["b"], 1, "minimal", leaf="fmaf")
+    assert O.rel_frobenius(got, ref64) <= 1.25 * O.rel_frobenius(ref_cuda, ref64) + 2e-8
 
 
 def test_bag_matmul_interface_rejections(bag, torch_mod):
