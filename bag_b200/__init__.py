@@ -68,6 +68,7 @@ SIGNATURES = {
     "bag_sgemm_ex": (_I, [_I, _I, _I, _I, _VP, _LL, _VP, _LL, _VP, _LL, _F, _I, _I, _VP, _VP]),
     "bag_sgemm_batched": (_I, [_I, _I, _I, _I, _VP, _LL, _LL, _VP, _LL, _LL, _VP, _LL, _LL, _I,
                                _F, _I, _I, _VP, _VP]),
+    "bag_sgemm_noalloc": (_I, [_I, _I, _I, _I, _VP, _LL, _VP, _LL, _VP, _LL, _F, _I, _I, _VP]),
     "bag_primitive": (_I, [_I, _I, _I, _I, _I, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _LL, _LL,
                            _LL, _LL, _LL, _LL, _VP]),
     "bag_primitive_pair": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_VP), ctypes.POINTER(_VP), _I,

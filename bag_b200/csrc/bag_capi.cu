@@ -812,6 +812,38 @@ void run_leaves(std::vector<HostLeaf> leaves, cudaStream_t stream) {
 }
 
 }  // namespace
+
+// Message for bag_last_error() from code outside this file (bag_noalloc.cu).
+void set_last_error(const std::string& message) { g_last_error = message; }
+
+// The body of bag_sgemm_noalloc (bag_noalloc.cu): the same call as
+// bag_sgemm_ex, with a caller-provided device scratch region of
+// `scratch_elements` floats standing in for a workspace.  Problems whose plan
+// needs more scratch than that are rejected before anything is enqueued.
+bag_status sgemm_with_scratch(int layout, int m, int n, int k, const float* a, long long lda,
+                              const float* b, long long ldb, float* c, long long ldc, float beta,
+                              int depth, int basis, cudaStream_t stream, float* scratch,
+                              size_t scratch_elements) {
+  return guarded([&] {
+    const GemmDesc g = make_desc(layout, m, n, k, a, lda, 0, b, ldb, 0, c, ldc, 0, 1, depth, basis);
+    if (g.m < 0 || g.n < 0 || g.k < 0) fail(BAG_ERR_SHAPE, "negative extent");
+    if (g.depth < 0 || g.depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8");
+    if (g.basis != kMinimal && g.basis != kFull && g.basis != kClassic)
+      fail(BAG_ERR_INVALID, "unknown basis");
+    const size_t need = (g.m > 0 && g.n > 0 && g.k > 0) ? plan_workspace_elements(g) : 0;
+    if (need > scratch_elements)
+      fail(BAG_ERR_WORKSPACE,
+           "bag_sgemm_noalloc: this problem needs " + std::to_string(need) +
+               " floats of scratch but the built-in scratch holds " +
+               std::to_string(scratch_elements) +
+               "; use bag_sgemm_ex with a workspace from bag_workspace_create_ex");
+    int dev = 0;
+    cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+    bag_workspace ws{g.m, g.n, g.k, depth, basis, 1, dev, scratch, scratch_elements};
+    run_gemm(g, beta, stream, &ws);
+  });
+}
+
 }  // namespace bag_b200
 
 extern "C" {

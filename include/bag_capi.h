@@ -92,6 +92,22 @@ bag_status bag_sgemm_ex(int layout, int m, int n, int k, const float* a, long lo
                         const float* b, long long ldb, float* c, long long ldc, float beta,
                         int depth, int basis, bag_stream_t stream, bag_workspace* ws);
 
+/* bag_sgemm_ex for callers that cannot allocate device memory -- e.g. a host
+ * framework or serving process that owns a fixed device-memory pool and lets no
+ * library call cudaMalloc, or a latency-critical caller that cannot afford an
+ * allocation that may synchronise the device.  No counterpart in the reference.
+ * Instead of a workspace it uses one built-in device scratch array of
+ * 4,194,304 floats (16 MiB) that each GPU loading the library holds until the
+ * process exits; problems needing more scratch (e.g. depth 2 beyond N = 1448
+ * square) fail with BAG_ERR_WORKSPACE before anything is enqueued.  The first
+ * call on a device looks up the array's address and should come before any
+ * stream capture on that device.  All calls share the array, so calls that can
+ * overlap on the GPU race and must be serialised by the caller.  Allocates
+ * nothing (no cudaMalloc/cudaFree). */
+bag_status bag_sgemm_noalloc(int layout, int m, int n, int k, const float* a, long long lda,
+                             const float* b, long long ldb, float* c, long long ldc, float beta,
+                             int depth, int basis, bag_stream_t stream);
+
 /* `batch` independent problems, operand i at base + i*stride (one launch). */
 bag_status bag_sgemm_batched(int layout, int m, int n, int k, const float* a, long long lda,
                              long long stride_a, const float* b, long long ldb, long long stride_b,
