@@ -80,6 +80,7 @@ SIGNATURES = {
     "bag_profile_set_events": (_I, [_VP, _VP]),
     "bag_launch_count": (ctypes.c_ulonglong, []),
     "bag_ffma_probe": (_I, [_VP, _I, _VP, ctypes.POINTER(ctypes.c_double)]),
+    "bag_device_error": (_I, [ctypes.POINTER(ctypes.c_uint)]),
 }
 
 _lib = None
@@ -146,6 +147,13 @@ def profile_events(start=None, end=None) -> None:
     """Bracket later leaf launches of this thread with two ``torch.cuda.Event``s."""
     handle = lambda ev: None if ev is None else ev.cuda_event  # noqa: E731
     _check(lib().bag_profile_set_events(handle(start), handle(end)))
+
+
+def device_error() -> int:
+    """Read and clear the device error word (0 when no in-kernel wait timed out)."""
+    out = ctypes.c_uint(0)
+    _check(lib().bag_device_error(ctypes.byref(out)))
+    return int(out.value)
 
 
 def local_elements(n: int, depth: int, basis="minimal") -> int:

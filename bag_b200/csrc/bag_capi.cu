@@ -359,24 +359,28 @@ size_t plan_workspace_elements(GemmDesc g) {
 // Tile configuration: the env var BAG_B200_TILE (a kTile* id) pins one for
 // tuning runs; otherwise the measured-fastest Tall tile, or small tiles when
 // the grid cannot fill the GPU.
-int choose_tile(const std::vector<HostLeaf>& leaves, int sm_count) {
+int signature(const HostLeaf& l, bool vec);
+
+int choose_tile(const std::vector<HostLeaf>& leaves, int sm_count, bool vec) {
   static const int forced = [] {
     const char* s = std::getenv("BAG_B200_TILE");
     if (!s || !*s) return -1;
     const int v = std::atoi(s);
     return (v >= 0 && v < kTileCount) ? v : -1;
   }();
-  if (forced >= 0) return forced;
-  long long tiles = 0;
-  const TileShape big = leaf_tile_shape(kTileTall);
-  for (const HostLeaf& l : leaves)
-    tiles += (long long)((l.m + big.bm - 1) / big.bm) * ((l.n + big.bn - 1) / big.bn);
-  if (tiles >= 2LL * sm_count) return kTileTall;
-  tiles = 0;
-  const TileShape mid = leaf_tile_shape(kTileLarge);
-  for (const HostLeaf& l : leaves)
-    tiles += (long long)((l.m + mid.bm - 1) / mid.bm) * ((l.n + mid.bn - 1) / mid.bn);
-  return tiles >= 2LL * sm_count ? kTileLarge : kTileSmall;
+  bool all_fast = vec;
+  for (const HostLeaf& l : leaves) all_fast = all_fast && signature(l, vec) != kSigGeneric;
+  if (forced >= 0 && (forced != kTileWS || all_fast)) return forced;
+  auto tiles_for = [&](int cfg) {
+    const TileShape t = leaf_tile_shape(cfg);
+    long long tiles = 0;
+    for (const HostLeaf& l : leaves)
+      tiles += (long long)((l.m + t.bm - 1) / t.bm) * ((l.n + t.bn - 1) / t.bn);
+    return tiles;
+  };
+  if (all_fast && tiles_for(kTileWS) >= sm_count) return kTileWS;
+  if (tiles_for(kTileTall) >= 2LL * sm_count) return kTileTall;
+  return tiles_for(kTileLarge) >= 2LL * sm_count ? kTileLarge : kTileSmall;
 }
 
 // The compiled main loop for a product (kSigGeneric when none applies).
@@ -444,14 +448,14 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream) {
   }
   if (g_prof_start) cuda_check(cudaEventRecord(g_prof_start, stream), "cudaEventRecord");
   // Leaf products, grouped into as few launches as the parameter block allows.
-  const int cfg = choose_tile(B.leaves, sms);
-  const TileShape ts = leaf_tile_shape(cfg);
   bool vec = true;
   for (const HostLeaf& l : B.leaves) {
     for (const STerm& t : l.left) vec = vec && view_vec_ok(t.v);
     for (const STerm& t : l.right) vec = vec && view_vec_ok(t.v);
     for (const Target& t : l.out) vec = vec && view_vec_ok(t.v);
   }
+  const int cfg = choose_tile(B.leaves, sms, vec);
+  const TileShape ts = leaf_tile_shape(cfg);
   size_t i = 0;
   while (i < B.leaves.size()) {
     LeafPlan lp;
@@ -931,6 +935,13 @@ bag_status bag_profile_set_events(void* start_event, void* end_event) {
 }
 
 unsigned long long bag_launch_count(void) { return g_launches.load(); }
+
+bag_status bag_device_error(unsigned* code) {
+  return guarded([&] {
+    if (!code) fail(BAG_ERR_INVALID, "null output pointer");
+    cuda_check(read_and_clear_device_error(code), "reading the device error word");
+  });
+}
 
 bag_status bag_ffma_probe(float* sink, int iterations, bag_stream_t stream, double* flops) {
   return guarded([&] {

@@ -558,6 +558,7 @@ TileShape leaf_tile_shape(int config) {
     case kTileLarge1: return {CfgLarge1::BM, CfgLarge1::BN};
     case kTileHalf: return {CfgHalf::BM, CfgHalf::BN};
     case kTileTallS: return {CfgTallS::BM, CfgTallS::BN};
+    case kTileWS: return ws_tile_shape();
     default: return {CfgLarge::BM, CfgLarge::BN};
   }
 }
@@ -571,6 +572,7 @@ cudaError_t launch_leaf(const LeafPlan& plan, int config, bool vec, int batch, c
     case kTileLarge1: return launch_cfg<CfgLarge1>(plan, vec, batch, stream);
     case kTileHalf: return launch_cfg<CfgHalf>(plan, vec, batch, stream);
     case kTileTallS: return launch_cfg<CfgTallS>(plan, vec, batch, stream);
+    case kTileWS: return launch_leaf_ws(plan, batch, stream);
     default: return launch_cfg<CfgLarge>(plan, vec, batch, stream);
   }
 }

@@ -15,7 +15,8 @@ enum : int {
   kTileLarge1 = 4,  // 128 x 128 CTA tile, 256 threads, 8 x 8 per thread, 1 CTA/SM
   kTileHalf = 5,    // 128 x 64 CTA tile, 128 threads, 8 x 8 per thread, 2 CTAs/SM
   kTileTallS = 6,   // Tall with single-buffered register fragments
-  kTileCount = 7,
+  kTileWS = 7,      // warp-specialised 128 x 128 kernel (bag_ws_kernel.cu), fast signatures only
+  kTileCount = 8,
 };
 
 struct TileShape {
@@ -33,6 +34,14 @@ cudaError_t launch_leaf(const LeafPlan& plan, int config, bool vec, int batch, c
 // blocks*256 floats.  *flops receives the FLOPs the launch performs.
 cudaError_t launch_ffma_probe(float* sink, int blocks, int iters, cudaStream_t stream,
                               double* flops);
+
+// Warp-specialised leaf kernel (bag_ws_kernel.cu): every product must have a
+// fast signature (sig != kSigGeneric) and 16-byte-aligned operands.
+TileShape ws_tile_shape();
+cudaError_t launch_leaf_ws(const LeafPlan& plan, int batch, cudaStream_t stream);
+
+// Reads and clears the device error word that bounded waits set on timeout.
+cudaError_t read_and_clear_device_error(unsigned* value);
 
 // One launch of every materialisation job in `plan`.
 cudaError_t launch_materialize(const MatPlan& plan, int batch, cudaStream_t stream, int sm_count);

@@ -1,0 +1,367 @@
+// Warp-specialised leaf kernel of the BAG FP32 matmul (sm_100a).
+//
+// One launch runs every leaf product of a plan whose operands are 16-byte
+// aligned (the fast signatures of bag_plan.h).  Each CTA of 384 threads owns a
+// 128 x 128 output tile of one product:
+//
+//  * 4 producer warps load the next k-tiles of every signed operand term with
+//    128-bit loads two tiles ahead, sum the terms in the reference's order
+//    (x + delta*y, bag.cuh:69-73), and store the transformed A tile (k-major)
+//    and B tile (in its natural K-contiguous layout, 16-byte chunks
+//    XOR-swizzled so both the stores and the consumers' column reads hit 32
+//    distinct banks) into a 4-stage shared-memory ring, then arrive on the
+//    stage's "full" mbarrier;
+//  * 8 consumer warps wait on "full", run the register-blocked outer product
+//    (8 x 8 outputs per thread) with Blackwell's paired FMA __ffma2_rn (two
+//    IEEE round-to-nearest fmaf per instruction, so every output stays one
+//    sequential fmaf chain over k), arrive on the stage's "empty" mbarrier,
+//    and finally add coef*M into every target C block (128-bit red.global).
+//
+// Every mbarrier wait sleeps in try_wait (suspend-time hint) rather than
+// spinning, and is bounded: after kWaitLimitNs of wall time the thread sets
+// g_device_error and leaves its loop, so a logic error cannot hang the GPU;
+// nothing is left in flight (producers use plain loads).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "bag_kernels.h"
+
+namespace bag_b200 {
+
+__device__ unsigned int g_device_error = 0;
+
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 8, kStages = 4;
+constexpr int kConsumers = 256, kProducers = 128, kThreads = kConsumers + kProducers;
+constexpr unsigned kSuspendNs = 1000000;                  // try_wait sleep hint (1 ms)
+constexpr unsigned long long kWaitLimitNs = 2000000000ull; // give up after 2 s
+
+struct WsSmem {
+  float a[kStages][kBK][kBM];   // A tile, k-major: a[s][k][m]
+  float b[kStages][kBN][kBK];   // B tile, n-major: b[s][n][chunk' * 4 + e], chunk' swizzled
+  unsigned long long full[kStages];
+  unsigned long long empty[kStages];
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
+  unsigned long long state;
+  asm volatile("mbarrier.arrive.shared::cta.b64 %0, [%1];"
+               : "=l"(state)
+               : "r"(smem_u32(bar))
+               : "memory");
+  (void)state;
+}
+
+// One try_wait; the thread may sleep up to `suspend_ns` for the phase to
+// complete, so a waiting warp does not spin on the issue slots of the
+// computing warps.
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity,
+                                              unsigned suspend_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for the phase of parity `parity`: gives up (error word set,
+// false) when the phase has not completed after kWaitLimitNs of wall time.
+__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity, kSuspendNs)) return true;
+  const unsigned long long start = global_ns();
+  while (!mbar_try_wait(bar, parity, kSuspendNs)) {
+    if (global_ns() - start > kWaitLimitNs) {
+      atomicOr(&g_device_error, 1u);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ const Prod& find_prod(const LeafPlan& plan, int item) {
+  int pid = 0;
+  while (pid + 1 < plan.nprod && plan.prod[pid + 1].tile_begin <= item) ++pid;
+  return plan.prod[pid];
+}
+
+__device__ __forceinline__ float4 ldg4(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+
+__device__ __forceinline__ float4 add_signed(float4 acc, float4 v, float coef) {
+  return make_float4(fmaf(coef, v.x, acc.x), fmaf(coef, v.y, acc.y), fmaf(coef, v.z, acc.z),
+                     fmaf(coef, v.w, acc.w));
+}
+
+__device__ __forceinline__ float4 signed_first(float4 v, float coef) {
+  return coef < 0.f ? make_float4(-v.x, -v.y, -v.z, -v.w) : v;
+}
+
+// Producer: 128 threads.  Thread p stages A vectors (rows a_m..a_m+3 of
+// columns a_k and a_k+4) and B vectors (k-chunk b_kc of columns b_n and b_n+64).
+template <int NL, int NR>
+__device__ __forceinline__ void produce(const LeafPlan& plan, const Prod& P, int m0, int n0,
+                                        long long batch, WsSmem& sm, int p, int ktiles) {
+  const int a_m = (p % 32) * 4, a_k = p / 32;
+  const int b_n = p / 2, b_kc = p % 2;
+  const long long lda = plan.terms[P.l0].ld, ldb = plan.terms[P.r0].ld;
+  const float* ba[NL];
+  float ca[NL];
+#pragma unroll
+  for (int t = 0; t < NL; ++t) {
+    const Term& T = plan.terms[P.l0 + t];
+    ba[t] = T.p + batch * T.bstride;
+    ca[t] = T.coef;
+  }
+  const float* bb[NR];
+  float cb[NR];
+#pragma unroll
+  for (int t = 0; t < NR; ++t) {
+    const Term& T = plan.terms[P.r0 + t];
+    bb[t] = T.p + batch * T.bstride;
+    cb[t] = T.coef;
+  }
+  // Clamped addresses: rows >= m and columns >= n are loaded but never stored.
+  long long oa = min(m0 + a_m, P.m - 4) + (long long)a_k * lda;
+  long long ob0 = b_kc * 4 + (long long)min(n0 + b_n, P.n - 1) * ldb;
+  long long ob1 = b_kc * 4 + (long long)min(n0 + b_n + 64, P.n - 1) * ldb;
+  const int kfull = P.k / kBK;
+
+  float4 la[2][NL][2], lb[2][NR][2];
+  auto load = [&](float4 (&xa)[NL][2], float4 (&xb)[NR][2], int kt) {
+    if (kt < kfull) {
+#pragma unroll
+      for (int t = 0; t < NL; ++t) {
+        xa[t][0] = ldg4(ba[t] + oa);
+        xa[t][1] = ldg4(ba[t] + oa + 4 * lda);
+      }
+#pragma unroll
+      for (int t = 0; t < NR; ++t) {
+        xb[t][0] = ldg4(bb[t] + ob0);
+        xb[t][1] = ldg4(bb[t] + ob1);
+      }
+    } else {   // the last, partial k-tile: zero beyond k (k % 4 == 0 here)
+      const int k0 = kt * kBK;
+      const bool a0 = k0 + a_k < P.k, a1 = k0 + a_k + 4 < P.k, bk = k0 + b_kc * 4 < P.k;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int t = 0; t < NL; ++t) {
+        xa[t][0] = a0 ? ldg4(ba[t] + oa) : z;
+        xa[t][1] = a1 ? ldg4(ba[t] + oa + 4 * lda) : z;
+      }
+#pragma unroll
+      for (int t = 0; t < NR; ++t) {
+        xb[t][0] = bk ? ldg4(bb[t] + ob0) : z;
+        xb[t][1] = bk ? ldg4(bb[t] + ob1) : z;
+      }
+    }
+    oa += kBK * lda;
+    ob0 += kBK;
+    ob1 += kBK;
+  };
+  auto store = [&](const float4 (&xa)[NL][2], const float4 (&xb)[NR][2], int s) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      float4 v = signed_first(xa[0][q], ca[0]);
+#pragma unroll
+      for (int t = 1; t < NL; ++t) v = add_signed(v, xa[t][q], ca[t]);
+      *reinterpret_cast<float4*>(&sm.a[s][a_k + 4 * q][a_m]) = v;
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      float4 v = signed_first(xb[0][q], cb[0]);
+#pragma unroll
+      for (int t = 1; t < NR; ++t) v = add_signed(v, xb[t][q], cb[t]);
+      const int n = b_n + 64 * q;
+      *reinterpret_cast<float4*>(&sm.b[s][n][(b_kc ^ ((n >> 2) & 1)) * 4]) = v;
+    }
+  };
+  // Publish tile kt from register buffer x: wait until consumers released the
+  // stage's previous use, store, arrive.  False when a wait timed out.
+  auto publish = [&](const float4 (&xa)[NL][2], const float4 (&xb)[NR][2], int kt) {
+    const int s = kt % kStages;
+    if (kt >= kStages && !mbar_wait(&sm.empty[s], ((kt / kStages) - 1) & 1)) return false;
+    store(xa, xb, s);
+    mbar_arrive(&sm.full[s]);
+    return true;
+  };
+
+  if (ktiles > 0) load(la[0], lb[0], 0);
+  if (ktiles > 1) load(la[1], lb[1], 1);
+  for (int kt = 0; kt < ktiles; kt += 2) {
+    if (!publish(la[0], lb[0], kt)) return;
+    if (kt + 2 < ktiles) load(la[0], lb[0], kt + 2);
+    if (kt + 1 < ktiles) {
+      if (!publish(la[1], lb[1], kt + 1)) return;
+      if (kt + 3 < ktiles) load(la[1], lb[1], kt + 3);
+    }
+  }
+}
+
+// Consumer: 256 threads in 8 warps (4 along M x 2 along N).  Thread rows are
+// wm + lane_m*4 + {0..3, 16..19}; columns wn + lane_n + 8c, c = 0..7.
+__device__ __forceinline__ bool consume(WsSmem& sm, int ctid, int ktiles, float2 (&acc)[4][8]) {
+  const int warp = ctid >> 5, lane = ctid & 31;
+  const int lane_m = lane >> 3, lane_n = lane & 7;
+  const int wm = (warp & 3) * 32, wn = (warp >> 2) * 64;
+  const int am = wm + lane_m * 4;
+  const int swz = (lane_n >> 2) & 1;   // bit 2 of every column this thread reads
+  for (int kt = 0; kt < ktiles; ++kt) {
+    const int s = kt % kStages;
+    if (!mbar_wait(&sm.full[s], (kt / kStages) & 1)) return false;
+#pragma unroll
+    for (int kq = 0; kq < kBK / 4; ++kq) {
+      float4 bf[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        bf[c] = *reinterpret_cast<const float4*>(&sm.b[s][wn + lane_n + 8 * c][(kq ^ swz) * 4]);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int k = kq * 4 + kk;
+        const float4 a0 = *reinterpret_cast<const float4*>(&sm.a[s][k][am]);
+        const float4 a1 = *reinterpret_cast<const float4*>(&sm.a[s][k][am + 16]);
+        const float2 ap[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w),
+                              make_float2(a1.x, a1.y), make_float2(a1.z, a1.w)};
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float bv = kk == 0 ? bf[c].x : kk == 1 ? bf[c].y : kk == 2 ? bf[c].z : bf[c].w;
+          const float2 b2 = make_float2(bv, bv);
+#pragma unroll
+          for (int ip = 0; ip < 4; ++ip) acc[ip][c] = __ffma2_rn(ap[ip], b2, acc[ip][c]);
+        }
+      }
+    }
+    mbar_arrive(&sm.empty[s]);
+  }
+  return true;
+}
+
+__device__ __forceinline__ void store_outputs(const LeafPlan& plan, const Prod& P, int m0, int n0,
+                                              long long batch, int ctid,
+                                              const float2 (&acc)[4][8]) {
+  const int warp = ctid >> 5, lane = ctid & 31;
+  const int lane_m = lane >> 3, lane_n = lane & 7;
+  const int wm = (warp & 3) * 32, wn = (warp >> 2) * 64;
+  for (int o = 0; o < P.no; ++o) {
+    const Term& T = plan.terms[P.o0 + o];
+    float* base = const_cast<float*>(T.p) + batch * T.bstride;
+    const float coef = T.coef;
+    const int mode = T.mode;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const int r = m0 + wm + lane_m * 4 + 16 * g;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int col = n0 + wn + lane_n + 8 * c;
+        if (col >= P.n || r >= P.m) continue;
+        float* q = base + r + (long long)col * T.ld;
+        const float v[4] = {coef * acc[2 * g][c].x, coef * acc[2 * g][c].y,
+                            coef * acc[2 * g + 1][c].x, coef * acc[2 * g + 1][c].y};
+        if (r + 3 < P.m) {
+          float4* q4 = reinterpret_cast<float4*>(q);
+          if (mode == kOutAtomic) {
+            atomicAdd(q4, make_float4(v[0], v[1], v[2], v[3]));
+          } else if (mode == kOutAdd) {
+            const float4 old = *q4;
+            *q4 = make_float4(old.x + v[0], old.y + v[1], old.z + v[2], old.w + v[3]);
+          } else {
+            *q4 = make_float4(v[0], v[1], v[2], v[3]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (r + e >= P.m) break;
+            if (mode == kOutAtomic) atomicAdd(q + e, v[e]);
+            else if (mode == kOutAdd) q[e] += v[e];
+            else q[e] = v[e];
+          }
+        }
+      }
+    }
+  }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1) leaf_ws_kernel(const __grid_constant__ LeafPlan plan) {
+  __shared__ __align__(16) WsSmem sm;
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], kProducers);
+      mbar_init(&sm.empty[s], kConsumers);
+    }
+  }
+  __syncthreads();
+  const Prod& P = find_prod(plan, blockIdx.x);
+  const int local = blockIdx.x - P.tile_begin;
+  constexpr int GROUP_M = 8;   // CTAs resident together share operand panels in L2
+  const int in_group = GROUP_M * P.tiles_n;
+  const int first_m = (local / in_group) * GROUP_M;
+  const int gsize = min(P.tiles_m - first_m, GROUP_M);
+  const int m0 = (first_m + (local % in_group) % gsize) * kBM;
+  const int n0 = ((local % in_group) / gsize) * kBN;
+  const long long batch = blockIdx.y;
+  const int ktiles = (P.k + kBK - 1) / kBK;
+
+  if (threadIdx.x >= kConsumers) {
+    const int p = threadIdx.x - kConsumers;
+    switch (P.sig) {
+      case kSig11: produce<1, 1>(plan, P, m0, n0, batch, sm, p, ktiles); break;
+      case kSig12: produce<1, 2>(plan, P, m0, n0, batch, sm, p, ktiles); break;
+      case kSig21: produce<2, 1>(plan, P, m0, n0, batch, sm, p, ktiles); break;
+      case kSig22: produce<2, 2>(plan, P, m0, n0, batch, sm, p, ktiles); break;
+      case kSig33: produce<3, 3>(plan, P, m0, n0, batch, sm, p, ktiles); break;
+      case kSig41: produce<4, 1>(plan, P, m0, n0, batch, sm, p, ktiles); break;
+      case kSig14: produce<1, 4>(plan, P, m0, n0, batch, sm, p, ktiles); break;
+      default: atomicOr(&g_device_error, 2u); break;   // the host never sends these here
+    }
+    return;
+  }
+  float2 acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[i][c] = make_float2(0.f, 0.f);
+  if (P.sig == kSigGeneric) return;
+  if (!consume(sm, threadIdx.x, ktiles, acc)) return;
+  store_outputs(plan, P, m0, n0, batch, threadIdx.x, acc);
+}
+
+TileShape ws_tile_shape() { return {kBM, kBN}; }
+
+cudaError_t launch_leaf_ws(const LeafPlan& plan, int batch, cudaStream_t stream) {
+  if (plan.nprod == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
+  leaf_ws_kernel<<<dim3(plan.ntiles, batch), kThreads, 0, stream>>>(plan);
+  return cudaGetLastError();
+}
+
+cudaError_t read_and_clear_device_error(unsigned* value) {
+  cudaError_t e = cudaMemcpyFromSymbol(value, g_device_error, sizeof(unsigned));
+  if (e != cudaSuccess) return e;
+  const unsigned zero = 0;
+  return cudaMemcpyToSymbol(g_device_error, &zero, sizeof(unsigned));
+}
+
+}  // namespace bag_b200

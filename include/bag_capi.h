@@ -142,6 +142,10 @@ bag_status bag_valid_shape(int backend, int s, int* valid);
  * bag_launch_count returns how many kernels this process has launched. */
 bag_status bag_profile_set_events(void* start_event, void* end_event);
 unsigned long long bag_launch_count(void);
+/* Reads and clears the device error word (synchronous): non-zero when a
+ * bounded in-kernel wait gave up instead of hanging (1) or a product reached a
+ * kernel it was not planned for (2).  New; no reference counterpart. */
+bag_status bag_device_error(unsigned* code);
 /* FP32 FFMA throughput probe (a roofline denominator): one launch of
  * 4 x SM-count CTAs x 256 threads of register-only fmaf chains; `sink` must
  * hold 1024 x SM-count floats.  *flops receives the launch's FLOP count. */

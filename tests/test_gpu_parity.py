@@ -405,3 +405,10 @@ def test_classic_matches_reference_strassen(bag, torch_mod):
     e_ref = float((c_ref.double() - exact).norm() / exact.norm())
     e_mine = float((c.double() - exact).norm() / exact.norm())
     assert e_mine <= 1.25 * e_ref and e_mine <= 1e-4
+
+
+def test_no_bounded_wait_timed_out(bag, torch_mod):
+    """Every in-kernel wait of the tests above completed (device error word 0)."""
+    torch = torch_mod
+    torch.cuda.synchronize()
+    assert bag.device_error() == 0
