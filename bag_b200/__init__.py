@@ -81,7 +81,11 @@ SIGNATURES = {
     "bag_launch_count": (ctypes.c_ulonglong, []),
     "bag_ffma_probe": (_I, [_VP, _I, _VP, ctypes.POINTER(ctypes.c_double)]),
     "bag_device_error": (_I, [ctypes.POINTER(ctypes.c_uint)]),
+    "bag_set_math_mode": (_I, [_I]),
+    "bag_get_math_mode": (_I, []),
+    "bag_last_leaf_path": (_I, []),
 }
+MATH = {"ffma": 0, "3xtf32": 1}
 
 _lib = None
 
@@ -147,6 +151,22 @@ def profile_events(start=None, end=None) -> None:
     """Bracket later leaf launches of this thread with two ``torch.cuda.Event``s."""
     handle = lambda ev: None if ev is None else ev.cuda_event  # noqa: E731
     _check(lib().bag_profile_set_events(handle(start), handle(end)))
+
+
+def set_math_mode(mode: str) -> None:
+    """Leaf arithmetic of later calls on this thread: "ffma" (default) or "3xtf32"."""
+    if mode not in MATH:
+        raise ValueError(f"math mode must be one of {sorted(MATH)}, got {mode!r}")
+    _check(lib().bag_set_math_mode(MATH[mode]))
+
+
+def get_math_mode() -> str:
+    return {v: k for k, v in MATH.items()}[int(lib().bag_get_math_mode())]
+
+
+def last_leaf_path() -> str:
+    """Leaf arithmetic ("ffma" or "3xtf32") the last call on this thread used."""
+    return {v: k for k, v in MATH.items()}[int(lib().bag_last_leaf_path())]
 
 
 def device_error() -> int:

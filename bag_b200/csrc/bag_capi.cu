@@ -38,6 +38,14 @@ namespace bag_b200 {
 namespace {
 
 thread_local std::string g_last_error;
+thread_local int g_math_mode = BAG_MATH_FFMA;
+thread_local int g_last_leaf_path = BAG_MATH_FFMA;
+// Shortest leaf K the 3xTF32 path takes.  Its tensor-core partial sums carry a
+// fixed error of about 1.4e-7 (hi/lo split and round-toward-zero
+// accumulation within a 32-long chunk); an FP32 FFMA dot product's error grows
+// with K and passes it near K = 256.  Measured on B200 (N(0,1) operands):
+// tensor/FFMA error ratio 2.1 at K = 64, 1.07 at 256, 0.56 at 1024, 0.32 at 4096.
+constexpr int kTcMinK = 1024;
 thread_local cudaEvent_t g_prof_start = nullptr;
 thread_local cudaEvent_t g_prof_end = nullptr;
 std::atomic<unsigned long long> g_launches{0};
@@ -454,8 +462,14 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream) {
     for (const STerm& t : l.right) vec = vec && view_vec_ok(t.v);
     for (const Target& t : l.out) vec = vec && view_vec_ok(t.v);
   }
-  const int cfg = choose_tile(B.leaves, sms, vec);
-  const TileShape ts = leaf_tile_shape(cfg);
+  bool all_fast = vec;
+  for (const HostLeaf& l : B.leaves) all_fast = all_fast && signature(l, vec) != kSigGeneric;
+  bool long_k = true;
+  for (const HostLeaf& l : B.leaves) long_k = long_k && l.k >= kTcMinK;
+  const bool tensor = g_math_mode == BAG_MATH_3XTF32 && all_fast && long_k;
+  g_last_leaf_path = tensor ? BAG_MATH_3XTF32 : BAG_MATH_FFMA;
+  const int cfg = tensor ? -1 : choose_tile(B.leaves, sms, vec);
+  const TileShape ts = tensor ? tc_tile_shape() : leaf_tile_shape(cfg);
   size_t i = 0;
   while (i < B.leaves.size()) {
     LeafPlan lp;
@@ -494,7 +508,8 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream) {
       ++i;
     }
     if (lp.nprod == 0 && i < B.leaves.size()) fail(BAG_ERR_INTERNAL, "plan chunking failed");
-    cuda_check(launch_leaf(lp, cfg, vec, batch, stream), "leaf launch");
+    cuda_check(tensor ? launch_leaf_tc(lp, batch, stream) : launch_leaf(lp, cfg, vec, batch, stream),
+               "leaf launch");
     if (lp.nprod) ++g_launches;
   }
   if (g_prof_end) cuda_check(cudaEventRecord(g_prof_end, stream), "cudaEventRecord");
@@ -936,10 +951,23 @@ bag_status bag_profile_set_events(void* start_event, void* end_event) {
 
 unsigned long long bag_launch_count(void) { return g_launches.load(); }
 
+bag_status bag_set_math_mode(int mode) {
+  return guarded([&] {
+    if (mode != BAG_MATH_FFMA && mode != BAG_MATH_3XTF32) fail(BAG_ERR_INVALID, "unknown math mode");
+    g_math_mode = mode;
+  });
+}
+
+int bag_get_math_mode(void) { return g_math_mode; }
+int bag_last_leaf_path(void) { return g_last_leaf_path; }
+
 bag_status bag_device_error(unsigned* code) {
   return guarded([&] {
     if (!code) fail(BAG_ERR_INVALID, "null output pointer");
+    unsigned tc = 0;
     cuda_check(read_and_clear_device_error(code), "reading the device error word");
+    cuda_check(read_and_clear_tc_device_error(&tc), "reading the device error word");
+    *code |= tc;
   });
 }
 

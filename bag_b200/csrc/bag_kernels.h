@@ -40,6 +40,11 @@ cudaError_t launch_ffma_probe(float* sink, int blocks, int iters, cudaStream_t s
 TileShape ws_tile_shape();
 cudaError_t launch_leaf_ws(const LeafPlan& plan, int batch, cudaStream_t stream);
 
+// 3xTF32 tcgen05 leaf kernel (bag_tc_kernel.cu): fast signatures only.
+TileShape tc_tile_shape();
+cudaError_t launch_leaf_tc(const LeafPlan& plan, int batch, cudaStream_t stream);
+cudaError_t read_and_clear_tc_device_error(unsigned* value);
+
 // Reads and clears the device error word that bounded waits set on timeout.
 cudaError_t read_and_clear_device_error(unsigned* value);
 

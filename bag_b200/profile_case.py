@@ -2,6 +2,7 @@
 
     python -m bag_b200.profile_case --n 4096 --depth 1          # one small case for ncu
     python -m bag_b200.profile_case --sweep                      # time the current tile config
+    python -m bag_b200.profile_case --math 3xtf32 ...            # tensor-core leaf variant
 
 The case mode builds N(0,1) FP32 operands on cuda:0 (torch generator, seed 0)
 and calls ``bag_b200.sgemm`` ``--calls`` times, so an ``ncu -k regex:leaf_gemm
@@ -82,7 +83,10 @@ def main() -> None:
     p.add_argument("--basis", default="minimal")
     p.add_argument("--calls", type=int, default=3)
     p.add_argument("--sweep", action="store_true")
+    p.add_argument("--math", default="ffma", choices=("ffma", "3xtf32"))
     args = p.parse_args()
+    import bag_b200 as bag
+    bag.set_math_mode(args.math)
     if args.sweep:
         print(json.dumps(run_sweep()), flush=True)
     else:

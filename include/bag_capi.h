@@ -55,6 +55,12 @@ enum {
   BAG_STRASSEN_PAIRED_NORMAL = 5, BAG_STRASSEN_FOUR_BATCHED_ATOMIC = 6
 };
 enum { BAG_LAYOUT_COL_MAJOR = 0, BAG_LAYOUT_ROW_MAJOR = 1 };
+/* Leaf arithmetic (bag_set_math_mode).  FFMA: every output a sequential fmaf
+ * chain, the reference's SIMT numerics.  3XTF32: tcgen05 tensor cores on
+ * hi/lo TF32 splits (hi*hi + hi*lo + lo*hi) with 32-long K chunks summed in
+ * FP32 -- error below an FP32 FFMA dot product's for K >= 1024; used where
+ * bag_last_leaf_path says, FFMA elsewhere. */
+enum { BAG_MATH_FFMA = 0, BAG_MATH_3XTF32 = 1 };
 /* Backend ids are the positions of strassen_cuda::Backend (strassen.cuh:11-16);
  * every id runs this library's kernel, valid_shape keeps its constraints. */
 enum { BAG_BACKEND_LEGACY = 0, BAG_BACKEND_LARGE = 1, BAG_BACKEND_MEDIUM = 2, BAG_BACKEND_HUGE = 3,
@@ -142,6 +148,16 @@ bag_status bag_valid_shape(int backend, int s, int* valid);
  * bag_launch_count returns how many kernels this process has launched. */
 bag_status bag_profile_set_events(void* start_event, void* end_event);
 unsigned long long bag_launch_count(void);
+/* Math mode of later calls on this host thread (like cublasSetMathMode);
+ * new, no reference counterpart. */
+bag_status bag_set_math_mode(int mode);
+int bag_get_math_mode(void);
+/* Leaf arithmetic the last call on this host thread used (BAG_MATH_*): 3XTF32
+ * only where the mode asks for it, every product has 16-byte-aligned operands
+ * and every leaf K is >= 1024 (below that the FFMA path is the more accurate).
+ * New; no reference counterpart. */
+int bag_last_leaf_path(void);
+
 /* Reads and clears the device error word (synchronous): non-zero when a
  * bounded in-kernel wait gave up instead of hanging (1) or a product reached a
  * kernel it was not planned for (2).  New; no reference counterpart. */

@@ -1,0 +1,132 @@
+"""GPU tests of the 3xTF32 tcgen05 variant (bag_set_math_mode(BAG_MATH_3XTF32)).
+
+Bar: relative Frobenius error vs FP64 no worse than 1.25x the FFMA path's (the
+reference's numerics) on the same inputs, and <= 1e-4; ragged edges, K tails,
+BAG depths and bases, batches; leaves shorter than K = 1024 stay on the FFMA
+kernel; every in-kernel wait completes (device error word 0)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import bag_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def tensor_mode(bag, cuda):
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    bag.set_math_mode("3xtf32")
+    yield bag
+    bag.set_math_mode("ffma")
+
+
+def _operands(torch, m, k, n, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(m, k, device="cuda", generator=g),
+            torch.randn(k, n, device="cuda", generator=g))
+
+
+def _sgemm(bag, torch, a, b, depth, basis, ws, mode):
+    bag.set_math_mode(mode)
+    c = torch.zeros(a.shape[0], b.shape[1], device="cuda")
+    bag.sgemm(a, b, c, beta=0.0, depth=depth, basis=basis, workspace=ws)
+    torch.cuda.synchronize()
+    return c, bag.last_leaf_path()
+
+
+def _rel(torch, c, a, b):
+    exact = a.double() @ b.double()
+    return float((c.double() - exact).norm() / exact.norm())
+
+
+# Leaf K >= 1024 everywhere: the tensor path runs.  Ragged M/N, a K tail that
+# is not a multiple of the stage length, depths 0-2 and both bases.
+@pytest.mark.parametrize("m,k,n,depth,basis", [
+    (256, 1024, 384, 0, "minimal"), (200, 1032, 136, 0, "minimal"), (132, 1100, 260, 0, "minimal"),
+    (2048, 2048, 2048, 1, "minimal"), (1536, 2064, 1032, 1, "minimal"),
+    (2048, 2048, 2048, 1, "classic"), (4096, 4096, 4096, 2, "minimal"),
+    (2048, 4096, 2048, 2, "classic")])
+def test_tensor_path_error(tensor_mode, m, k, n, depth, basis):
+    import torch
+    bag = tensor_mode
+    a, b = _operands(torch, m, k, n, seed=m + k + n + depth)
+    # sgemm's row-major call is the column-major C^T(n x m) = B^T A^T; leaf K = k / 2^depth.
+    ws = bag.Workspace.for_problem(n, m, k, depth, basis) if depth >= 2 or basis != "minimal" else None
+    c_tc, path = _sgemm(bag, torch, a, b, depth, basis, ws, "3xtf32")
+    assert path == "3xtf32"
+    assert bag.device_error() == 0
+    c_ff, path_ff = _sgemm(bag, torch, a, b, depth, basis, ws, "ffma")
+    assert path_ff == "ffma"
+    err, ffma = _rel(torch, c_tc, a, b), _rel(torch, c_ff, a, b)
+    assert err <= 1e-4
+    assert err <= 1.25 * ffma, (err, ffma)
+
+
+@pytest.mark.parametrize("m,k,n,depth", [(128, 8, 128, 0), (512, 256, 512, 0), (1024, 1024, 1024, 1),
+                                         (768, 520, 1000, 1)])
+def test_short_leaves_stay_on_ffma(tensor_mode, m, k, n, depth):
+    import torch
+    bag = tensor_mode
+    a, b = _operands(torch, m, k, n, seed=7)
+    c_tc, path = _sgemm(bag, torch, a, b, depth, "minimal", None, "3xtf32")
+    assert path == "ffma"
+    c_ff, _ = _sgemm(bag, torch, a, b, depth, "minimal", None, "ffma")
+    if depth == 0:   # one writer per element: the same kernel gives the same bits
+        assert torch.equal(c_tc, c_ff)
+    assert bag.device_error() == 0
+
+
+def test_tensor_path_accumulates(tensor_mode):
+    import torch
+    bag = tensor_mode
+    n = 2048
+    a, b = _operands(torch, n, n, n, seed=3)
+    c0 = torch.randn(n, n, device="cuda")
+    c = c0.clone()
+    bag.sgemm(a, b, c, beta=1.0, depth=1)
+    bag.sgemm(a, b, c, beta=1.0, depth=1)
+    torch.cuda.synchronize()
+    assert bag.last_leaf_path() == "3xtf32"
+    exact = c0.double() + 2 * (a.double() @ b.double())
+    assert float((c.double() - exact).norm() / exact.norm()) <= 2e-6
+    assert bag.device_error() == 0
+
+
+def test_tensor_path_batched(tensor_mode):
+    import torch
+    bag = tensor_mode
+    batch, n = 3, 2048
+    g = torch.Generator(device="cuda").manual_seed(4)
+    a = torch.rand(batch, n, n, device="cuda", generator=g)
+    b = torch.rand(batch, n, n, device="cuda", generator=g)
+    c = torch.zeros(batch, n, n, device="cuda")
+    bag.sgemm_batched(a, b, c, beta=0.0, depth=1)
+    torch.cuda.synchronize()
+    assert bag.last_leaf_path() == "3xtf32"
+    exact = a.double() @ b.double()
+    assert float((c.double() - exact).norm() / exact.norm()) <= 2e-6
+    assert bag.device_error() == 0
+
+
+def test_tensor_path_against_oracle(tensor_mode):
+    """Against the restated reference numerics (sequential-fmaf leaves) on the
+    same inputs: rectangular, one level, leaf K = 1024."""
+    import torch
+    bag = tensor_mode
+    m, k, n = 512, 2048, 256
+    rng = np.random.default_rng(9)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    tc = torch.zeros(m, n, device="cuda")
+    bag.sgemm(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda(), tc, beta=0.0, depth=1)
+    torch.cuda.synchronize()
+    assert bag.last_leaf_path() == "3xtf32"
+    got = tc.cpu().numpy()
+    ref = O.bag_product(a, b, 1, "minimal", leaf="fmaf")
+    exact = O.fp64_matmul(a, b)
+    assert O.rel_frobenius(got, exact) <= 1.25 * O.rel_frobenius(ref, exact)
+    assert bag.device_error() == 0
