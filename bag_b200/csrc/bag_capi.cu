@@ -426,7 +426,10 @@ Term make_term(const View& v, float coef, int mode) {
 
 bool view_vec_ok(const View& v) { return aligned16(v.p) && v.ld % 4 == 0 && v.bstride % 4 == 0; }
 
-void execute_plan(Builder& B, int batch, cudaStream_t stream) {
+// `sources` lists the whole operand matrices (A, B) the tensor-core path may
+// address blocks of through one tensor map each; may be empty.
+void execute_plan(Builder& B, int batch, cudaStream_t stream,
+                  const std::vector<TcSource>& sources = {}) {
   const int sms = sm_count_for_current_device();
   // Materialisation stages.
   for (const auto& jobs : B.stages) {
@@ -464,9 +467,11 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream) {
   }
   bool all_fast = vec;
   for (const HostLeaf& l : B.leaves) all_fast = all_fast && signature(l, vec) != kSigGeneric;
-  bool long_k = true;
-  for (const HostLeaf& l : B.leaves) long_k = long_k && l.k >= kTcMinK;
-  const bool tensor = g_math_mode == BAG_MATH_3XTF32 && all_fast && long_k;
+  // The tensor path reads operands by TMA, so it needs aligned operands
+  // (vec) but no common leading dimension among a product's terms.
+  bool tensor = g_math_mode == BAG_MATH_3XTF32 && vec;
+  for (const HostLeaf& l : B.leaves)
+    tensor = tensor && l.k >= kTcMinK && tc_supported(int(l.left.size()), int(l.right.size()));
   g_last_leaf_path = tensor ? BAG_MATH_3XTF32 : BAG_MATH_FFMA;
   const int cfg = tensor ? -1 : choose_tile(B.leaves, sms, vec);
   const TileShape ts = tensor ? tc_tile_shape() : leaf_tile_shape(cfg);
@@ -508,7 +513,8 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream) {
       ++i;
     }
     if (lp.nprod == 0 && i < B.leaves.size()) fail(BAG_ERR_INTERNAL, "plan chunking failed");
-    cuda_check(tensor ? launch_leaf_tc(lp, batch, stream) : launch_leaf(lp, cfg, vec, batch, stream),
+    cuda_check(tensor ? launch_leaf_tc(lp, sources.data(), int(sources.size()), batch, stream)
+                      : launch_leaf(lp, cfg, vec, batch, stream),
                "leaf launch");
     if (lp.nprod) ++g_launches;
   }
@@ -551,7 +557,8 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
   Builder B;
   build_plan(g, base ? base : reinterpret_cast<float*>(uintptr_t(1) << 44), (long long)need, B);
   if (B.ws_used != need) fail(BAG_ERR_INTERNAL, "plan size changed between passes");
-  execute_plan(B, g.batch, stream);
+  const std::vector<TcSource> sources = {{g.a, g.lda, g.sa, g.m, g.k}, {g.b, g.ldb, g.sb, g.k, g.n}};
+  execute_plan(B, g.batch, stream, sources);
 }
 
 GemmDesc make_desc(int layout, int m, int n, int k, const float* a, long long lda, long long sa,

@@ -40,9 +40,22 @@ cudaError_t launch_ffma_probe(float* sink, int blocks, int iters, cudaStream_t s
 TileShape ws_tile_shape();
 cudaError_t launch_leaf_ws(const LeafPlan& plan, int batch, cudaStream_t stream);
 
-// 3xTF32 tcgen05 leaf kernel (bag_tc_kernel.cu): fast signatures only.
+// 3xTF32 tcgen05 leaf kernel (bag_tc_kernel.cu).  Operand terms are read by
+// TMA: a term inside one of `sources` (same ld and batch stride, block within
+// its rows x cols) goes through that matrix's tensor map at the block's
+// coordinates, any other term through a map of its own block.  Every operand
+// must be 16-byte aligned with ld and batch stride multiples of 4.
+struct TcSource {
+  const float* base;
+  long long ld, bstride;
+  long long rows, cols;
+};
 TileShape tc_tile_shape();
-cudaError_t launch_leaf_tc(const LeafPlan& plan, int batch, cudaStream_t stream);
+// Whether the kernel takes a product with nl left and nr right terms (and the
+// driver offers cuTensorMapEncodeTiled).
+bool tc_supported(int nl, int nr);
+cudaError_t launch_leaf_tc(const LeafPlan& plan, const TcSource* sources, int nsources, int batch,
+                           cudaStream_t stream);
 cudaError_t read_and_clear_tc_device_error(unsigned* value);
 
 // Reads and clears the device error word that bounded waits set on timeout.

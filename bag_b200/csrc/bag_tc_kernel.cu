@@ -4,34 +4,47 @@
 // Every leaf product is computed as A_hi*B_hi + A_hi*B_lo + A_lo*B_hi where
 // x_hi = rn_tf32(x) and x_lo = rn_tf32(x - x_hi) split each transformed
 // operand element (the lo*lo term, below 2^-22 relative, is dropped).  The
-// tensor core accumulates only 256-long K chunks; each finished chunk is added
-// into an FP32 running sum with round-to-nearest on the CUDA cores, which keeps
-// the error below an FP32 FFMA dot product's (a whole-K tensor-core accumulation
-// grows with K instead).
+// tensor core accumulates with round-toward-zero, so it only sums 32-long K
+// chunks; each finished chunk is added into an FP32 running sum with
+// round-to-nearest on the CUDA cores (Ootomo & Yokota 2022, "Recovering single
+// precision accuracy from Tensor Cores while surpassing the FP32 theoretical
+// peak performance", sec. 4).  Measured error: 0.3-0.6x an FP32 FFMA dot
+// product's for K >= 1024.
 //
-// One CTA (288 threads) computes a 128 x 128 output tile of one product:
-//  * warps 5-8 (producers) load every signed operand term two k-blocks ahead
-//    (A: one row of 8 per thread, coalesced along m; B: 128-bit loads along
-//    k), sum the terms in the reference's order (x + delta*y, bag.cuh:69-73),
-//    split hi/lo and store the four 128 x 8 operand tiles of a k-block into a
-//    6-stage shared-memory ring in the tensor core's canonical K-major
-//    no-swizzle layout, then arrive on "full".  (TF32 operands are staged
-//    K-major: an M-major no-swizzle A operand produced no output on B200.)
-//  * warp 4 allocates 384 TMEM columns (two chunk accumulators and the running
-//    sum) and one elected thread issues the three tcgen05.mma.kind::tf32 per
-//    k-block into the current chunk buffer, committing "empty" (stage free)
-//    and, at the end of a chunk, "chunk_full";
-//  * warps 0-3 (one per TMEM lane quadrant, thread = output row) fold each
-//    finished chunk into the running sum (tcgen05.ld/st), release the chunk
-//    buffer, and finally add coef*sum into every target C block (red.global).
+// One CTA (320 threads, 227 KB shared memory, 1 per SM) computes a 128 x 128
+// output tile of one product; the K loop runs in stages of 16:
+//  * warp 8, lane 0 (producer): TMA-loads the raw FP32 tile of every signed
+//    operand term of the stage (A term: 128 m x 16 k, M-contiguous; B term:
+//    16 k x 128 n with 64-byte swizzle) into a ring of raw stages whose depth
+//    is sized per product (11 stages for single-term operands, 3 for 3+3).
+//    Tensor maps come from the host: one per source matrix (A, B) addressed
+//    by block coordinates, one per workspace block.  Warp 8 also owns TMEM.
+//  * warps 0-3 (A side; thread = tile row = TMEM lane): sum the A terms in the
+//    reference's order (x + delta*y, bag.cuh:69-73), zero the K tail, split
+//    hi/lo and store them into a TMEM A slot (tcgen05.st); fold each finished
+//    accumulation chunk into the running sum; finally add coef*sum into every
+//    target C block (red.global, coalesced along the column).
+//  * warps 4-7 (B side; thread = tile column): sum, split and store the B terms
+//    as K-major no-swizzle hi/lo tiles in a shared-memory ring.
+//  * warp 9, lane 0: per stage issues six tcgen05.mma.kind::tf32 with A from
+//    TMEM and B from shared memory (two K-steps x three products) into the
+//    chunk's TMEM accumulator; commits free the A slot, the B stage and, at the
+//    end of a chunk, publish it to the A side.
+// TMEM columns: [0, 256) two chunk accumulators, [256, 384) running sum,
+// [384, 480) three A slots of 16 hi + 16 lo columns.
 //
 // All waits are bounded (kWaitLimitNs of wall time, then this file's device
-// error word is set); on any timeout every role skips the rest of its work and meets the
-// others at the final barrier, after the MMA thread has waited (bounded) for its
-// outstanding MMAs, so TMEM is always freed.
+// error word is set and the CTA's abort flag raised); on a timeout every role
+// skips the rest of its work and meets the others at the final barrier, after
+// the producer has waited (bounded) for its copies in flight and the MMA thread
+// for its MMAs, so TMEM is always freed and no copy outlives the CTA.
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstring>
+#include <vector>
 
 #include "bag_kernels.h"
 
@@ -42,21 +55,21 @@ __device__ unsigned int g_tc_device_error = 0;
 
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 8, kStages = 6;
-#ifndef BAG_TC_CHUNK_BLOCKS
-#define BAG_TC_CHUNK_BLOCKS 4
-#endif
-// k-blocks per tensor-core accumulation chunk (K = 8 * kChunkBlocks).  The
-// tensor core accumulates with round-toward-zero, so its error grows linearly
-// with the chunk length; chunks are kept short and summed in FP32 with
-// round-to-nearest (Ootomo & Yokota 2022, sec. 4).
-constexpr int kChunkBlocks = BAG_TC_CHUNK_BLOCKS;
-constexpr int kEpiThreads = 128, kProdThreads = 128;
-constexpr int kThreads = kEpiThreads + 32 + kProdThreads;   // 288
-constexpr int kMmaWarp = 4;
-constexpr unsigned kTmemCols = 512;   // power of two >= 3 x 128 columns
+constexpr int kBM = 128, kBN = 128;
+constexpr int kKS = 16;            // k per pipeline stage: two MMA K-steps of 8
+constexpr int kChunkStages = 2;    // stages per tensor-core accumulation chunk (K = 32)
+constexpr int kASlots = 3;         // TMEM A stages
+constexpr int kBStages = 3;        // shared-memory B hi/lo stages
+constexpr int kMaxRaw = 12;        // raw operand stages, upper bound
+constexpr int kThreads = 320;
+constexpr int kTmaWarp = 8, kMmaWarp = 9;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColTotal = 256, kColA = 384;
+constexpr int kTermBytes = kBM * kKS * 4;   // one operand term's raw tile per stage (8 KB)
+constexpr int kSmemBytes = 232448;          // 227 KB, the sm_100 per-CTA maximum
 constexpr unsigned kSuspendNs = 1000000;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+constexpr int kMaxMaps = 64;
 
 // Instruction descriptor: F32 accumulate, TF32 A and B, both K-major,
 // N = 128, M = 128 (bits: c_format[4,6)=1, a_format[7,10)=2, b_format[10,13)=2,
@@ -64,22 +77,34 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) |
                             (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
 
-struct TcSmem {
-  // Per stage: four 128 x 8 TF32 tiles of 4 KB each, K-major without swizzle:
-  // core matrices of 8 rows x 4 k (16 B rows), element (r, k) of a tile at byte
-  // (r/8)*256 + (k/4)*128 + (r%8)*16 + (k%4)*4 (r = m for A, n for B).
-  float a_hi[kStages][kBM * kBK];
-  float a_lo[kStages][kBM * kBK];
-  float b_hi[kStages][kBN * kBK];
-  float b_lo[kStages][kBN * kBK];
-  unsigned long long full[kStages];
-  unsigned long long empty[kStages];
-  unsigned long long chunk_full[2];
-  unsigned long long chunk_empty[2];
+struct TcShared {
+  // B hi/lo tiles per stage and K-step, K-major without swizzle: core
+  // matrices of 8 rows x 4 k (16-byte rows), element (n, k) at byte
+  // (n/8)*256 + (k/4)*128 + (n%8)*16 + (k%4)*4 of its 4 KB tile.
+  float b_tiles[kBStages][2][2][kBN * 8];
+  unsigned long long raw_full[kMaxRaw], raw_empty[kMaxRaw];
+  unsigned long long a_full[kASlots], a_empty[kASlots];
+  unsigned long long b_full[kBStages], b_empty[kBStages];
+  unsigned long long chunk_full[2], chunk_empty[2];
   unsigned long long mma_done;
   uint32_t tmem_base;
   int abort;
 };
+constexpr int kRawOffset = (int(sizeof(TcShared)) + 1023) / 1024 * 1024;
+constexpr int kRawBytes = kSmemBytes - kRawOffset;
+static_assert(kRawBytes >= 2 * 2 * kMaxOperandTerms * kTermBytes,
+              "two raw stages of the largest product must fit");
+
+// Kernel-parameter tensor maps: operand term i of the plan is read through
+// map[op_map[i] & 0xffff] at block origin (op_x[i], op_y[i]); bit 16 of
+// op_map marks an operand shared by every batch entry (batch coordinate 0).
+struct alignas(64) TcMaps {
+  CUtensorMap map[kMaxMaps];
+  int op_map[kMaxTerms];
+  int op_x[kMaxTerms];
+  int op_y[kMaxTerms];
+};
+static_assert(sizeof(LeafPlan) + sizeof(TcMaps) + 64 <= 32764, "kernel parameters too large");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -91,12 +116,13 @@ __device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned coun
 }
 
 __device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
-  unsigned long long state;
-  asm volatile("mbarrier.arrive.shared::cta.b64 %0, [%1];"
-               : "=l"(state)
-               : "r"(smem_u32(bar))
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, int bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
                : "memory");
-  (void)state;
 }
 
 __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
@@ -117,8 +143,9 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Bounded wait; on timeout sets the error word and the CTA's abort flag.
-__device__ __forceinline__ bool mbar_wait(TcSmem& sm, unsigned long long* bar, unsigned parity) {
+// Bounded wait; on timeout (or when another role gave up) sets the error word
+// and the CTA's abort flag and returns false.
+__device__ __forceinline__ bool mbar_wait(TcShared& sm, unsigned long long* bar, unsigned parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_ns();
   while (!mbar_try_wait(bar, parity)) {
@@ -131,11 +158,33 @@ __device__ __forceinline__ bool mbar_wait(TcSmem& sm, unsigned long long* bar, u
   return true;
 }
 
+// Bounded wait that ignores the abort flag: for copies and MMAs already in
+// flight, which must land before the CTA exits.
+__device__ __forceinline__ void mbar_drain(unsigned long long* bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity)) return;
+  const unsigned long long start = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - start > kWaitLimitNs) {
+      atomicOr(&g_tc_device_error, 1u);
+      return;
+    }
+  }
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
 }
 
 // Shared-memory matrix descriptor, no swizzle: start, leading and stride byte
@@ -146,16 +195,17 @@ __device__ __forceinline__ uint64_t smem_desc(const void* p, uint32_t lbo, uint3
          (uint64_t((sbo >> 4) & 0x3FFF) << 32) | (uint64_t(1) << 46);
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                         bool accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem]^T, one K-step of 8.
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                       bool accumulate) {
   const uint32_t acc = accumulate ? 1u : 0u;
   const uint32_t zero = 0u;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}"
       :
-      : "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(kIdesc), "r"(acc), "r"(zero)
+      : "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(kIdesc), "r"(acc), "r"(zero)
       : "memory");
 }
 
@@ -198,6 +248,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ float tf32_rn(float x) {
   uint32_t u;
   asm("cvt.rn.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));
@@ -212,16 +271,6 @@ __device__ __forceinline__ float4 split_lo(float4 v, float4 hi) {
                      tf32_rn(v.w - hi.w));
 }
 
-__device__ __forceinline__ const Prod& find_prod(const LeafPlan& plan, int item) {
-  int pid = 0;
-  while (pid + 1 < plan.nprod && plan.prod[pid + 1].tile_begin <= item) ++pid;
-  return plan.prod[pid];
-}
-
-__device__ __forceinline__ float4 ldg4(const float* p) {
-  return __ldg(reinterpret_cast<const float4*>(p));
-}
-
 __device__ __forceinline__ float4 add_signed(float4 acc, float4 v, float coef) {
   return make_float4(fmaf(coef, v.x, acc.x), fmaf(coef, v.y, acc.y), fmaf(coef, v.z, acc.z),
                      fmaf(coef, v.w, acc.w));
@@ -231,187 +280,171 @@ __device__ __forceinline__ float4 signed_first(float4 v, float coef) {
   return coef < 0.f ? make_float4(-v.x, -v.y, -v.z, -v.w) : v;
 }
 
-// Producer thread p (0..127) stages, per k-block, row p of the A tile (its 8
-// k values as two 4-vectors, q = k/4; scalar loads, coalesced along m across
-// the warp) and the B vectors (k-chunk kc of column n) for
-// n = (idx/16)*8 + idx%8, kc = (idx/8)%2 with idx = p and p+128.  Every 16-byte
-// shared store of a quarter warp covers 128 contiguous bytes (no conflicts).
-template <int NL, int NR>
-__device__ __forceinline__ void produce(const LeafPlan& plan, const Prod& P, int m0, int n0,
-                                        long long batch, TcSmem& sm, int p, int kblocks) {
-  int bn[2], bkc[2];
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int idx = p + 128 * q;
-    bn[q] = (idx / 16) * 8 + idx % 8;
-    bkc[q] = (idx / 8) % 2;
-  }
-  const long long lda = plan.terms[P.l0].ld, ldb = plan.terms[P.r0].ld;
-  const float* ba[NL];
-  float ca[NL];
-#pragma unroll
-  for (int t = 0; t < NL; ++t) {
-    const Term& T = plan.terms[P.l0 + t];
-    ba[t] = T.p + batch * T.bstride;
-    ca[t] = T.coef;
-  }
-  const float* bb[NR];
-  float cb[NR];
-#pragma unroll
-  for (int t = 0; t < NR; ++t) {
-    const Term& T = plan.terms[P.r0 + t];
-    bb[t] = T.p + batch * T.bstride;
-    cb[t] = T.coef;
-  }
-  // Clamped addresses: rows >= m and columns >= n are loaded but never stored.
-  long long oa = min(m0 + p, P.m - 1), ob[2];
-#pragma unroll
-  for (int q = 0; q < 2; ++q) ob[q] = 4 * bkc[q] + (long long)min(n0 + bn[q], P.n - 1) * ldb;
-  const int kfull = P.k / kBK;
-  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-
-  float4 la[2][NL][2], lb[2][NR][2];
-  auto load = [&](float4 (&xa)[NL][2], float4 (&xb)[NR][2], int kb) {
-    const bool full_tile = kb < kfull;
-    const int k0 = kb * kBK;
-#pragma unroll
-    for (int t = 0; t < NL; ++t) {
-      const float* col = ba[t] + oa;
-      float e[kBK];
-#pragma unroll
-      for (int j = 0; j < kBK; ++j)
-        e[j] = (full_tile || k0 + j < P.k) ? __ldg(col + (long long)j * lda) : 0.f;
-      xa[t][0] = make_float4(e[0], e[1], e[2], e[3]);
-      xa[t][1] = make_float4(e[4], e[5], e[6], e[7]);
-    }
-    oa += kBK * lda;
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const bool bv = full_tile || k0 + 4 * bkc[q] < P.k;
-#pragma unroll
-      for (int t = 0; t < NR; ++t) xb[t][q] = bv ? ldg4(bb[t] + ob[q]) : z;
-      ob[q] += kBK;
-    }
-  };
-  auto store = [&](const float4 (&xa)[NL][2], const float4 (&xb)[NR][2], int s) {
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      float4 v = signed_first(xa[0][q], ca[0]);
-#pragma unroll
-      for (int t = 1; t < NL; ++t) v = add_signed(v, xa[t][q], ca[t]);
-      const float4 hi = split_hi(v);
-      const int off = (p / 8) * 64 + q * 32 + (p % 8) * 4;   // floats
-      *reinterpret_cast<float4*>(&sm.a_hi[s][off]) = hi;
-      *reinterpret_cast<float4*>(&sm.a_lo[s][off]) = split_lo(v, hi);
-    }
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      float4 v = signed_first(xb[0][q], cb[0]);
-#pragma unroll
-      for (int t = 1; t < NR; ++t) v = add_signed(v, xb[t][q], cb[t]);
-      const float4 hi = split_hi(v);
-      const int off = (bn[q] / 8) * 64 + bkc[q] * 32 + (bn[q] % 8) * 4;   // floats
-      *reinterpret_cast<float4*>(&sm.b_hi[s][off]) = hi;
-      *reinterpret_cast<float4*>(&sm.b_lo[s][off]) = split_lo(v, hi);
-    }
-  };
-  auto publish = [&](const float4 (&xa)[NL][2], const float4 (&xb)[NR][2], int kb) {
-    const int s = kb % kStages;
-    if (kb >= kStages && !mbar_wait(sm, &sm.empty[s], ((kb / kStages) - 1) & 1)) return false;
-    store(xa, xb, s);
-    // The tensor core reads these tiles through the async proxy.
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_arrive(&sm.full[s]);
-    return true;
-  };
-  if (kblocks > 0) load(la[0], lb[0], 0);
-  if (kblocks > 1) load(la[1], lb[1], 1);
-  for (int kb = 0; kb < kblocks; kb += 2) {
-    if (!publish(la[0], lb[0], kb)) return;
-    if (kb + 2 < kblocks) load(la[0], lb[0], kb + 2);
-    if (kb + 1 < kblocks) {
-      if (!publish(la[1], lb[1], kb + 1)) return;
-      if (kb + 3 < kblocks) load(la[1], lb[1], kb + 3);
-    }
-  }
+__device__ __forceinline__ const Prod& find_prod(const LeafPlan& plan, int item) {
+  int pid = 0;
+  while (pid + 1 < plan.nprod && plan.prod[pid + 1].tile_begin <= item) ++pid;
+  return plan.prod[pid];
 }
 
-// Single elected thread of the MMA warp.
-__device__ __forceinline__ void issue_mmas(TcSmem& sm, uint32_t tmem, int kblocks) {
+// ---- producer (warp 8, lane 0) --------------------------------------------
+__device__ void run_producer(TcShared& sm, unsigned char* raw, const TcMaps& maps, const Prod& P,
+                             int m0, int n0, int batch, int nraw, int slot_bytes, int stages) {
   int issued = 0;
-  for (int kb = 0; kb < kblocks; ++kb) {
-    const int chunk = kb / kChunkBlocks, in_chunk = kb % kChunkBlocks;
-    const int buf = chunk & 1;
-    if (in_chunk == 0 && chunk >= 2 && !mbar_wait(sm, &sm.chunk_empty[buf], ((chunk >> 1) - 1) & 1))
-      break;
-    const int s = kb % kStages;
-    if (!mbar_wait(sm, &sm.full[s], (kb / kStages) & 1)) break;
+  for (int s = 0; s < stages; ++s) {
+    const int slot = s % nraw;
+    if (s >= nraw && !mbar_wait(sm, &sm.raw_empty[slot], ((s / nraw) - 1) & 1)) break;
+    unsigned char* dst = raw + slot * slot_bytes;
+    mbar_expect_tx(&sm.raw_full[slot], slot_bytes);
+    const int k0 = s * kKS;
+    for (int t = 0; t < P.nl; ++t) {
+      const int ti = P.l0 + t, id = maps.op_map[ti];
+      tma_load_3d(dst + t * kTermBytes, &maps.map[id & 0xffff], maps.op_x[ti] + m0,
+                  maps.op_y[ti] + k0, (id >> 16) ? 0 : batch, &sm.raw_full[slot]);
+    }
+    for (int t = 0; t < P.nr; ++t) {
+      const int ti = P.r0 + t, id = maps.op_map[ti];
+      tma_load_3d(dst + (P.nl + t) * kTermBytes, &maps.map[id & 0xffff], maps.op_x[ti] + k0,
+                  maps.op_y[ti] + n0, (id >> 16) ? 0 : batch, &sm.raw_full[slot]);
+    }
+    ++issued;
+  }
+  // No copy may outlive the CTA: wait for the latest phase of every slot that
+  // still has one in flight (the earlier phases of a slot completed before the
+  // consumers released it).
+  for (int s = max(0, issued - nraw); s < issued; ++s) mbar_drain(&sm.raw_full[s % nraw], (s / nraw) & 1);
+}
+
+// ---- MMA issuer (warp 9, lane 0) ------------------------------------------
+__device__ void run_mma(TcShared& sm, uint32_t tmem, int stages) {
+  for (int s = 0; s < stages; ++s) {
+    const int c = s / kChunkStages, buf = c & 1, as = s % kASlots, bs = s % kBStages;
+    const bool first = s % kChunkStages == 0;
+    if (first && c >= 2 && !mbar_wait(sm, &sm.chunk_empty[buf], ((c >> 1) - 1) & 1)) break;
+    if (!mbar_wait(sm, &sm.a_full[as], (s / kASlots) & 1)) break;
+    if (!mbar_wait(sm, &sm.b_full[bs], (s / kBStages) & 1)) break;
     tc_fence_after();
     const uint32_t d = tmem + uint32_t(buf * kBN);
-    // A and B: 8-row groups 256 B apart (SBO), the two K halves 128 B apart (LBO).
-    const uint64_t ahi = smem_desc(sm.a_hi[s], 128, 256);
-    const uint64_t alo = smem_desc(sm.a_lo[s], 128, 256);
-    const uint64_t bhi = smem_desc(sm.b_hi[s], 128, 256);
-    const uint64_t blo = smem_desc(sm.b_lo[s], 128, 256);
-    mma_tf32(d, ahi, bhi, in_chunk > 0);
-    mma_tf32(d, ahi, blo, true);
-    mma_tf32(d, alo, bhi, true);
-    mma_commit(&sm.empty[s]);
-    ++issued;
-    if (in_chunk == kChunkBlocks - 1 || kb == kblocks - 1) mma_commit(&sm.chunk_full[buf]);
-  }
-  // Drain: all issued MMAs must finish before TMEM is released.
-  mma_commit(&sm.mma_done);
-  mbar_wait(sm, &sm.mma_done, 0);
-  (void)issued;
-}
-
-// Epilogue warps 0-3: thread = TMEM lane = output row of the tile.
-__device__ __forceinline__ bool fold_chunks(TcSmem& sm, uint32_t tmem, int kblocks) {
-  const int warp = threadIdx.x >> 5;
-  const uint32_t lane_base = uint32_t(warp * 32) << 16;
-  const uint32_t total = tmem + lane_base + uint32_t(2 * kBN);
-  const int chunks = (kblocks + kChunkBlocks - 1) / kChunkBlocks;
-  for (int c = 0; c < chunks; ++c) {
-    const int buf = c & 1;
-    // Warp-uniform outcome: the tcgen05.ld/st below are warp-collective.
-    const bool ok = mbar_wait(sm, &sm.chunk_full[buf], (c >> 1) & 1);
-    if (!__all_sync(0xffffffffu, ok)) return false;
-    tc_fence_after();
-    const uint32_t chunk = tmem + lane_base + uint32_t(buf * kBN);
-#pragma unroll 1
-    for (int piece = 0; piece < kBN / 32; ++piece) {
-      float v[32];
-      tmem_ld32(chunk + piece * 32, v);
-      if (c > 0) {
-        float t[32];
-        tmem_ld32(total + piece * 32, t);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(t[i], v[i]);
-      } else {
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      }
-      tmem_st32(total + piece * 32, v);
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t a_hi = tmem + kColA + uint32_t(as * 32 + j * 8);
+      const uint32_t a_lo = a_hi + 16;
+      // B tiles: 8-row groups 256 B apart (SBO), the two K halves 128 B apart (LBO).
+      const uint64_t b_hi = smem_desc(sm.b_tiles[bs][0][j], 128, 256);
+      const uint64_t b_lo = smem_desc(sm.b_tiles[bs][1][j], 128, 256);
+      mma_ts(d, a_hi, b_hi, !(first && j == 0));
+      mma_ts(d, a_hi, b_lo, true);
+      mma_ts(d, a_lo, b_hi, true);
     }
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-    tc_fence_before();
-    mbar_arrive(&sm.chunk_empty[buf]);
+    mma_commit(&sm.a_empty[as]);
+    mma_commit(&sm.b_empty[bs]);
+    if (s % kChunkStages == kChunkStages - 1 || s == stages - 1) mma_commit(&sm.chunk_full[buf]);
   }
-  return true;
+  // All issued MMAs must finish before TMEM is released.
+  mma_commit(&sm.mma_done);
+  mbar_drain(&sm.mma_done, 0);
 }
 
-__device__ __forceinline__ void store_outputs(const LeafPlan& plan, const Prod& P, int m0, int n0,
-                                              long long batch, uint32_t tmem) {
-  const int warp = threadIdx.x >> 5;
-  const int row = warp * 32 + (threadIdx.x & 31);
-  const uint32_t total = tmem + (uint32_t(warp * 32) << 16) + uint32_t(2 * kBN);
-  const int r = m0 + row;
+// ---- B side (warps 4-7; thread = tile column n) -----------------------------
+__device__ void run_b_side(TcShared& sm, const unsigned char* raw, const LeafPlan& plan,
+                           const Prod& P, int nraw, int slot_bytes, int stages) {
+  const int lane = threadIdx.x & 31;
+  const int n = threadIdx.x - 128;
+  float coef[kMaxOperandTerms];
+#pragma unroll
+  for (int t = 0; t < kMaxOperandTerms; ++t) coef[t] = t < P.nr ? plan.terms[P.r0 + t].coef : 0.f;
+  // Raw B tile: row n of 64 bytes, 16-byte chunk j at chunk j ^ ((n >> 1) & 3).
+  int chunk_off[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) chunk_off[j] = n * 64 + ((j ^ ((n >> 1) & 3)) * 16);
+  const int tile_off = (n / 8) * 64 + (n % 8) * 4;   // floats, within a 4 KB hi/lo tile
+  for (int s = 0; s < stages; ++s) {
+    const int slot = s % nraw, bs = s % kBStages;
+    bool w = mbar_wait(sm, &sm.raw_full[slot], (s / nraw) & 1);
+    if (w && s >= kBStages) w = mbar_wait(sm, &sm.b_empty[bs], ((s / kBStages) - 1) & 1);
+    if (!__all_sync(0xffffffffu, w)) return;
+    const unsigned char* src = raw + slot * slot_bytes + P.nl * kTermBytes;
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      v[j] = signed_first(*reinterpret_cast<const float4*>(src + chunk_off[j]), coef[0]);
+#pragma unroll
+    for (int t = 1; t < kMaxOperandTerms; ++t) {
+      if (t >= P.nr) break;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        v[j] = add_signed(v[j], *reinterpret_cast<const float4*>(src + t * kTermBytes + chunk_off[j]),
+                          coef[t]);
+    }
+    const int k0 = s * kKS;
+    if (k0 + kKS > P.k) {   // K tail: the box reaches past the block
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (k0 + 4 * j + 0 >= P.k) v[j].x = 0.f;
+        if (k0 + 4 * j + 1 >= P.k) v[j].y = 0.f;
+        if (k0 + 4 * j + 2 >= P.k) v[j].z = 0.f;
+        if (k0 + 4 * j + 3 >= P.k) v[j].w = 0.f;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.raw_empty[slot]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 hi = split_hi(v[j]);
+      const int off = tile_off + (j & 1) * 32;
+      *reinterpret_cast<float4*>(&sm.b_tiles[bs][0][j >> 1][off]) = hi;
+      *reinterpret_cast<float4*>(&sm.b_tiles[bs][1][j >> 1][off]) = split_lo(v[j], hi);
+    }
+    // The tensor core reads these tiles through the async proxy.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.b_full[bs]);
+  }
+}
+
+// ---- A side (warps 0-3; thread = tile row = TMEM lane) ----------------------
+// Folds accumulation chunk c into the running sum (columns kColTotal..).
+__device__ bool fold_chunk(TcShared& sm, uint32_t tmem, uint32_t lane_base, int c) {
+  const int buf = c & 1;
+  const bool w = mbar_wait(sm, &sm.chunk_full[buf], (c >> 1) & 1);
+  if (!__all_sync(0xffffffffu, w)) return false;   // tcgen05.ld/st below are warp-collective
+  tc_fence_after();
+  const uint32_t chunk = tmem + lane_base + uint32_t(buf * kBN);
+  const uint32_t total = tmem + lane_base + kColTotal;
 #pragma unroll 1
   for (int piece = 0; piece < kBN / 32; ++piece) {
     float v[32];
-    tmem_ld32(total + piece * 32, v);
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    tmem_ld32(chunk + piece * 32, v);
+    if (c > 0) {
+      float t[32];
+      tmem_ld32(total + piece * 32, t);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(t[i], v[i]);
+    } else {
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    }
+    tmem_st32(total + piece * 32, v);
+  }
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  tc_fence_before();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.chunk_empty[buf]);
+  return true;
+}
+
+__device__ void store_outputs(const LeafPlan& plan, const Prod& P, int m0, int n0, long long batch,
+                              uint32_t total, bool empty_sum) {
+  const int r = m0 + int(threadIdx.x);
+#pragma unroll 1
+  for (int piece = 0; piece < kBN / 32; ++piece) {
+    float v[32];
+    if (empty_sum) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    } else {
+      tmem_ld32(total + piece * 32, v);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    }
     if (r >= P.m) continue;
     for (int o = 0; o < P.no; ++o) {
       const Term& T = plan.terms[P.o0 + o];
@@ -430,25 +463,111 @@ __device__ __forceinline__ void store_outputs(const LeafPlan& plan, const Prod& 
   }
 }
 
+__device__ void run_a_side(TcShared& sm, const unsigned char* raw, const LeafPlan& plan,
+                           const Prod& P, int m0, int n0, long long batch, uint32_t tmem, int nraw,
+                           int slot_bytes, int stages) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = threadIdx.x;
+  const uint32_t lane_base = uint32_t(warp * 32) << 16;
+  float coef[kMaxOperandTerms];
+#pragma unroll
+  for (int t = 0; t < kMaxOperandTerms; ++t) coef[t] = t < P.nl ? plan.terms[P.l0 + t].coef : 0.f;
+  for (int s = 0; s < stages; ++s) {
+    const int slot = s % nraw, as = s % kASlots;
+    bool w = mbar_wait(sm, &sm.raw_full[slot], (s / nraw) & 1);
+    if (w && s >= kASlots) w = mbar_wait(sm, &sm.a_empty[as], ((s / kASlots) - 1) & 1);
+    if (!__all_sync(0xffffffffu, w)) return;   // tcgen05.st below is warp-collective
+    // Raw A tile: 16 k-rows of 128 m (512 B each); a warp reads 128 contiguous bytes.
+    const float* src = reinterpret_cast<const float*>(raw + slot * slot_bytes) + row;
+    float v[kKS];
+#pragma unroll
+    for (int k = 0; k < kKS; ++k) {
+      const float x = src[k * kBM];
+      v[k] = coef[0] < 0.f ? -x : x;
+    }
+#pragma unroll
+    for (int t = 1; t < kMaxOperandTerms; ++t) {
+      if (t >= P.nl) break;
+#pragma unroll
+      for (int k = 0; k < kKS; ++k) v[k] = fmaf(coef[t], src[t * (kTermBytes / 4) + k * kBM], v[k]);
+    }
+    const int k0 = s * kKS;
+    if (k0 + kKS > P.k) {   // K tail: the box reaches past the block
+#pragma unroll
+      for (int k = 0; k < kKS; ++k)
+        if (k0 + k >= P.k) v[k] = 0.f;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.raw_empty[slot]);
+    uint32_t hi[kKS], lo[kKS];
+#pragma unroll
+    for (int k = 0; k < kKS; ++k) {
+      const float h = tf32_rn(v[k]);
+      hi[k] = __float_as_uint(h);
+      lo[k] = __float_as_uint(tf32_rn(v[k] - h));
+    }
+    const uint32_t a_col = tmem + lane_base + kColA + uint32_t(as * 32);
+    tmem_st16(a_col, hi);
+    tmem_st16(a_col + 16, lo);
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.a_full[as]);
+    // Fold the chunk that ended with the previous stage while this one runs.
+    if (s > 0 && s % kChunkStages == 0 && !fold_chunk(sm, tmem, lane_base, s / kChunkStages - 1))
+      return;
+  }
+  if (stages > 0 && !fold_chunk(sm, tmem, lane_base, (stages - 1) / kChunkStages)) return;
+  if (*(volatile int*)&sm.abort) return;
+  store_outputs(plan, P, m0, n0, batch, tmem + lane_base + kColTotal, stages == 0);
+}
+
 }  // namespace
 
-__global__ void __launch_bounds__(kThreads, 1) leaf_tc_kernel(const __grid_constant__ LeafPlan plan) {
+__global__ void __launch_bounds__(kThreads, 1)
+    leaf_tc_kernel(const __grid_constant__ LeafPlan plan, const __grid_constant__ TcMaps maps) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  TcSmem& sm = *reinterpret_cast<TcSmem*>(smem_raw);
-  const int warp = threadIdx.x >> 5;
+  TcShared& sm = *reinterpret_cast<TcShared*>(smem_raw);
+  unsigned char* raw = smem_raw + kRawOffset;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const Prod& P = find_prod(plan, blockIdx.x);
+  const int local = blockIdx.x - P.tile_begin;
+  constexpr int GROUP_M = 8;
+  const int in_group = GROUP_M * P.tiles_n;
+  const int first_m = (local / in_group) * GROUP_M;
+  const int gsize = min(P.tiles_m - first_m, GROUP_M);
+  const int m0 = (first_m + (local % in_group) % gsize) * kBM;
+  const int n0 = ((local % in_group) / gsize) * kBN;
+  const int batch = blockIdx.y;
+  const bool valid = P.nl >= 1 && P.nl <= kMaxOperandTerms && P.nr >= 1 && P.nr <= kMaxOperandTerms;
+  const int slot_bytes = (valid ? P.nl + P.nr : 1) * kTermBytes;
+  const int nraw = min(kMaxRaw, kRawBytes / slot_bytes);
+  const int stages = (P.k + kKS - 1) / kKS;
+
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], kProdThreads);
-      mbar_init(&sm.empty[s], 1);
+    for (int i = 0; i < nraw; ++i) {
+      mbar_init(&sm.raw_full[i], 1);
+      mbar_init(&sm.raw_empty[i], 8);   // the 8 transform warps
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.chunk_full[b], 1);
-      mbar_init(&sm.chunk_empty[b], kEpiThreads);
+    for (int i = 0; i < kASlots; ++i) {
+      mbar_init(&sm.a_full[i], 4);
+      mbar_init(&sm.a_empty[i], 1);
+    }
+    for (int i = 0; i < kBStages; ++i) {
+      mbar_init(&sm.b_full[i], 4);
+      mbar_init(&sm.b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.chunk_full[i], 1);
+      mbar_init(&sm.chunk_empty[i], 4);
     }
     mbar_init(&sm.mma_done, 1);
     sm.abort = 0;
+    // Make the initialised barriers visible to the async proxy (TMA, tcgen05).
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == kMmaWarp) {
+  if (warp == kTmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&sm.tmem_base)),
                  "r"(kTmemCols)
@@ -460,53 +579,22 @@ __global__ void __launch_bounds__(kThreads, 1) leaf_tc_kernel(const __grid_const
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  const Prod& P = find_prod(plan, blockIdx.x);
-  const int local = blockIdx.x - P.tile_begin;
-  constexpr int GROUP_M = 8;
-  const int in_group = GROUP_M * P.tiles_n;
-  const int first_m = (local / in_group) * GROUP_M;
-  const int gsize = min(P.tiles_m - first_m, GROUP_M);
-  const int m0 = (first_m + (local % in_group) % gsize) * kBM;
-  const int n0 = ((local % in_group) / gsize) * kBN;
-  const long long batch = blockIdx.y;
-  const int kblocks = (P.k + kBK - 1) / kBK;
-
-  if (warp > kMmaWarp) {
-    const int p = threadIdx.x - (kEpiThreads + 32);
-    switch (P.sig) {
-      case kSig11: produce<1, 1>(plan, P, m0, n0, batch, sm, p, kblocks); break;
-      case kSig12: produce<1, 2>(plan, P, m0, n0, batch, sm, p, kblocks); break;
-      case kSig21: produce<2, 1>(plan, P, m0, n0, batch, sm, p, kblocks); break;
-      case kSig22: produce<2, 2>(plan, P, m0, n0, batch, sm, p, kblocks); break;
-      case kSig33: produce<3, 3>(plan, P, m0, n0, batch, sm, p, kblocks); break;
-      case kSig41: produce<4, 1>(plan, P, m0, n0, batch, sm, p, kblocks); break;
-      case kSig14: produce<1, 4>(plan, P, m0, n0, batch, sm, p, kblocks); break;
-      default:
-        atomicOr(&g_tc_device_error, 2u);
-        *(volatile int*)&sm.abort = 1;
-        break;
-    }
-  } else if (warp == kMmaWarp) {
-    if (P.sig != kSigGeneric && (threadIdx.x & 31) == 0) issue_mmas(sm, tmem, kblocks);
+  if (!valid) {
+    if (threadIdx.x == 0) atomicOr(&g_tc_device_error, 2u);
+  } else if (warp == kTmaWarp) {
+    if (lane == 0) run_producer(sm, raw, maps, P, m0, n0, batch, nraw, slot_bytes, stages);
     __syncwarp();
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) run_mma(sm, tmem, stages);
+    __syncwarp();
+  } else if (warp >= 4) {
+    run_b_side(sm, raw, plan, P, nraw, slot_bytes, stages);
   } else {
-    bool ok = P.sig != kSigGeneric;
-    if (ok && kblocks > 0) ok = fold_chunks(sm, tmem, kblocks);
-    if (ok) {
-      if (kblocks == 0) {   // empty reduction: the sum is zero
-        float zero[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) zero[i] = 0.f;
-        const uint32_t total = tmem + (uint32_t(warp * 32) << 16) + uint32_t(2 * kBN);
-        for (int piece = 0; piece < kBN / 32; ++piece) tmem_st32(total + piece * 32, zero);
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      }
-      if (!*(volatile int*)&sm.abort) store_outputs(plan, P, m0, n0, batch, tmem);
-    }
+    run_a_side(sm, raw, plan, P, m0, n0, batch, tmem, nraw, slot_bytes, stages);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kTmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols)
@@ -514,27 +602,168 @@ __global__ void __launch_bounds__(kThreads, 1) leaf_tc_kernel(const __grid_const
   }
 }
 
+namespace {
+
+using EncodeTiled = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeTiled encode_fn() {
+  static const EncodeTiled fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return EncodeTiled(nullptr);
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+struct MapKey {
+  const float* base;
+  long long ld, bstride, rows, cols, nb;
+  bool left;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && ld == o.ld && bstride == o.bstride && rows == o.rows &&
+           cols == o.cols && nb == o.nb && left == o.left;
+  }
+};
+
+// Tensor maps of one launch.  Left operands use box {128 m, 16 k} without
+// swizzle, right operands box {16 k, 128 n} with 64-byte swizzle.
+class MapTable {
+ public:
+  explicit MapTable(TcMaps& out) : out_(out) {}
+  void reset() {
+    keys_.clear();
+    std::memset(&out_, 0, sizeof(out_));
+  }
+  // Map id for `key`, encoding a new map when needed; -1 when the table is
+  // full, -2 when the driver rejects the map.
+  int get(const MapKey& key) {
+    for (size_t i = 0; i < keys_.size(); ++i)
+      if (keys_[i] == key) return int(i);
+    if (keys_.size() >= size_t(kMaxMaps)) return -1;
+    const EncodeTiled enc = encode_fn();
+    if (!enc) return -2;
+    const cuuint64_t dims[3] = {cuuint64_t(key.rows), cuuint64_t(key.cols), cuuint64_t(key.nb)};
+    const long long bs = key.bstride ? key.bstride : key.ld * key.cols;
+    const cuuint64_t strides[2] = {cuuint64_t(key.ld) * 4, cuuint64_t(bs) * 4};
+    const cuuint32_t box[3] = {key.left ? 128u : 16u, key.left ? 16u : 128u, 1u};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUtensorMap& m = out_.map[keys_.size()];
+    const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(key.base),
+                           dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           key.left ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return -2;
+    keys_.push_back(key);
+    return int(keys_.size()) - 1;
+  }
+
+ private:
+  TcMaps& out_;
+  std::vector<MapKey> keys_;
+};
+
+// Map and origin of operand term `t` (extent rows x cols): the containing
+// source matrix when there is one, else a map of the block itself (whose
+// zero fill then also covers the tile's overhang).
+int assign_operand(MapTable& maps, TcMaps& out, int ti, const Term& t, long long rows,
+                   long long cols, bool left, const TcSource* src, int nsrc, int batch) {
+  const long long nb = t.bstride ? batch : 1;
+  for (int i = 0; i < nsrc; ++i) {
+    const TcSource& S = src[i];
+    if (S.ld != t.ld || S.bstride != t.bstride || t.p < S.base) continue;
+    const long long off = t.p - S.base;
+    const long long x = off % S.ld, y = off / S.ld;
+    if (x + rows > S.rows || y + cols > S.cols) continue;
+    const int id = maps.get({S.base, S.ld, S.bstride, S.rows, S.cols, nb, left});
+    if (id < 0) return id;
+    out.op_map[ti] = id | (t.bstride ? 0 : 0x10000);
+    out.op_x[ti] = int(x);
+    out.op_y[ti] = int(y);
+    return id;
+  }
+  const int id = maps.get({t.p, t.ld, t.bstride, rows, cols, nb, left});
+  if (id < 0) return id;
+  out.op_map[ti] = id | (t.bstride ? 0 : 0x10000);
+  out.op_x[ti] = 0;
+  out.op_y[ti] = 0;
+  return id;
+}
+
+cudaError_t launch_subplan(const LeafPlan& full, int p0, int p1, const TcMaps& maps, int batch,
+                           cudaStream_t stream) {
+  if (p1 <= p0) return cudaSuccess;
+  LeafPlan sub;
+  sub.nprod = p1 - p0;
+  const int base = full.prod[p0].tile_begin;
+  const int end = p1 < full.nprod ? full.prod[p1].tile_begin : full.ntiles;
+  sub.ntiles = end - base;
+  for (int i = p0; i < p1; ++i) {
+    sub.prod[i - p0] = full.prod[i];
+    sub.prod[i - p0].tile_begin -= base;
+  }
+  std::memcpy(sub.terms, full.terms, sizeof(full.terms));
+  if (sub.ntiles <= 0) return cudaSuccess;
+  leaf_tc_kernel<<<dim3(sub.ntiles, batch), kThreads, kSmemBytes, stream>>>(sub, maps);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
 TileShape tc_tile_shape() { return {kBM, kBN}; }
+
+bool tc_supported(int nl, int nr) {
+  return nl >= 1 && nl <= kMaxOperandTerms && nr >= 1 && nr <= kMaxOperandTerms &&
+         encode_fn() != nullptr;
+}
+
+cudaError_t launch_leaf_tc(const LeafPlan& plan, const TcSource* sources, int nsources, int batch,
+                           cudaStream_t stream) {
+  if (plan.nprod == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
+  // The attribute is per device: set it before every launch (cheap).
+  cudaError_t e = cudaFuncSetAttribute(leaf_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kSmemBytes);
+  if (e != cudaSuccess) return e;
+  // Products are launched in runs whose tensor maps fit the parameter block.
+  static thread_local TcMaps maps;
+  MapTable table(maps);
+  table.reset();
+  int run_begin = 0;
+  for (int p = 0; p < plan.nprod; ++p) {
+    const Prod& P = plan.prod[p];
+    for (int attempt = 0; attempt < 2; ++attempt) {
+      bool ok = true;
+      for (int t = 0; t < P.nl && ok; ++t) {
+        const int id = assign_operand(table, maps, P.l0 + t, plan.terms[P.l0 + t], P.m, P.k, true,
+                                      sources, nsources, batch);
+        if (id == -2) return cudaErrorInvalidValue;
+        ok = id >= 0;
+      }
+      for (int t = 0; t < P.nr && ok; ++t) {
+        const int id = assign_operand(table, maps, P.r0 + t, plan.terms[P.r0 + t], P.k, P.n, false,
+                                      sources, nsources, batch);
+        if (id == -2) return cudaErrorInvalidValue;
+        ok = id >= 0;
+      }
+      if (ok) break;
+      if (attempt == 1 || p == run_begin) return cudaErrorInvalidValue;   // one product > kMaxMaps
+      // Table full: launch the run so far and start a new one with this product.
+      e = launch_subplan(plan, run_begin, p, maps, batch, stream);
+      if (e != cudaSuccess) return e;
+      run_begin = p;
+      table.reset();
+    }
+  }
+  return launch_subplan(plan, run_begin, plan.nprod, maps, batch, stream);
+}
 
 cudaError_t read_and_clear_tc_device_error(unsigned* value) {
   cudaError_t e = cudaMemcpyFromSymbol(value, g_tc_device_error, sizeof(unsigned));
   if (e != cudaSuccess) return e;
   const unsigned zero = 0;
   return cudaMemcpyToSymbol(g_tc_device_error, &zero, sizeof(unsigned));
-}
-
-// Dynamic shared memory per CTA: the ring, padded past half of the SM's 228 KB
-// so that only one CTA (and one 512-column TMEM allocation) fits per SM.
-constexpr int kTcSmemBytes = sizeof(TcSmem) > 120 * 1024 ? int(sizeof(TcSmem)) : 120 * 1024;
-
-cudaError_t launch_leaf_tc(const LeafPlan& plan, int batch, cudaStream_t stream) {
-  if (plan.nprod == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
-  // The attribute is per device: set it before every launch (cheap).
-  cudaError_t e = cudaFuncSetAttribute(leaf_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kTcSmemBytes);
-  if (e != cudaSuccess) return e;
-  leaf_tc_kernel<<<dim3(plan.ntiles, batch), kThreads, kTcSmemBytes, stream>>>(plan);
-  return cudaGetLastError();
 }
 
 }  // namespace bag_b200

@@ -49,7 +49,7 @@ def _rel(torch, c, a, b):
     (256, 1024, 384, 0, "minimal"), (200, 1032, 136, 0, "minimal"), (132, 1100, 260, 0, "minimal"),
     (2048, 2048, 2048, 1, "minimal"), (1536, 2064, 1032, 1, "minimal"),
     (2048, 2048, 2048, 1, "classic"), (4096, 4096, 4096, 2, "minimal"),
-    (2048, 4096, 2048, 2, "classic")])
+    (2048, 4096, 2048, 2, "classic"), (2048, 4096, 2048, 2, "full")])
 def test_tensor_path_error(tensor_mode, m, k, n, depth, basis):
     import torch
     bag = tensor_mode
