@@ -11,7 +11,7 @@
 // peak performance", sec. 4).  Measured error: 0.3-0.6x an FP32 FFMA dot
 // product's for K >= 1024.
 //
-// One CTA (320 threads, 227 KB shared memory, 1 per SM) computes a 128 x 128
+// One CTA (576 threads, 227 KB shared memory, 1 per SM) computes a 128 x 128
 // output tile of one product; the K loop runs in stages of 16:
 //  * warp 8, lane 0 (producer): TMA-loads the raw FP32 tile of every signed
 //    operand term of the stage (A term: 128 m x 16 k, M-contiguous; B term:
@@ -21,9 +21,10 @@
 //    by block coordinates, one per workspace block.  Warp 8 also owns TMEM.
 //  * warps 0-3 (A side; thread = tile row = TMEM lane): sum the A terms in the
 //    reference's order (x + delta*y, bag.cuh:69-73), zero the K tail, split
-//    hi/lo and store them into a TMEM A slot (tcgen05.st); fold each finished
-//    accumulation chunk into the running sum; finally add coef*sum into every
-//    target C block (red.global, coalesced along the column).
+//    hi/lo and store them into a TMEM A slot (tcgen05.st).
+//  * warps 10-17 (fold; two per TMEM lane quadrant, 64 columns each): add each
+//    finished accumulation chunk into the running sum, then add coef*sum into
+//    every target C block (red.global, coalesced along the column).
 //  * warps 4-7 (B side; thread = tile column): sum, split and store the B terms
 //    as K-major no-swizzle hi/lo tiles in a shared-memory ring.
 //  * warp 9, lane 0: per stage issues six tcgen05.mma.kind::tf32 with A from
@@ -56,17 +57,17 @@ __device__ unsigned int g_tc_device_error = 0;
 namespace {
 
 constexpr int kBM = 128, kBN = 128;
-constexpr int kKS = 16;            // k per pipeline stage: two MMA K-steps of 8
-constexpr int kChunkStages = 2;    // stages per tensor-core accumulation chunk (K = 32)
-constexpr int kASlots = 3;         // TMEM A stages
-constexpr int kBStages = 3;        // shared-memory B hi/lo stages
+// k per pipeline stage: 32 (four MMA K-steps of 8) for products with at most
+// four operand terms, 16 otherwise (their raw stages are larger).
+constexpr int kChunkK = 32;        // k per tensor-core accumulation chunk
 constexpr int kMaxRaw = 12;        // raw operand stages, upper bound
-constexpr int kThreads = 320;
-constexpr int kTmaWarp = 8, kMmaWarp = 9;
+constexpr int kTmaWarp = 8, kMmaWarp = 9, kFoldWarp0 = 10, kFoldWarps = 8;
+constexpr int kThreads = (kFoldWarp0 + kFoldWarps) * 32;   // 576
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColTotal = 256, kColA = 384;
-constexpr int kTermBytes = kBM * kKS * 4;   // one operand term's raw tile per stage (8 KB)
-constexpr int kSmemBytes = 232448;          // 227 KB, the sm_100 per-CTA maximum
+constexpr uint32_t kColTotal = 256, kColA = 384, kColsA = 128;
+constexpr int kBRegion = 65536;    // shared-memory ring of B hi/lo stages
+constexpr int kBoxBytes = 128 * 16 * 4;   // one TMA box: 128 m x 16 k or 16 k x 128 n
+constexpr int kSmemBytes = 232448;        // 227 KB, the sm_100 per-CTA maximum
 constexpr unsigned kSuspendNs = 1000000;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 constexpr int kMaxMaps = 64;
@@ -78,13 +79,14 @@ constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) |
                             (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
 
 struct TcShared {
-  // B hi/lo tiles per stage and K-step, K-major without swizzle: core
-  // matrices of 8 rows x 4 k (16-byte rows), element (n, k) at byte
-  // (n/8)*256 + (k/4)*128 + (n%8)*16 + (k%4)*4 of its 4 KB tile.
-  float b_tiles[kBStages][2][2][kBN * 8];
+  // B stage s (KS k) at b_region + s*KS*1024: KS/8 hi tiles then KS/8 lo
+  // tiles of 4 KB, one per MMA K-step, K-major without swizzle: core matrices
+  // of 8 rows x 4 k (16-byte rows), element (n, k) at byte
+  // (n/8)*256 + (k/4)*128 + (n%8)*16 + (k%4)*4 of its tile.
+  unsigned char b_region[kBRegion];
   unsigned long long raw_full[kMaxRaw], raw_empty[kMaxRaw];
-  unsigned long long a_full[kASlots], a_empty[kASlots];
-  unsigned long long b_full[kBStages], b_empty[kBStages];
+  unsigned long long a_full[4], a_empty[4];
+  unsigned long long b_full[4], b_empty[4];
   unsigned long long chunk_full[2], chunk_empty[2];
   unsigned long long mma_done;
   uint32_t tmem_base;
@@ -92,8 +94,8 @@ struct TcShared {
 };
 constexpr int kRawOffset = (int(sizeof(TcShared)) + 1023) / 1024 * 1024;
 constexpr int kRawBytes = kSmemBytes - kRawOffset;
-static_assert(kRawBytes >= 2 * 2 * kMaxOperandTerms * kTermBytes,
-              "two raw stages of the largest product must fit");
+// Two raw stages of the largest product: 4 terms x 32 k, or 8 terms x 16 k.
+static_assert(kRawBytes >= 2 * 2 * kMaxOperandTerms * 16 * kBM * 4, "raw ring too small");
 
 // Kernel-parameter tensor maps: operand term i of the plan is read through
 // map[op_map[i] & 0xffff] at block origin (op_x[i], op_y[i]); bit 16 of
@@ -280,6 +282,18 @@ __device__ __forceinline__ float4 signed_first(float4 v, float coef) {
   return coef < 0.f ? make_float4(-v.x, -v.y, -v.z, -v.w) : v;
 }
 
+// Position in a ring of n stages: slot index and the parity of its current use.
+struct Ring {
+  int idx = 0;
+  unsigned phase = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++idx == n) {
+      idx = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 __device__ __forceinline__ const Prod& find_prod(const LeafPlan& plan, int item) {
   int pid = 0;
   while (pid + 1 < plan.nprod && plan.prod[pid + 1].tile_begin <= item) ++pid;
@@ -287,24 +301,31 @@ __device__ __forceinline__ const Prod& find_prod(const LeafPlan& plan, int item)
 }
 
 // ---- producer (warp 8, lane 0) --------------------------------------------
+// Stage s of `ks` k: per left term ks/16 boxes {128 m, 16 k}, per right term
+// ks/16 boxes {16 k, 128 n}, each term's boxes contiguous in the slot.
 __device__ void run_producer(TcShared& sm, unsigned char* raw, const TcMaps& maps, const Prod& P,
-                             int m0, int n0, int batch, int nraw, int slot_bytes, int stages) {
+                             int m0, int n0, int batch, int nraw, int slot_bytes, int stages,
+                             int ks) {
+  const int boxes = ks / 16, term_bytes = boxes * kBoxBytes;
   int issued = 0;
-  for (int s = 0; s < stages; ++s) {
-    const int slot = s % nraw;
-    if (s >= nraw && !mbar_wait(sm, &sm.raw_empty[slot], ((s / nraw) - 1) & 1)) break;
+  Ring r;
+  for (int s = 0; s < stages; ++s, r.next(nraw)) {
+    const int slot = r.idx;
+    if (s >= nraw && !mbar_wait(sm, &sm.raw_empty[slot], r.phase ^ 1u)) break;
     unsigned char* dst = raw + slot * slot_bytes;
     mbar_expect_tx(&sm.raw_full[slot], slot_bytes);
-    const int k0 = s * kKS;
+    const int k0 = s * ks;
     for (int t = 0; t < P.nl; ++t) {
-      const int ti = P.l0 + t, id = maps.op_map[ti];
-      tma_load_3d(dst + t * kTermBytes, &maps.map[id & 0xffff], maps.op_x[ti] + m0,
-                  maps.op_y[ti] + k0, (id >> 16) ? 0 : batch, &sm.raw_full[slot]);
+      const int ti = P.l0 + t, id = maps.op_map[ti], z = (id >> 16) ? 0 : batch;
+      for (int b = 0; b < boxes; ++b)
+        tma_load_3d(dst + t * term_bytes + b * kBoxBytes, &maps.map[id & 0xffff],
+                    maps.op_x[ti] + m0, maps.op_y[ti] + k0 + 16 * b, z, &sm.raw_full[slot]);
     }
     for (int t = 0; t < P.nr; ++t) {
-      const int ti = P.r0 + t, id = maps.op_map[ti];
-      tma_load_3d(dst + (P.nl + t) * kTermBytes, &maps.map[id & 0xffff], maps.op_x[ti] + k0,
-                  maps.op_y[ti] + n0, (id >> 16) ? 0 : batch, &sm.raw_full[slot]);
+      const int ti = P.r0 + t, id = maps.op_map[ti], z = (id >> 16) ? 0 : batch;
+      for (int b = 0; b < boxes; ++b)
+        tma_load_3d(dst + (P.nl + t) * term_bytes + b * kBoxBytes, &maps.map[id & 0xffff],
+                    maps.op_x[ti] + k0 + 16 * b, maps.op_y[ti] + n0, z, &sm.raw_full[slot]);
     }
     ++issued;
   }
@@ -315,29 +336,34 @@ __device__ void run_producer(TcShared& sm, unsigned char* raw, const TcMaps& map
 }
 
 // ---- MMA issuer (warp 9, lane 0) ------------------------------------------
+template <int KS>
 __device__ void run_mma(TcShared& sm, uint32_t tmem, int stages) {
-  for (int s = 0; s < stages; ++s) {
-    const int c = s / kChunkStages, buf = c & 1, as = s % kASlots, bs = s % kBStages;
-    const bool first = s % kChunkStages == 0;
+  constexpr int kSteps = KS / 8, kNA = kColsA / (2 * KS), kNB = kBRegion / (KS * 1024);
+  constexpr int kCS = kChunkK / KS;   // stages per accumulation chunk
+  Ring ra, rb;
+  for (int s = 0; s < stages; ++s, ra.next(kNA), rb.next(kNB)) {
+    const int c = s / kCS, buf = c & 1;
+    const bool first = s % kCS == 0;
     if (first && c >= 2 && !mbar_wait(sm, &sm.chunk_empty[buf], ((c >> 1) - 1) & 1)) break;
-    if (!mbar_wait(sm, &sm.a_full[as], (s / kASlots) & 1)) break;
-    if (!mbar_wait(sm, &sm.b_full[bs], (s / kBStages) & 1)) break;
+    if (!mbar_wait(sm, &sm.a_full[ra.idx], ra.phase)) break;
+    if (!mbar_wait(sm, &sm.b_full[rb.idx], rb.phase)) break;
     tc_fence_after();
     const uint32_t d = tmem + uint32_t(buf * kBN);
+    const unsigned char* bst = sm.b_region + rb.idx * KS * 1024;
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t a_hi = tmem + kColA + uint32_t(as * 32 + j * 8);
-      const uint32_t a_lo = a_hi + 16;
+    for (int j = 0; j < kSteps; ++j) {
+      const uint32_t a_hi = tmem + kColA + uint32_t(ra.idx * 2 * KS + j * 8);
+      const uint32_t a_lo = a_hi + KS;
       // B tiles: 8-row groups 256 B apart (SBO), the two K halves 128 B apart (LBO).
-      const uint64_t b_hi = smem_desc(sm.b_tiles[bs][0][j], 128, 256);
-      const uint64_t b_lo = smem_desc(sm.b_tiles[bs][1][j], 128, 256);
+      const uint64_t b_hi = smem_desc(bst + j * 4096, 128, 256);
+      const uint64_t b_lo = smem_desc(bst + (kSteps + j) * 4096, 128, 256);
       mma_ts(d, a_hi, b_hi, !(first && j == 0));
       mma_ts(d, a_hi, b_lo, true);
       mma_ts(d, a_lo, b_hi, true);
     }
-    mma_commit(&sm.a_empty[as]);
-    mma_commit(&sm.b_empty[bs]);
-    if (s % kChunkStages == kChunkStages - 1 || s == stages - 1) mma_commit(&sm.chunk_full[buf]);
+    mma_commit(&sm.a_empty[ra.idx]);
+    mma_commit(&sm.b_empty[rb.idx]);
+    if (s % kCS == kCS - 1 || s == stages - 1) mma_commit(&sm.chunk_full[buf]);
   }
   // All issued MMAs must finish before TMEM is released.
   mma_commit(&sm.mma_done);
@@ -345,73 +371,78 @@ __device__ void run_mma(TcShared& sm, uint32_t tmem, int stages) {
 }
 
 // ---- B side (warps 4-7; thread = tile column n) -----------------------------
+template <int KS>
 __device__ void run_b_side(TcShared& sm, const unsigned char* raw, const LeafPlan& plan,
                            const Prod& P, int nraw, int slot_bytes, int stages) {
+  constexpr int kQ = KS / 4, kSteps = KS / 8, kNB = kBRegion / (KS * 1024);
+  constexpr int kTermBytes = KS / 16 * kBoxBytes;
   const int lane = threadIdx.x & 31;
   const int n = threadIdx.x - 128;
   float coef[kMaxOperandTerms];
 #pragma unroll
   for (int t = 0; t < kMaxOperandTerms; ++t) coef[t] = t < P.nr ? plan.terms[P.r0 + t].coef : 0.f;
-  // Raw B tile: row n of 64 bytes, 16-byte chunk j at chunk j ^ ((n >> 1) & 3).
-  int chunk_off[4];
+  // Raw B box: row n of 64 bytes, 16-byte chunk j at chunk j ^ ((n >> 1) & 3).
+  int chunk_off[kQ];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) chunk_off[j] = n * 64 + ((j ^ ((n >> 1) & 3)) * 16);
-  const int tile_off = (n / 8) * 64 + (n % 8) * 4;   // floats, within a 4 KB hi/lo tile
-  for (int s = 0; s < stages; ++s) {
-    const int slot = s % nraw, bs = s % kBStages;
-    bool w = mbar_wait(sm, &sm.raw_full[slot], (s / nraw) & 1);
-    if (w && s >= kBStages) w = mbar_wait(sm, &sm.b_empty[bs], ((s / kBStages) - 1) & 1);
+  for (int q = 0; q < kQ; ++q)
+    chunk_off[q] = (q / 4) * kBoxBytes + n * 64 + (((q % 4) ^ ((n >> 1) & 3)) * 16);
+  const int tile_off = (n / 8) * 256 + (n % 8) * 16;   // bytes, within a 4 KB hi/lo tile
+  Ring r, rb;
+  for (int s = 0; s < stages; ++s, r.next(nraw), rb.next(kNB)) {
+    bool w = mbar_wait(sm, &sm.raw_full[r.idx], r.phase);
+    if (w && s >= kNB) w = mbar_wait(sm, &sm.b_empty[rb.idx], rb.phase ^ 1u);
     if (!__all_sync(0xffffffffu, w)) return;
-    const unsigned char* src = raw + slot * slot_bytes + P.nl * kTermBytes;
-    float4 v[4];
+    const unsigned char* src = raw + r.idx * slot_bytes + P.nl * kTermBytes;
+    float4 v[kQ];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      v[j] = signed_first(*reinterpret_cast<const float4*>(src + chunk_off[j]), coef[0]);
+    for (int q = 0; q < kQ; ++q)
+      v[q] = signed_first(*reinterpret_cast<const float4*>(src + chunk_off[q]), coef[0]);
 #pragma unroll
     for (int t = 1; t < kMaxOperandTerms; ++t) {
       if (t >= P.nr) break;
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        v[j] = add_signed(v[j], *reinterpret_cast<const float4*>(src + t * kTermBytes + chunk_off[j]),
+      for (int q = 0; q < kQ; ++q)
+        v[q] = add_signed(v[q], *reinterpret_cast<const float4*>(src + t * kTermBytes + chunk_off[q]),
                           coef[t]);
     }
-    const int k0 = s * kKS;
-    if (k0 + kKS > P.k) {   // K tail: the box reaches past the block
+    const int k0 = s * KS;
+    if (k0 + KS > P.k) {   // K tail: the box reaches past the block
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (k0 + 4 * j + 0 >= P.k) v[j].x = 0.f;
-        if (k0 + 4 * j + 1 >= P.k) v[j].y = 0.f;
-        if (k0 + 4 * j + 2 >= P.k) v[j].z = 0.f;
-        if (k0 + 4 * j + 3 >= P.k) v[j].w = 0.f;
+      for (int q = 0; q < kQ; ++q) {
+        if (k0 + 4 * q + 0 >= P.k) v[q].x = 0.f;
+        if (k0 + 4 * q + 1 >= P.k) v[q].y = 0.f;
+        if (k0 + 4 * q + 2 >= P.k) v[q].z = 0.f;
+        if (k0 + 4 * q + 3 >= P.k) v[q].w = 0.f;
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.raw_empty[slot]);
+    if (lane == 0) mbar_arrive(&sm.raw_empty[r.idx]);
+    unsigned char* bst = sm.b_region + rb.idx * KS * 1024;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float4 hi = split_hi(v[j]);
-      const int off = tile_off + (j & 1) * 32;
-      *reinterpret_cast<float4*>(&sm.b_tiles[bs][0][j >> 1][off]) = hi;
-      *reinterpret_cast<float4*>(&sm.b_tiles[bs][1][j >> 1][off]) = split_lo(v[j], hi);
+    for (int q = 0; q < kQ; ++q) {
+      const float4 hi = split_hi(v[q]);
+      const int off = (q / 2) * 4096 + tile_off + (q % 2) * 128;
+      *reinterpret_cast<float4*>(bst + off) = hi;
+      *reinterpret_cast<float4*>(bst + kSteps * 4096 + off) = split_lo(v[q], hi);
     }
     // The tensor core reads these tiles through the async proxy.
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.b_full[bs]);
+    if (lane == 0) mbar_arrive(&sm.b_full[rb.idx]);
   }
 }
 
-// ---- A side (warps 0-3; thread = tile row = TMEM lane) ----------------------
-// Folds accumulation chunk c into the running sum (columns kColTotal..).
-__device__ bool fold_chunk(TcShared& sm, uint32_t tmem, uint32_t lane_base, int c) {
+// ---- fold warps (10-17): quadrant q = warp % 4, columns [col0, col0 + 64) ----
+// Adds accumulation chunk c into the running sum (columns kColTotal..).
+__device__ bool fold_chunk(TcShared& sm, uint32_t tmem, uint32_t lane_base, int col0, int c) {
   const int buf = c & 1;
   const bool w = mbar_wait(sm, &sm.chunk_full[buf], (c >> 1) & 1);
   if (!__all_sync(0xffffffffu, w)) return false;   // tcgen05.ld/st below are warp-collective
   tc_fence_after();
-  const uint32_t chunk = tmem + lane_base + uint32_t(buf * kBN);
-  const uint32_t total = tmem + lane_base + kColTotal;
+  const uint32_t chunk = tmem + lane_base + uint32_t(buf * kBN + col0);
+  const uint32_t total = tmem + lane_base + kColTotal + uint32_t(col0);
 #pragma unroll 1
-  for (int piece = 0; piece < kBN / 32; ++piece) {
+  for (int piece = 0; piece < 2; ++piece) {
     float v[32];
     tmem_ld32(chunk + piece * 32, v);
     if (c > 0) {
@@ -433,10 +464,10 @@ __device__ bool fold_chunk(TcShared& sm, uint32_t tmem, uint32_t lane_base, int 
 }
 
 __device__ void store_outputs(const LeafPlan& plan, const Prod& P, int m0, int n0, long long batch,
-                              uint32_t total, bool empty_sum) {
-  const int r = m0 + int(threadIdx.x);
+                              int row, int col0, uint32_t total, bool empty_sum) {
+  const int r = m0 + row;
 #pragma unroll 1
-  for (int piece = 0; piece < kBN / 32; ++piece) {
+  for (int piece = 0; piece < 2; ++piece) {
     float v[32];
     if (empty_sum) {
 #pragma unroll
@@ -452,7 +483,7 @@ __device__ void store_outputs(const LeafPlan& plan, const Prod& P, int m0, int n
       const float coef = T.coef;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const int col = n0 + piece * 32 + i;
+        const int col = n0 + col0 + piece * 32 + i;
         if (col >= P.n) break;
         float* q = base + (long long)col * T.ld;
         if (T.mode == kOutAtomic) atomicAdd(q, coef * v[i]);
@@ -463,25 +494,28 @@ __device__ void store_outputs(const LeafPlan& plan, const Prod& P, int m0, int n
   }
 }
 
+// ---- A side (warps 0-3; thread = tile row = TMEM lane) ----------------------
+template <int KS>
 __device__ void run_a_side(TcShared& sm, const unsigned char* raw, const LeafPlan& plan,
-                           const Prod& P, int m0, int n0, long long batch, uint32_t tmem, int nraw,
-                           int slot_bytes, int stages) {
+                           const Prod& P, uint32_t tmem, int nraw, int slot_bytes, int stages) {
+  constexpr int kNA = kColsA / (2 * KS);
+  constexpr int kTermFloats = KS / 16 * kBoxBytes / 4;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = threadIdx.x;
   const uint32_t lane_base = uint32_t(warp * 32) << 16;
   float coef[kMaxOperandTerms];
 #pragma unroll
   for (int t = 0; t < kMaxOperandTerms; ++t) coef[t] = t < P.nl ? plan.terms[P.l0 + t].coef : 0.f;
-  for (int s = 0; s < stages; ++s) {
-    const int slot = s % nraw, as = s % kASlots;
-    bool w = mbar_wait(sm, &sm.raw_full[slot], (s / nraw) & 1);
-    if (w && s >= kASlots) w = mbar_wait(sm, &sm.a_empty[as], ((s / kASlots) - 1) & 1);
+  Ring r, ra;
+  for (int s = 0; s < stages; ++s, r.next(nraw), ra.next(kNA)) {
+    bool w = mbar_wait(sm, &sm.raw_full[r.idx], r.phase);
+    if (w && s >= kNA) w = mbar_wait(sm, &sm.a_empty[ra.idx], ra.phase ^ 1u);
     if (!__all_sync(0xffffffffu, w)) return;   // tcgen05.st below is warp-collective
-    // Raw A tile: 16 k-rows of 128 m (512 B each); a warp reads 128 contiguous bytes.
-    const float* src = reinterpret_cast<const float*>(raw + slot * slot_bytes) + row;
-    float v[kKS];
+    // Raw A term: KS k-rows of 128 m (512 B each); a warp reads 128 contiguous bytes.
+    const float* src = reinterpret_cast<const float*>(raw + r.idx * slot_bytes) + row;
+    float v[KS];
 #pragma unroll
-    for (int k = 0; k < kKS; ++k) {
+    for (int k = 0; k < KS; ++k) {
       const float x = src[k * kBM];
       v[k] = coef[0] < 0.f ? -x : x;
     }
@@ -489,37 +523,48 @@ __device__ void run_a_side(TcShared& sm, const unsigned char* raw, const LeafPla
     for (int t = 1; t < kMaxOperandTerms; ++t) {
       if (t >= P.nl) break;
 #pragma unroll
-      for (int k = 0; k < kKS; ++k) v[k] = fmaf(coef[t], src[t * (kTermBytes / 4) + k * kBM], v[k]);
+      for (int k = 0; k < KS; ++k) v[k] = fmaf(coef[t], src[t * kTermFloats + k * kBM], v[k]);
     }
-    const int k0 = s * kKS;
-    if (k0 + kKS > P.k) {   // K tail: the box reaches past the block
+    const int k0 = s * KS;
+    if (k0 + KS > P.k) {   // K tail: the box reaches past the block
 #pragma unroll
-      for (int k = 0; k < kKS; ++k)
+      for (int k = 0; k < KS; ++k)
         if (k0 + k >= P.k) v[k] = 0.f;
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.raw_empty[slot]);
-    uint32_t hi[kKS], lo[kKS];
+    if (lane == 0) mbar_arrive(&sm.raw_empty[r.idx]);
+    const uint32_t a_col = tmem + lane_base + kColA + uint32_t(ra.idx * 2 * KS);
 #pragma unroll
-    for (int k = 0; k < kKS; ++k) {
-      const float h = tf32_rn(v[k]);
-      hi[k] = __float_as_uint(h);
-      lo[k] = __float_as_uint(tf32_rn(v[k] - h));
+    for (int h = 0; h < KS / 16; ++h) {
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float x = v[16 * h + k];
+        const float hv = tf32_rn(x);
+        hi[k] = __float_as_uint(hv);
+        lo[k] = __float_as_uint(tf32_rn(x - hv));
+      }
+      tmem_st16(a_col + 16 * h, hi);
+      tmem_st16(a_col + KS + 16 * h, lo);
     }
-    const uint32_t a_col = tmem + lane_base + kColA + uint32_t(as * 32);
-    tmem_st16(a_col, hi);
-    tmem_st16(a_col + 16, lo);
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.a_full[as]);
-    // Fold the chunk that ended with the previous stage while this one runs.
-    if (s > 0 && s % kChunkStages == 0 && !fold_chunk(sm, tmem, lane_base, s / kChunkStages - 1))
-      return;
+    if (lane == 0) mbar_arrive(&sm.a_full[ra.idx]);
   }
-  if (stages > 0 && !fold_chunk(sm, tmem, lane_base, (stages - 1) / kChunkStages)) return;
+}
+
+__device__ void run_fold(TcShared& sm, const LeafPlan& plan, const Prod& P, int m0, int n0,
+                         long long batch, uint32_t tmem) {
+  const int warp = threadIdx.x >> 5;
+  const int q = warp % 4, col0 = ((warp - kFoldWarp0) / 4) * 64;
+  const uint32_t lane_base = uint32_t(q * 32) << 16;
+  const int chunks = (P.k + kChunkK - 1) / kChunkK;
+  for (int c = 0; c < chunks; ++c)
+    if (!fold_chunk(sm, tmem, lane_base, col0, c)) return;
   if (*(volatile int*)&sm.abort) return;
-  store_outputs(plan, P, m0, n0, batch, tmem + lane_base + kColTotal, stages == 0);
+  store_outputs(plan, P, m0, n0, batch, q * 32 + (threadIdx.x & 31), col0,
+                tmem + lane_base + kColTotal + uint32_t(col0), chunks == 0);
 }
 
 }  // namespace
@@ -541,26 +586,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n0 = ((local % in_group) / gsize) * kBN;
   const int batch = blockIdx.y;
   const bool valid = P.nl >= 1 && P.nl <= kMaxOperandTerms && P.nr >= 1 && P.nr <= kMaxOperandTerms;
-  const int slot_bytes = (valid ? P.nl + P.nr : 1) * kTermBytes;
+  const int terms = valid ? P.nl + P.nr : 1;
+  const int ks = terms <= 4 ? 32 : 16;
+  const int slot_bytes = terms * ks * kBM * 4;
   const int nraw = min(kMaxRaw, kRawBytes / slot_bytes);
-  const int stages = (P.k + kKS - 1) / kKS;
+  const int stages = (P.k + ks - 1) / ks;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < nraw; ++i) {
       mbar_init(&sm.raw_full[i], 1);
       mbar_init(&sm.raw_empty[i], 8);   // the 8 transform warps
     }
-    for (int i = 0; i < kASlots; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&sm.a_full[i], 4);
       mbar_init(&sm.a_empty[i], 1);
-    }
-    for (int i = 0; i < kBStages; ++i) {
       mbar_init(&sm.b_full[i], 4);
       mbar_init(&sm.b_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.chunk_full[i], 1);
-      mbar_init(&sm.chunk_empty[i], 4);
+      mbar_init(&sm.chunk_empty[i], kFoldWarps);
     }
     mbar_init(&sm.mma_done, 1);
     sm.abort = 0;
@@ -582,15 +627,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (!valid) {
     if (threadIdx.x == 0) atomicOr(&g_tc_device_error, 2u);
   } else if (warp == kTmaWarp) {
-    if (lane == 0) run_producer(sm, raw, maps, P, m0, n0, batch, nraw, slot_bytes, stages);
+    if (lane == 0) run_producer(sm, raw, maps, P, m0, n0, batch, nraw, slot_bytes, stages, ks);
     __syncwarp();
   } else if (warp == kMmaWarp) {
-    if (lane == 0) run_mma(sm, tmem, stages);
+    if (lane == 0) {
+      if (ks == 32) run_mma<32>(sm, tmem, stages);
+      else run_mma<16>(sm, tmem, stages);
+    }
     __syncwarp();
+  } else if (warp >= kFoldWarp0) {
+    run_fold(sm, plan, P, m0, n0, batch, tmem);
   } else if (warp >= 4) {
-    run_b_side(sm, raw, plan, P, nraw, slot_bytes, stages);
+    if (ks == 32) run_b_side<32>(sm, raw, plan, P, nraw, slot_bytes, stages);
+    else run_b_side<16>(sm, raw, plan, P, nraw, slot_bytes, stages);
   } else {
-    run_a_side(sm, raw, plan, P, m0, n0, batch, tmem, nraw, slot_bytes, stages);
+    if (ks == 32) run_a_side<32>(sm, raw, plan, P, tmem, nraw, slot_bytes, stages);
+    else run_a_side<16>(sm, raw, plan, P, tmem, nraw, slot_bytes, stages);
   }
   tc_fence_before();
   __syncthreads();
