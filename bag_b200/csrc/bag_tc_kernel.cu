@@ -64,7 +64,7 @@ constexpr int kMaxRaw = 12;        // raw operand stages, upper bound
 constexpr int kTmaWarp = 8, kMmaWarp = 9, kFoldWarp0 = 10, kFoldWarps = 8;
 constexpr int kThreads = (kFoldWarp0 + kFoldWarps) * 32;   // 576
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColTotal = 256, kColA = 384, kColsA = 128;
+constexpr uint32_t kColA = 256, kColsA = 256;   // chunk accumulators in [0, 256)
 constexpr int kBRegion = 65536;    // shared-memory ring of B hi/lo stages
 constexpr int kBoxBytes = 128 * 16 * 4;   // one TMA box: 128 m x 16 k or 16 k x 128 n
 constexpr int kSmemBytes = 232448;        // 227 KB, the sm_100 per-CTA maximum
@@ -85,7 +85,7 @@ struct TcShared {
   // (n/8)*256 + (k/4)*128 + (n%8)*16 + (k%4)*4 of its tile.
   unsigned char b_region[kBRegion];
   unsigned long long raw_full[kMaxRaw], raw_empty[kMaxRaw];
-  unsigned long long a_full[4], a_empty[4];
+  unsigned long long a_full[8], a_empty[8];
   unsigned long long b_full[4], b_empty[4];
   unsigned long long chunk_full[2], chunk_empty[2];
   unsigned long long mma_done;
@@ -230,6 +230,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
       : "r"(taddr));
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
@@ -433,30 +446,22 @@ __device__ void run_b_side(TcShared& sm, const unsigned char* raw, const LeafPla
 }
 
 // ---- fold warps (10-17): quadrant q = warp % 4, columns [col0, col0 + 64) ----
-// Adds accumulation chunk c into the running sum (columns kColTotal..).
-__device__ bool fold_chunk(TcShared& sm, uint32_t tmem, uint32_t lane_base, int col0, int c) {
+// Adds accumulation chunk c into this thread's running sums (registers).
+__device__ bool fold_chunk(TcShared& sm, uint32_t tmem, uint32_t lane_base, int col0, int c,
+                           float (&total)[64]) {
   const int buf = c & 1;
   const bool w = mbar_wait(sm, &sm.chunk_full[buf], (c >> 1) & 1);
-  if (!__all_sync(0xffffffffu, w)) return false;   // tcgen05.ld/st below are warp-collective
+  if (!__all_sync(0xffffffffu, w)) return false;   // tcgen05.ld below is warp-collective
   tc_fence_after();
   const uint32_t chunk = tmem + lane_base + uint32_t(buf * kBN + col0);
-  const uint32_t total = tmem + lane_base + kColTotal + uint32_t(col0);
-#pragma unroll 1
-  for (int piece = 0; piece < 2; ++piece) {
-    float v[32];
-    tmem_ld32(chunk + piece * 32, v);
-    if (c > 0) {
-      float t[32];
-      tmem_ld32(total + piece * 32, t);
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(t[i], v[i]);
-    } else {
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-    }
-    tmem_st32(total + piece * 32, v);
+  for (int piece = 0; piece < 4; ++piece) {
+    float v[16];
+    tmem_ld16(chunk + 16 * piece, v);
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) total[16 * piece + i] = __fadd_rn(total[16 * piece + i], v[i]);
   }
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
   tc_fence_before();
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.chunk_empty[buf]);
@@ -464,32 +469,21 @@ __device__ bool fold_chunk(TcShared& sm, uint32_t tmem, uint32_t lane_base, int 
 }
 
 __device__ void store_outputs(const LeafPlan& plan, const Prod& P, int m0, int n0, long long batch,
-                              int row, int col0, uint32_t total, bool empty_sum) {
+                              int row, int col0, const float (&total)[64]) {
   const int r = m0 + row;
-#pragma unroll 1
-  for (int piece = 0; piece < 2; ++piece) {
-    float v[32];
-    if (empty_sum) {
+  if (r >= P.m) return;
+  for (int o = 0; o < P.no; ++o) {
+    const Term& T = plan.terms[P.o0 + o];
+    float* base = const_cast<float*>(T.p) + batch * T.bstride + r;
+    const float coef = T.coef;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = 0.f;
-    } else {
-      tmem_ld32(total + piece * 32, v);
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-    }
-    if (r >= P.m) continue;
-    for (int o = 0; o < P.no; ++o) {
-      const Term& T = plan.terms[P.o0 + o];
-      float* base = const_cast<float*>(T.p) + batch * T.bstride + r;
-      const float coef = T.coef;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int col = n0 + col0 + piece * 32 + i;
-        if (col >= P.n) break;
-        float* q = base + (long long)col * T.ld;
-        if (T.mode == kOutAtomic) atomicAdd(q, coef * v[i]);
-        else if (T.mode == kOutAdd) *q += coef * v[i];
-        else *q = coef * v[i];
-      }
+    for (int i = 0; i < 64; ++i) {
+      const int col = n0 + col0 + i;
+      if (col >= P.n) break;
+      float* q = base + (long long)col * T.ld;
+      if (T.mode == kOutAtomic) atomicAdd(q, coef * total[i]);
+      else if (T.mode == kOutAdd) *q += coef * total[i];
+      else *q = coef * total[i];
     }
   }
 }
@@ -560,16 +554,20 @@ __device__ void run_fold(TcShared& sm, const LeafPlan& plan, const Prod& P, int 
   const int q = warp % 4, col0 = ((warp - kFoldWarp0) / 4) * 64;
   const uint32_t lane_base = uint32_t(q * 32) << 16;
   const int chunks = (P.k + kChunkK - 1) / kChunkK;
+  float total[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) total[i] = 0.f;
   for (int c = 0; c < chunks; ++c)
-    if (!fold_chunk(sm, tmem, lane_base, col0, c)) return;
+    if (!fold_chunk(sm, tmem, lane_base, col0, c, total)) return;
   if (*(volatile int*)&sm.abort) return;
-  store_outputs(plan, P, m0, n0, batch, q * 32 + (threadIdx.x & 31), col0,
-                tmem + lane_base + kColTotal + uint32_t(col0), chunks == 0);
+  store_outputs(plan, P, m0, n0, batch, q * 32 + (threadIdx.x & 31), col0, total);
 }
 
 }  // namespace
 
-__global__ void __launch_bounds__(kThreads, 1)
+// 18 warps put 5 on one SM sub-partition (16K registers): at most 96 per
+// thread.  The fold warps hold 64 running sums each.
+__global__ void __maxnreg__(96)
     leaf_tc_kernel(const __grid_constant__ LeafPlan plan, const __grid_constant__ TcMaps maps) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   TcShared& sm = *reinterpret_cast<TcShared*>(smem_raw);
@@ -587,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int batch = blockIdx.y;
   const bool valid = P.nl >= 1 && P.nl <= kMaxOperandTerms && P.nr >= 1 && P.nr <= kMaxOperandTerms;
   const int terms = valid ? P.nl + P.nr : 1;
-  const int ks = terms <= 4 ? 32 : 16;
+  const int ks = 2 * terms * 32 * kBM * 4 <= kRawBytes ? 32 : 16;   // up to five terms
   const int slot_bytes = terms * ks * kBM * 4;
   const int nraw = min(kMaxRaw, kRawBytes / slot_bytes);
   const int stages = (P.k + ks - 1) / ks;
@@ -597,9 +595,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.raw_full[i], 1);
       mbar_init(&sm.raw_empty[i], 8);   // the 8 transform warps
     }
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 8; ++i) {
       mbar_init(&sm.a_full[i], 4);
       mbar_init(&sm.a_empty[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&sm.b_full[i], 4);
       mbar_init(&sm.b_empty[i], 1);
     }
