@@ -12,27 +12,28 @@
 // product's for K >= 1024.
 //
 // One CTA (576 threads, 227 KB shared memory, 1 per SM) computes a 128 x 128
-// output tile of one product; the K loop runs in stages of 16:
+// output tile of one product; the K loop runs in stages of 32 k (products of
+// up to five operand terms) or 16 k (more terms: their raw stages are larger):
 //  * warp 8, lane 0 (producer): TMA-loads the raw FP32 tile of every signed
-//    operand term of the stage (A term: 128 m x 16 k, M-contiguous; B term:
-//    16 k x 128 n with 64-byte swizzle) into a ring of raw stages whose depth
-//    is sized per product (11 stages for single-term operands, 3 for 3+3).
-//    Tensor maps come from the host: one per source matrix (A, B) addressed
-//    by block coordinates, one per workspace block.  Warp 8 also owns TMEM.
+//    operand term of the stage (A term: boxes of 128 m x 16 k, M-contiguous;
+//    B term: boxes of 16 k x 128 n with 64-byte swizzle) into a ring of raw
+//    stages whose depth is sized per product.  Tensor maps come from the host:
+//    one per source matrix (A, B) addressed by block coordinates, one per
+//    workspace block.  Warp 8 also owns TMEM.
 //  * warps 0-3 (A side; thread = tile row = TMEM lane): sum the A terms in the
 //    reference's order (x + delta*y, bag.cuh:69-73), zero the K tail, split
 //    hi/lo and store them into a TMEM A slot (tcgen05.st).
-//  * warps 10-17 (fold; two per TMEM lane quadrant, 64 columns each): add each
-//    finished accumulation chunk into the running sum, then add coef*sum into
-//    every target C block (red.global, coalesced along the column).
 //  * warps 4-7 (B side; thread = tile column): sum, split and store the B terms
 //    as K-major no-swizzle hi/lo tiles in a shared-memory ring.
-//  * warp 9, lane 0: per stage issues six tcgen05.mma.kind::tf32 with A from
-//    TMEM and B from shared memory (two K-steps x three products) into the
-//    chunk's TMEM accumulator; commits free the A slot, the B stage and, at the
-//    end of a chunk, publish it to the A side.
-// TMEM columns: [0, 256) two chunk accumulators, [256, 384) running sum,
-// [384, 480) three A slots of 16 hi + 16 lo columns.
+//  * warp 9, lane 0: per K-step of 8 issues three tcgen05.mma.kind::tf32 with A
+//    from TMEM and B from shared memory into the chunk's TMEM accumulator;
+//    commits free the A slot, the B stage and, at the end of a 32-k chunk,
+//    publish the chunk.
+//  * warps 10-17 (fold; two per TMEM lane quadrant, 64 columns each): add each
+//    finished chunk into 64 running sums held in registers, then add coef*sum
+//    into every target C block (red.global, coalesced along the column).
+// TMEM columns: [0, 256) two chunk accumulators, [256, 512) the A slots
+// (four of 32 k or eight of 16 k, hi then lo).
 //
 // All waits are bounded (kWaitLimitNs of wall time, then this file's device
 // error word is set and the CTA's abort flag raised); on a timeout every role

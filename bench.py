@@ -5,7 +5,10 @@ Workload: C = A @ B, FP32, M=N=K=16384, row-major, A then B
 drawn N(0,1) from ``numpy.random.default_rng(2)``, two BAG recursion levels
 (49 leaf products of 4096^3), Minimal basis.  A step is one
 ``C <- A@B + C`` call; inputs are 1 GiB each, larger than the 126 MB L2, so no
-flush is needed between steps.
+flush is needed between steps.  The leaf arithmetic is ``--math``: 3xTF32
+(default; tcgen05 tensor cores on hi/lo TF32 splits with FP32-folded chunks,
+checked in the same run to stay within 1.25x the FFMA path's error, the
+reference's numerics) or ffma (sequential FP32 fmaf chains, SIMT).
 
 On N GPUs (one process per GPU, torchrun) every rank owns the same row band
 of each of the 2^depth block-rows of A and C (a compact (M/N) x K shard whose
@@ -57,6 +60,7 @@ def parse_args():
     p.add_argument("--size", type=int, default=SIZE)
     p.add_argument("--depth", type=int, default=DEPTH)
     p.add_argument("--basis", default="minimal", choices=["minimal", "full", "classic"])
+    p.add_argument("--math", default="3xtf32", choices=["3xtf32", "ffma"])
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU time of the bounded CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -238,6 +242,7 @@ def run_bag(args) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     torch.backends.cuda.matmul.allow_tf32 = False
+    bag.set_math_mode(args.math)
 
     size, depth = args.size, args.depth
     if size % ((4 << depth) * world):
@@ -306,6 +311,7 @@ def run_bag(args) -> None:
         torch.cuda.synchronize()
     barrier()
     launches = reduce_sum(bag.launch_count() - launches0)
+    leaf_path = bag.last_leaf_path()
     ms = reduce_max(t_start.elapsed_time(t_end)) / args.steps
     leaf_ms = reduce_max(sum(s.elapsed_time(e) for s, e in pairs) / args.steps)
     flops_total = 2.0 * size * size * size
@@ -364,8 +370,31 @@ def run_bag(args) -> None:
     h2d = 4 * (size * size + size * size)
     d2h = 4 * size * size
 
-    # Comparator: cuBLAS SGEMM (torch, IEEE FP32, no TF32) on the same inputs.
+    # Comparators: cuBLAS SGEMM (torch, IEEE FP32, no TF32) and this library's
+    # FFMA path on the same inputs.
     comparators = {}
+    if rank == 0 and world == 1 and not args.no_comparators and leaf_path != "ffma":
+        bag.set_math_mode("ffma")
+        c_tmp = torch.zeros_like(c_dev)   # c_dev keeps the e2e result for the accuracy check
+
+        def ffma_step():
+            bag.sgemm(a_dev, b_dev, c_tmp, beta=1.0, depth=depth, basis=args.basis, workspace=ws)
+
+        for _ in range(2):
+            ffma_step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.steps):
+            ffma_step()
+        f1.record()
+        torch.cuda.synchronize()
+        del c_tmp
+        fms = f0.elapsed_time(f1) / args.steps
+        comparators["bag_ffma_path"] = {"tflops": flops_total / (fms * 1e-3) / 1e12,
+                                        "ms_per_step": fms,
+                                        "how": "same call, bag_set_math_mode(BAG_MATH_FFMA)"}
+        bag.set_math_mode(args.math)
     if rank == 0 and world == 1 and not args.no_comparators:
         a_full = a_dev
         c_cmp = torch.zeros((size, size), dtype=torch.float32, device=device)
@@ -384,49 +413,84 @@ def run_bag(args) -> None:
                                             "how": "torch addmm_, allow_tf32=False (cuBLAS FP32)"}
         del c_cmp
 
-    # Accuracy of this run's result: the last e2e step computed C = A@B once.
+    # Accuracy of this run's result (the last e2e step computed C = A@B once)
+    # and, for the tensor path, of the FFMA path -- the reference's numerics --
+    # on the same inputs at the same depth: the bound is <= 1.25x that and <= 1e-4.
     accuracy = {}
     if rank == 0 and world == 1:
         c = c_dev
+        c_ffma = None
+        if leaf_path != "ffma":
+            bag.set_math_mode("ffma")
+            c_ffma = torch.zeros_like(c_dev)
+            bag.sgemm(a_dev, b_dev, c_ffma, beta=0.0, depth=depth, basis=args.basis, workspace=ws)
+            bag.set_math_mode(args.math)
         # FP64 reference on the GPU (cuBLAS DGEMM), column panels to bound memory.
         panel = 2048
-        num = den = 0.0
+        num = num_f = den = 0.0
         a64 = a_dev.double()
         for j in range(0, size, panel):
             ref = a64 @ b_dev[:, j:j + panel].double()
             diff = c[:, j:j + panel].double() - ref
             num += float((diff * diff).sum())
             den += float((ref * ref).sum())
+            if c_ffma is not None:
+                diff = c_ffma[:, j:j + panel].double() - ref
+                num_f += float((diff * diff).sum())
         del a64
         accuracy = {"rel_frobenius_vs_fp64": (num / den) ** 0.5}
+        if c_ffma is not None:
+            ffma_err = (num_f / den) ** 0.5
+            accuracy.update({"ffma_path_rel_frobenius_vs_fp64": ffma_err,
+                             "ratio_to_ffma_path": accuracy["rel_frobenius_vs_fp64"] / ffma_err,
+                             "bound": "<= 1.25x the FFMA path (sequential fmaf leaves, the "
+                                      "reference CUDA numerics) and <= 1e-4",
+                             "within_bound": accuracy["rel_frobenius_vs_fp64"] <= min(
+                                 1.25 * ffma_err, 1e-4)})
+            del c_ffma
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(a_host.numpy(), b_np, depth, args.basis, args.cpu_seconds)
 
     if rank == 0:
-        traffic = read_traffic()
+        if leaf_path == "3xtf32":
+            peaks = measured_peaks()
+            tf32 = peaks.get("bf16_tflops", 1590.0) / 2.0
+            sustained = peaks.get("bf16_tflops_sustained", 1400.0) / 2.0
+            roofline = {"bound": "tensor", "kernel": "leaf_tc_kernel (3xTF32 tcgen05, A from TMEM)",
+                        "achieved": leaf_tflops, "peak": tf32 / 3.0, "unit": "TFLOP/s",
+                        "frac": leaf_tflops / (tf32 / 3.0),
+                        "traffic": read_traffic("leaf_tc_cfg3_traffic.txt"),
+                        "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst, of measured) / 2 "
+                                       "(dense TF32 = half the bf16 rate) / 3 (three MMAs per "
+                                       "leaf product: hi*hi, hi*lo, lo*hi)",
+                        "frac_of_sustained": leaf_tflops / (sustained / 3.0),
+                        "leaf_ms": leaf_ms, "algorithmic_flops_per_launch": f_exec}
+        else:
+            roofline = {"bound": "compute", "kernel": "leaf_gemm_kernel (FP32 FFMA SIMT)",
+                        "achieved": leaf_tflops, "peak": nominal, "unit": "TFLOP/s",
+                        "frac": leaf_tflops / nominal,
+                        "traffic": read_traffic("leaf_gemm_cfg3_traffic.txt"),
+                        "peak_source": f"nominal FP32 FFMA {sms} SM x 128 lanes x 2 x "
+                                       f"{max_mhz:.0f} MHz (MEASURED_PEAKS.json has no FP32 "
+                                       f"SIMT figure)",
+                        "ffma_probe_tflops": probe, "frac_of_probe": leaf_tflops / probe,
+                        "leaf_ms": leaf_ms, "algorithmic_flops_per_launch": f_exec}
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "M": size, "N": size, "K": size, "depth": depth,
-                       "basis": args.basis, "layout": "row-major",
+                       "basis": args.basis, "layout": "row-major", "leaf_math": leaf_path,
                        "l2": "inputs larger than L2 (1 GiB each); no flush",
                        "parallelism": f"row-band shards x{world}, B replicated" if world > 1
                        else "single GPU"},
             "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "roofline": {"bound": "compute", "kernel": "leaf_gemm_kernel (FP32 FFMA SIMT)",
-                         "achieved": leaf_tflops, "peak": nominal, "unit": "TFLOP/s",
-                         "frac": leaf_tflops / nominal, "traffic": traffic,
-                         "peak_source": f"nominal FP32 FFMA {sms} SM x 128 lanes x 2 x "
-                                        f"{max_mhz:.0f} MHz (MEASURED_PEAKS.json has no FP32 "
-                                        f"SIMT figure)",
-                         "ffma_probe_tflops": probe, "frac_of_probe": leaf_tflops / probe,
-                         "leaf_ms": leaf_ms,
-                         "algorithmic_flops_per_launch": f_exec},
+            "roofline": roofline,
+            "ffma_probe_tflops": probe,
             "clocks": {k: csum[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
             "gpu_launches": int(launches),
             "executed_tflops": f_exec * world / (ms * 1e-3) / 1e12,
@@ -444,9 +508,17 @@ def run_bag(args) -> None:
         dist.destroy_process_group()
 
 
-def read_traffic():
+def measured_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def read_traffic(name: str):
     """DRAM bytes per leaf launch from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "leaf_gemm_cfg3_traffic.txt")
+    path = os.path.join(ROOT, "profiles", name)
     try:
         with open(path) as f:
             for line in f:
