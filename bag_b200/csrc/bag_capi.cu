@@ -246,6 +246,17 @@ struct Builder {
     return out;
   }
 
+  // Round every multi-term leaf operand into the workspace, so each leaf
+  // product reads one block per operand (the tensor-core path's option: there
+  // the fused multi-term prologue, not the tensor core, bounds a product,
+  // while one pass over the operand blocks runs at HBM speed).
+  void materialize_leaf_operands() {
+    for (HostLeaf& l : leaves) {
+      if (l.left.size() > 1) l.left = {{materialize(l.left, l.m, l.k), 1.f}};
+      if (l.right.size() > 1) l.right = {{materialize(l.right, l.k, l.n), 1.f}};
+    }
+  }
+
   // Reduce an operand to a single unit-coefficient block.  A lone negated
   // block keeps its data; the sign moves to the outputs (exact).
   View single(const Expr& e, int rows, int cols, float* sign) {
@@ -326,8 +337,10 @@ struct GemmDesc {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// Build the plan; ws may be a fake base when only sizes are wanted.
-void build_plan(const GemmDesc& g, float* ws, long long ws_bstride, Builder& B) {
+// Build the plan; ws may be a fake base when only sizes are wanted.  With
+// `leaf_operands` every multi-term leaf operand is materialised as well.
+void build_plan(const GemmDesc& g, float* ws, long long ws_bstride, Builder& B,
+                bool leaf_operands = false) {
   B.basis = g.basis;
   B.ws = ws;
   B.ws_bstride = ws_bstride;
@@ -342,6 +355,7 @@ void build_plan(const GemmDesc& g, float* ws, long long ws_bstride, Builder& B) 
     return;
   }
   B.expand({{A, 1.f}}, {{Bv, 1.f}}, {{C, 1.f, kOutAtomic}}, mc, kc, nc, depth);
+  if (leaf_operands) B.materialize_leaf_operands();
   if (kc < g.k)
     B.leaves.push_back({mc, nc, g.k - kc, {{{A.p + (long long)kc * A.ld, A.ld, A.bstride}, 1.f}},
                         {{{Bv.p + kc, Bv.ld, Bv.bstride}, 1.f}}, {{C, 1.f, kOutAtomic}}});
@@ -355,13 +369,31 @@ void build_plan(const GemmDesc& g, float* ws, long long ws_bstride, Builder& B) 
 }
 
 // Workspace elements per batch entry (dry run with a fake base).
-size_t plan_workspace_elements(GemmDesc g) {
+size_t plan_workspace_elements(GemmDesc g, bool leaf_operands = false) {
+  static float fake;
+  Builder B;
+  g.a = g.b = &fake;
+  g.c = &fake;
+  build_plan(g, reinterpret_cast<float*>(uintptr_t(1) << 44), 0, B, leaf_operands);
+  return B.ws_used;
+}
+
+// Whether this thread's math mode materialises multi-term leaf operands for
+// `g`: the 3xTF32 mode, every leaf long enough for the tensor path, and some
+// leaf with a multi-term operand.
+bool leaf_materialisation_wanted(GemmDesc g) {
+  if (g_math_mode != BAG_MATH_3XTF32 || g.depth == 0) return false;
   static float fake;
   Builder B;
   g.a = g.b = &fake;
   g.c = &fake;
   build_plan(g, reinterpret_cast<float*>(uintptr_t(1) << 44), 0, B);
-  return B.ws_used;
+  bool multi = false;
+  for (const HostLeaf& l : B.leaves) {
+    if (l.k < kTcMinK) return false;
+    multi = multi || l.left.size() > 1 || l.right.size() > 1;
+  }
+  return multi;
 }
 
 // Tile configuration: the env var BAG_B200_TILE (a kTile* id) pins one for
@@ -545,7 +577,14 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
                  "cudaMemset2DAsync");
   }
   if (g.k == 0) return;
-  const size_t need = plan_workspace_elements(g);
+  // 3xTF32 mode materialises multi-term leaf operands when the workspace was
+  // sized for it (created in that mode); otherwise the prologue stays fused.
+  bool leaf_operands = leaf_materialisation_wanted(g);
+  size_t need = plan_workspace_elements(g, leaf_operands);
+  if (leaf_operands && (!ws || need * size_t(g.batch) > ws->elements)) {
+    leaf_operands = false;
+    need = plan_workspace_elements(g);
+  }
   float* base = nullptr;
   if (need) {
     if (!ws) fail(BAG_ERR_WORKSPACE, "this plan needs a workspace");
@@ -555,7 +594,8 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
     base = ws->data;
   }
   Builder B;
-  build_plan(g, base ? base : reinterpret_cast<float*>(uintptr_t(1) << 44), (long long)need, B);
+  build_plan(g, base ? base : reinterpret_cast<float*>(uintptr_t(1) << 44), (long long)need, B,
+             leaf_operands);
   if (B.ws_used != need) fail(BAG_ERR_INTERNAL, "plan size changed between passes");
   const std::vector<TcSource> sources = {{g.a, g.lda, g.sa, g.m, g.k}, {g.b, g.ldb, g.sb, g.k, g.n}};
   execute_plan(B, g.batch, stream, sources);
@@ -713,7 +753,9 @@ bag_status bag_workspace_create_ex(int m, int n, int k, int depth, int basis, in
     if (basis != kMinimal && basis != kFull && basis != kClassic) fail(BAG_ERR_INVALID, "unknown basis");
     GemmDesc g{m, n, k, nullptr, std::max(1, m), 0, nullptr, std::max(1, k), 0, nullptr,
                std::max(1, m), 0, std::max(batch, 1), depth, basis};
-    const size_t per = plan_workspace_elements(g);
+    // Sized for the calling thread's math mode (3xTF32 adds the materialised
+    // multi-term leaf operands).
+    const size_t per = plan_workspace_elements(g, leaf_materialisation_wanted(g));
     const size_t total = per * size_t(std::max(batch, 1));
     auto* ws = new bag_workspace{m, n, k, depth, basis, batch, 0, nullptr, total};
     cudaError_t e = cudaGetDevice(&ws->device);
