@@ -15,8 +15,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libbag_b200.so")
-SOURCES = ["bag_kernels.cu", "bag_ws_kernel.cu", "bag_tc_kernel.cu", "bag_capi.cu",
-           "bag_noalloc.cu"]
+SOURCES = ["bag_kernels.cu", "bag_ws_kernel.cu", "bag_tc_kernel.cu", "bag_tc3_kernel.cu",
+           "bag_capi.cu", "bag_noalloc.cu"]
 HEADERS = ["bag_kernels.h", "bag_plan.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",

@@ -103,6 +103,7 @@ struct HostLeaf {
   int m, n, k;
   Expr left, right;
   std::vector<Target> out;
+  int prep_l = -1, prep_r = -1;   // prepared operands (Builder::prep), -1: none
 };
 
 struct HostJob {
@@ -246,15 +247,45 @@ struct Builder {
     return out;
   }
 
-  // Round every multi-term leaf operand into the workspace, so each leaf
-  // product reads one block per operand (the tensor-core path's option: there
-  // the fused multi-term prologue, not the tensor core, bounds a product,
-  // while one pass over the operand blocks runs at HBM speed).
-  void materialize_leaf_operands() {
-    for (HostLeaf& l : leaves) {
-      if (l.left.size() > 1) l.left = {{materialize(l.left, l.m, l.k), 1.f}};
-      if (l.right.size() > 1) l.right = {{materialize(l.right, l.k, l.n), 1.f}};
+  // Prepared operands (3xTF32 path): every distinct leaf operand is written
+  // once, as TF32 hi and lo rows of the prepared region (rows of
+  // prep_row_len k values), by one HBM-speed pass; the leaf products then
+  // only load and multiply.  With the tensor core the fused transform and
+  // split, not the tensor core, bound a product.
+  struct PrepOp {
+    Expr terms;
+    int rows, cols;
+    bool transpose;   // left operands: column-major rows x cols -> k-contiguous rows
+    int hi_row;       // lo rows follow at hi_row + rows
+  };
+  std::vector<PrepOp> prep;
+  int prep_rows = 0, prep_row_len = 0;
+  View prep_region{nullptr, 0, 0};
+
+  int prep_index(const Expr& e, int rows, int cols, bool transpose) {
+    for (size_t i = 0; i < prep.size(); ++i) {
+      const PrepOp& o = prep[i];
+      if (o.rows != rows || o.cols != cols || o.transpose != transpose || o.terms.size() != e.size())
+        continue;
+      bool same = true;
+      for (size_t t = 0; t < e.size() && same; ++t)
+        same = o.terms[t].v == e[t].v && o.terms[t].coef == e[t].coef;
+      if (same) return int(i);
     }
+    prep.push_back({e, rows, cols, transpose, prep_rows});
+    prep_rows += 2 * rows;
+    return int(prep.size()) - 1;
+  }
+
+  void prepare_leaf_operands(int row_align) {
+    int kmax = 0;
+    for (const HostLeaf& l : leaves) kmax = std::max(kmax, l.k);
+    prep_row_len = std::max(row_align, (kmax + row_align - 1) / row_align * row_align);
+    for (HostLeaf& l : leaves) {
+      l.prep_l = prep_index(l.left, l.m, l.k, true);
+      l.prep_r = prep_index(l.right, l.n, l.k, false);
+    }
+    prep_region = alloc(prep_row_len, std::max(prep_rows, 1), int(stages.size()) + 1);
   }
 
   // Reduce an operand to a single unit-coefficient block.  A lone negated
@@ -338,7 +369,8 @@ struct GemmDesc {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Build the plan; ws may be a fake base when only sizes are wanted.  With
-// `leaf_operands` every multi-term leaf operand is materialised as well.
+// `leaf_operands` every leaf operand is also given a prepared (TF32 hi/lo)
+// copy in the workspace.
 void build_plan(const GemmDesc& g, float* ws, long long ws_bstride, Builder& B,
                 bool leaf_operands = false) {
   B.basis = g.basis;
@@ -355,7 +387,7 @@ void build_plan(const GemmDesc& g, float* ws, long long ws_bstride, Builder& B,
     return;
   }
   B.expand({{A, 1.f}}, {{Bv, 1.f}}, {{C, 1.f, kOutAtomic}}, mc, kc, nc, depth);
-  if (leaf_operands) B.materialize_leaf_operands();
+  if (leaf_operands) B.prepare_leaf_operands(prep_row_align());
   if (kc < g.k)
     B.leaves.push_back({mc, nc, g.k - kc, {{{A.p + (long long)kc * A.ld, A.ld, A.bstride}, 1.f}},
                         {{{Bv.p + kc, Bv.ld, Bv.bstride}, 1.f}}, {{C, 1.f, kOutAtomic}}});
@@ -378,22 +410,19 @@ size_t plan_workspace_elements(GemmDesc g, bool leaf_operands = false) {
   return B.ws_used;
 }
 
-// Whether this thread's math mode materialises multi-term leaf operands for
-// `g`: the 3xTF32 mode, every leaf long enough for the tensor path, and some
-// leaf with a multi-term operand.
+// Whether this thread's math mode wants prepared leaf operands for `g`: the
+// 3xTF32 mode and every leaf long enough for the tensor path.
 bool leaf_materialisation_wanted(GemmDesc g) {
-  if (g_math_mode != BAG_MATH_3XTF32 || g.depth == 0) return false;
+  if (g_math_mode != BAG_MATH_3XTF32) return false;
   static float fake;
   Builder B;
   g.a = g.b = &fake;
   g.c = &fake;
   build_plan(g, reinterpret_cast<float*>(uintptr_t(1) << 44), 0, B);
-  bool multi = false;
-  for (const HostLeaf& l : B.leaves) {
+  if (B.leaves.empty()) return false;
+  for (const HostLeaf& l : B.leaves)
     if (l.k < kTcMinK) return false;
-    multi = multi || l.left.size() > 1 || l.right.size() > 1;
-  }
-  return multi;
+  return true;
 }
 
 // Tile configuration: the env var BAG_B200_TILE (a kTile* id) pins one for
@@ -458,6 +487,82 @@ Term make_term(const View& v, float coef, int mode) {
 
 bool view_vec_ok(const View& v) { return aligned16(v.p) && v.ld % 4 == 0 && v.bstride % 4 == 0; }
 
+// 3xTF32 leaf products on prepared operands: the prepare pass, then the leaf
+// launches (CTA tile 128 x kPrepBN).
+constexpr int kPrepBN = 256;
+
+void run_prepared(Builder& B, int batch, cudaStream_t stream) {
+  const int tile = prep_row_align();
+  for (size_t j0 = 0; j0 < B.prep.size(); j0 += kMaxPrepJobs) {
+    PrepPlan pp{};
+    pp.row_len = B.prep_row_len;
+    pp.region = const_cast<float*>(B.prep_region.p);
+    pp.region_bstride = B.ws_bstride;
+    long long tiles = 0;
+    for (size_t j = j0; j < std::min(B.prep.size(), j0 + kMaxPrepJobs); ++j) {
+      const Builder::PrepOp& o = B.prep[j];
+      PrepJob& J = pp.job[pp.njobs++];
+      J.rows = o.rows;
+      J.cols = o.cols;
+      J.nterms = int(o.terms.size());
+      J.transpose = o.transpose ? 1 : 0;
+      if (J.nterms < 1 || J.nterms > kMaxOperandTerms)
+        fail(BAG_ERR_INTERNAL, "prepared operand has an unsupported term count");
+      for (int t = 0; t < J.nterms; ++t) J.in[t] = make_term(o.terms[t].v, o.terms[t].coef, 0);
+      J.out_hi = o.hi_row;
+      J.out_lo = o.hi_row + o.rows;
+      J.tile_begin = tiles;
+      tiles += (long long)((o.rows + tile - 1) / tile) * (B.prep_row_len / tile);
+    }
+    pp.ntiles = tiles;
+    if (tiles > INT32_MAX) fail(BAG_ERR_SHAPE, "problem too large");
+    cuda_check(launch_prep(pp, batch, stream), "prepare launch");
+    ++g_launches;
+  }
+  if (g_prof_start) cuda_check(cudaEventRecord(g_prof_start, stream), "cudaEventRecord");
+  const TileShape ts = prep_tile_shape(kPrepBN);
+  size_t i = 0;
+  while (i < B.leaves.size()) {
+    PrepLeafPlan lp;
+    lp.nprod = 0;
+    lp.ntiles = 0;
+    int nouts = 0;
+    while (i < B.leaves.size() && lp.nprod < kMaxProducts) {
+      const HostLeaf& l = B.leaves[i];
+      if (nouts + int(l.out.size()) > kMaxTerms) break;
+      PrepProd& P = lp.prod[lp.nprod];
+      P.m = l.m;
+      P.n = l.n;
+      P.k = l.k;
+      P.tiles_m = (l.m + ts.bm - 1) / ts.bm;
+      P.tiles_n = (l.n + ts.bn - 1) / ts.bn;
+      P.tile_begin = lp.ntiles;
+      const Builder::PrepOp& L = B.prep[l.prep_l];
+      const Builder::PrepOp& R = B.prep[l.prep_r];
+      P.a_hi = L.hi_row;
+      P.a_lo = L.hi_row + L.rows;
+      P.b_hi = R.hi_row;
+      P.b_lo = R.hi_row + R.rows;
+      P.o0 = short(nouts);
+      P.no = short(l.out.size());
+      for (const Target& t : l.out) lp.outs[nouts++] = make_term(t.v, t.coef, t.mode);
+      const long long tiles = (long long)P.tiles_m * P.tiles_n;
+      if (tiles > 0) {
+        if ((long long)lp.ntiles + tiles > INT32_MAX) fail(BAG_ERR_SHAPE, "problem too large");
+        lp.ntiles += int(tiles);
+        ++lp.nprod;
+      }
+      ++i;
+    }
+    if (lp.nprod == 0 && i < B.leaves.size()) fail(BAG_ERR_INTERNAL, "plan chunking failed");
+    cuda_check(launch_leaf_prep(lp, kPrepBN, B.prep_region.p, B.prep_row_len, B.prep_rows,
+                                B.ws_bstride, batch, stream),
+               "prepared leaf launch");
+    if (lp.nprod) ++g_launches;
+  }
+  if (g_prof_end) cuda_check(cudaEventRecord(g_prof_end, stream), "cudaEventRecord");
+}
+
 // `sources` lists the whole operand matrices (A, B) the tensor-core path may
 // address blocks of through one tensor map each; may be empty.
 void execute_plan(Builder& B, int batch, cudaStream_t stream,
@@ -489,7 +594,6 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream,
       ++g_launches;
     }
   }
-  if (g_prof_start) cuda_check(cudaEventRecord(g_prof_start, stream), "cudaEventRecord");
   // Leaf products, grouped into as few launches as the parameter block allows.
   bool vec = true;
   for (const HostLeaf& l : B.leaves) {
@@ -505,6 +609,11 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream,
   for (const HostLeaf& l : B.leaves)
     tensor = tensor && l.k >= kTcMinK && tc_supported(int(l.left.size()), int(l.right.size()));
   g_last_leaf_path = tensor ? BAG_MATH_3XTF32 : BAG_MATH_FFMA;
+  if (tensor && !B.prep.empty() && prep_supported()) {
+    run_prepared(B, batch, stream);
+    return;
+  }
+  if (g_prof_start) cuda_check(cudaEventRecord(g_prof_start, stream), "cudaEventRecord");
   const int cfg = tensor ? -1 : choose_tile(B.leaves, sms, vec);
   const TileShape ts = tensor ? tc_tile_shape() : leaf_tile_shape(cfg);
   size_t i = 0;
@@ -577,8 +686,8 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
                  "cudaMemset2DAsync");
   }
   if (g.k == 0) return;
-  // 3xTF32 mode materialises multi-term leaf operands when the workspace was
-  // sized for it (created in that mode); otherwise the prologue stays fused.
+  // 3xTF32 mode prepares the leaf operands when the workspace was sized for
+  // it (created in that mode); otherwise the prologue stays fused.
   bool leaf_operands = leaf_materialisation_wanted(g);
   size_t need = plan_workspace_elements(g, leaf_operands);
   if (leaf_operands && (!ws || need * size_t(g.batch) > ws->elements)) {
@@ -753,8 +862,8 @@ bag_status bag_workspace_create_ex(int m, int n, int k, int depth, int basis, in
     if (basis != kMinimal && basis != kFull && basis != kClassic) fail(BAG_ERR_INVALID, "unknown basis");
     GemmDesc g{m, n, k, nullptr, std::max(1, m), 0, nullptr, std::max(1, k), 0, nullptr,
                std::max(1, m), 0, std::max(batch, 1), depth, basis};
-    // Sized for the calling thread's math mode (3xTF32 adds the materialised
-    // multi-term leaf operands).
+    // Sized for the calling thread's math mode (3xTF32 adds the prepared
+    // leaf operands).
     const size_t per = plan_workspace_elements(g, leaf_materialisation_wanted(g));
     const size_t total = per * size_t(std::max(batch, 1));
     auto* ws = new bag_workspace{m, n, k, depth, basis, batch, 0, nullptr, total};
@@ -1013,10 +1122,11 @@ int bag_last_leaf_path(void) { return g_last_leaf_path; }
 bag_status bag_device_error(unsigned* code) {
   return guarded([&] {
     if (!code) fail(BAG_ERR_INVALID, "null output pointer");
-    unsigned tc = 0;
+    unsigned tc = 0, tc3 = 0;
+    cuda_check(read_and_clear_tc3_device_error(&tc3), "reading the device error word");
     cuda_check(read_and_clear_device_error(code), "reading the device error word");
     cuda_check(read_and_clear_tc_device_error(&tc), "reading the device error word");
-    *code |= tc;
+    *code |= tc | tc3;
   });
 }
 

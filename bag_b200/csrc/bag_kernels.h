@@ -58,6 +58,19 @@ cudaError_t launch_leaf_tc(const LeafPlan& plan, const TcSource* sources, int ns
                            cudaStream_t stream);
 cudaError_t read_and_clear_tc_device_error(unsigned* value);
 
+// Prepared-operand 3xTF32 path (bag_tc3_kernel.cu): prep_kernel writes each
+// leaf operand's TF32 hi/lo rows into a workspace region (rows of row_len k,
+// row_len a multiple of prep_row_align()); leaf_prep_kernel runs the products
+// on them with 128 x bn tiles (bn 128 or 256).
+bool prep_supported();
+int prep_row_align();
+TileShape prep_tile_shape(int bn);
+cudaError_t launch_prep(const PrepPlan& plan, int batch, cudaStream_t stream);
+cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int bn, const float* region,
+                             long long row_len, long long rows, long long region_bstride,
+                             int batch, cudaStream_t stream);
+cudaError_t read_and_clear_tc3_device_error(unsigned* value);
+
 // Reads and clears the device error word that bounded waits set on timeout.
 cudaError_t read_and_clear_device_error(unsigned* value);
 

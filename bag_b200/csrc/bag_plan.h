@@ -86,7 +86,50 @@ struct MatPlan {
   MatJob job[kMaxJobs];
 };
 
+// Prepared-operand jobs (3xTF32 path): each writes one leaf operand -- the
+// signed sum of its terms, in the fused prologue's order -- as TF32 hi and lo
+// rows of `cols` k values (k contiguous, zero-padded to the region's row
+// length) at rows [out_hi, out_hi + rows) and [out_lo, out_lo + rows) of the
+// prepared region.  A left operand (column-major rows x cols, rows contiguous)
+// is transposed on the way; a right operand (column-major cols x rows, k
+// contiguous) keeps its orientation.
+constexpr int kMaxPrepJobs = 32;
+
+struct PrepJob {
+  int rows, cols;
+  int nterms, transpose;
+  Term in[kMaxOperandTerms];   // coef: +1 / -1
+  int out_hi, out_lo;          // region rows
+  long long tile_begin;        // first work item of this job
+};
+
+struct PrepPlan {
+  int njobs;
+  int row_len;                 // floats per region row (k, padded to the stage length)
+  float* region;
+  long long region_bstride;    // floats between batch entries' regions
+  long long ntiles;
+  PrepJob job[kMaxPrepJobs];
+};
+
+// Leaf products on prepared operands: A rows a_hi.., B rows b_hi.. of the
+// region; outputs as in LeafPlan.
+struct PrepProd {
+  int m, n, k;
+  int tiles_m, tiles_n, tile_begin;
+  int a_hi, a_lo, b_hi, b_lo;
+  short o0, no;
+};
+
+struct PrepLeafPlan {
+  int nprod;
+  int ntiles;
+  PrepProd prod[kMaxProducts];
+  Term outs[kMaxTerms];
+};
+
 static_assert(sizeof(LeafPlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(MatPlan) < 32000, "kernel parameter limit");
+static_assert(sizeof(PrepPlan) < 32000, "kernel parameter limit");
 
 }  // namespace bag_b200

@@ -1,0 +1,574 @@
+// Prepared-operand 3xTF32 path of the BAG FP32 matmul (sm_100a).
+//
+// prep_kernel: one HBM-speed pass writes every distinct leaf operand of the
+//   plan -- the signed sum of its blocks, in the fused prologue's order
+//   (x + delta*y, bag.cuh:69-73) -- as TF32 hi = rn_tf32(x) and
+//   lo = rn_tf32(x - hi) rows of a workspace region, k contiguous (left
+//   operands are transposed on the way through a shared-memory tile) and
+//   zero-padded to the region's row length (a multiple of the 64-k tile).
+//
+// leaf_prep_kernel<BN>: one CTA computes a 128 x BN output tile of one leaf
+//   product straight from the region:
+//  * warp 0, lane 0: per 32-k stage four TMA loads (A hi, A lo: 128 rows x
+//    32 k; B hi, B lo: BN rows x 32 k; 128-byte swizzle, K-major) into a ring
+//    of stages; warp 0 also owns TMEM.
+//  * warp 1, lane 0: per stage four K-steps of three tcgen05.mma.kind::tf32
+//    (A_hi*B_hi + A_hi*B_lo + A_lo*B_hi, both operands by shared-memory
+//    descriptor) into one TMEM chunk accumulator -- a stage is one 32-long
+//    accumulation chunk, since the tensor core accumulates with
+//    round-toward-zero (Ootomo & Yokota 2022, sec. 4) -- then commits the
+//    stage free and the chunk done.
+//  * warps 2.. (fold; BN/64 per TMEM lane quadrant, 64 columns each): add each
+//    finished chunk into 64 FP32 running sums in registers (round-to-nearest),
+//    then add coef*sum into every target C block (red.global, coalesced along
+//    the column).
+// TMEM: 512 / BN chunk accumulators of BN columns.
+//
+// All mbarrier waits are bounded (kWaitLimitNs of wall time; then this file's
+// device error word is set and the CTA's abort flag raised); every role then
+// skips the rest of its work, the producer drains its copies in flight and
+// the MMA thread its MMAs (bounded) before TMEM is freed.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "bag_kernels.h"
+
+namespace bag_b200 {
+
+// This file's device error word (read by read_and_clear_tc3_device_error).
+__device__ unsigned int g_tc3_device_error = 0;
+
+namespace {
+
+constexpr int kStageK = 32;
+constexpr unsigned kSuspendNs = 1000000;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+constexpr int kPrepTile = 64;   // prepare tile: 64 rows x 64 k, 256 threads
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = BN == 128 ? 3 : 2;
+  static constexpr int kABytes = 128 * kStageK * 4;   // one 128-row plane tile (16 KB)
+  static constexpr int kBBytes = BN * kStageK * 4;
+  static constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
+  static constexpr int kChunkBufs = 512 / BN;
+  static constexpr int kFoldWarps = 4 * (BN / 64);
+  static constexpr int kThreads = (2 + kFoldWarps) * 32;
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kSmemBytes = kBarOffset + 1024;
+  // Instruction descriptor: F32 accumulate, TF32 A and B, both K-major,
+  // N = BN, M = 128 (c_format[4,6)=1, a_format[7,10)=2, b_format[10,13)=2,
+  // n_dim[17,23)=N/8, m_dim[24,29)=M/16).
+  static constexpr uint32_t kIdesc =
+      (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+};
+
+struct alignas(64) PrepMaps {
+  CUtensorMap a;   // box 32 k x 128 rows
+  CUtensorMap b;   // box 32 k x BN rows
+};
+
+struct Bars {
+  unsigned long long full[4], empty[4];
+  unsigned long long chunk_full[4], chunk_empty[4];
+  unsigned long long mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, int bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait; on timeout (or when another role gave up) sets the error word
+// and the CTA's abort flag and returns false.
+__device__ __forceinline__ bool mbar_wait(Bars& sb, unsigned long long* bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - start > kWaitLimitNs || *(volatile int*)&sb.abort) {
+      atomicOr(&g_tc3_device_error, 1u);
+      *(volatile int*)&sb.abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// Bounded wait that ignores the abort flag (copies and MMAs already in flight).
+__device__ __forceinline__ void mbar_drain(unsigned long long* bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity)) return;
+  const unsigned long long start = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - start > kWaitLimitNs) {
+      atomicOr(&g_tc3_device_error, 1u);
+      return;
+    }
+  }
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// K-major, 128-byte-swizzled operand tile (rows of 32 k = 128 B, 8-row atoms of
+// 1024 B): start address in 16-byte units, LBO 16 B (unused for this layout),
+// SBO 1024 B, version 1 (bit 46), layout SWIZZLE_128B (2 at bits 61-63).  A
+// K-step of 8 TF32 advances the start address by 32 B inside the swizzle row.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+template <int BN>
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       bool accumulate) {
+  const uint32_t acc = accumulate ? 1u : 0u;
+  const uint32_t zero = 0u;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+      :
+      : "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(Cfg<BN>::kIdesc), "r"(acc), "r"(zero)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(unsigned long long* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float tf32_rn(float x) {
+  uint32_t u;
+  asm("cvt.rn.tf32.f32 %0, %1;" : "=r"(u) : "f"(x));
+  return __uint_as_float(u);
+}
+
+struct Ring {
+  int idx = 0;
+  unsigned phase = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++idx == n) {
+      idx = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// Signed sum of a job's terms at element (r, k) of the operand, in the fused
+// prologue's order: the first term with its sign, then fmaf(coef, x, acc).
+__device__ __forceinline__ float operand_sum(const PrepJob& J, long long batch, long long off_r,
+                                             long long k) {
+  const Term& T0 = J.in[0];
+  const float x0 = T0.p[batch * T0.bstride + off_r + k * T0.ld];
+  float v = T0.coef < 0.f ? -x0 : x0;
+  for (int t = 1; t < J.nterms; ++t) {
+    const Term& T = J.in[t];
+    v = fmaf(T.coef, T.p[batch * T.bstride + off_r + k * T.ld], v);
+  }
+  return v;
+}
+
+}  // namespace
+
+// ---- prepare pass ---------------------------------------------------------
+// One CTA (256 threads) writes a 64-row x 64-k tile of one prepared operand;
+// thread t covers rows t/16 + 16i (i < 4) and k values 4(t%16) .. +3.
+__device__ __forceinline__ float4 load4(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+
+// Signed sum of the job's terms over the 4 consecutive elements starting at
+// element a + b*ld of each term (its own ld; all 16-byte aligned).
+__device__ __forceinline__ float4 sum4(const PrepJob& J, long long batch, long long a, long long b) {
+  const Term& T0 = J.in[0];
+  float4 v = load4(T0.p + batch * T0.bstride + a + b * T0.ld);
+  if (T0.coef < 0.f) v = make_float4(-v.x, -v.y, -v.z, -v.w);
+  for (int t = 1; t < J.nterms; ++t) {
+    const Term& T = J.in[t];
+    const float4 x = load4(T.p + batch * T.bstride + a + b * T.ld);
+    v = make_float4(fmaf(T.coef, x.x, v.x), fmaf(T.coef, x.y, v.y), fmaf(T.coef, x.z, v.z),
+                    fmaf(T.coef, x.w, v.w));
+  }
+  return v;
+}
+
+__device__ __forceinline__ float4 hi4(float4 v) {
+  return make_float4(tf32_rn(v.x), tf32_rn(v.y), tf32_rn(v.z), tf32_rn(v.w));
+}
+__device__ __forceinline__ float4 lo4(float4 v, float4 h) {
+  return make_float4(tf32_rn(v.x - h.x), tf32_rn(v.y - h.y), tf32_rn(v.z - h.z),
+                     tf32_rn(v.w - h.w));
+}
+
+__global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ PrepPlan plan) {
+  __shared__ float tile[2][kPrepTile][kPrepTile + 1];   // [hi/lo][k][row] (transposed path)
+  const long long item = blockIdx.x;
+  int j = 0;
+  while (j + 1 < plan.njobs && plan.job[j + 1].tile_begin <= item) ++j;
+  const PrepJob& J = plan.job[j];
+  const long long local = item - J.tile_begin;
+  const int ktiles = plan.row_len / kPrepTile;
+  const int r0 = int(local / ktiles) * kPrepTile, k0 = int(local % ktiles) * kPrepTile;
+  const long long batch = blockIdx.y;
+  const int t4 = (threadIdx.x % 16) * 4, t16 = threadIdx.x / 16;
+  float* region = plan.region + batch * plan.region_bstride;
+  const long long ld = plan.row_len;
+  if (J.transpose) {
+    // Left operand: element (r, k) at p + r + k*ld.  Read 4 rows of one k
+    // column per thread, split, transpose through shared memory.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int kk = t16 + 16 * i, r = r0 + t4, k = k0 + kk;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k < J.cols) {
+        if (r + 3 < J.rows) {
+          v = sum4(J, batch, r, k);
+        } else {
+          float e[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int q = 0; q < 4 && r + q < J.rows; ++q) e[q] = operand_sum(J, batch, r + q, k);
+          v = make_float4(e[0], e[1], e[2], e[3]);
+        }
+      }
+      const float4 h = hi4(v), l = lo4(v, h);
+      tile[0][kk][t4 + 0] = h.x; tile[0][kk][t4 + 1] = h.y;
+      tile[0][kk][t4 + 2] = h.z; tile[0][kk][t4 + 3] = h.w;
+      tile[1][kk][t4 + 0] = l.x; tile[1][kk][t4 + 1] = l.y;
+      tile[1][kk][t4 + 2] = l.z; tile[1][kk][t4 + 3] = l.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = t16 + 16 * i, r = r0 + rr;
+      if (r >= J.rows) continue;
+      const float4 h = make_float4(tile[0][t4][rr], tile[0][t4 + 1][rr], tile[0][t4 + 2][rr],
+                                   tile[0][t4 + 3][rr]);
+      const float4 l = make_float4(tile[1][t4][rr], tile[1][t4 + 1][rr], tile[1][t4 + 2][rr],
+                                   tile[1][t4 + 3][rr]);
+      *reinterpret_cast<float4*>(region + (long long)(J.out_hi + r) * ld + k0 + t4) = h;
+      *reinterpret_cast<float4*>(region + (long long)(J.out_lo + r) * ld + k0 + t4) = l;
+    }
+  } else {
+    // Right operand: element (k, n) at p + k + n*ld; read and write along k.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = t16 + 16 * i, r = r0 + rr, k = k0 + t4;
+      if (r >= J.rows) continue;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k + 3 < J.cols) {
+        v = sum4(J, batch, k, r);
+      } else if (k < J.cols) {
+        float e[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int q = 0; q < 4 && k + q < J.cols; ++q) {
+          const Term& T0 = J.in[0];
+          const float x0 = T0.p[batch * T0.bstride + k + q + (long long)r * T0.ld];
+          float acc = T0.coef < 0.f ? -x0 : x0;
+          for (int t = 1; t < J.nterms; ++t) {
+            const Term& T = J.in[t];
+            acc = fmaf(T.coef, T.p[batch * T.bstride + k + q + (long long)r * T.ld], acc);
+          }
+          e[q] = acc;
+        }
+        v = make_float4(e[0], e[1], e[2], e[3]);
+      }
+      const float4 h = hi4(v);
+      *reinterpret_cast<float4*>(region + (long long)(J.out_hi + r) * ld + k) = h;
+      *reinterpret_cast<float4*>(region + (long long)(J.out_lo + r) * ld + k) = lo4(v, h);
+    }
+  }
+}
+
+// ---- leaf products on prepared operands -------------------------------------
+template <int BN>
+__global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
+    leaf_prep_kernel(const __grid_constant__ PrepLeafPlan plan, const __grid_constant__ PrepMaps maps) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  Bars& sb = *reinterpret_cast<Bars*>(smem + C::kBarOffset);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  int pid = 0;
+  while (pid + 1 < plan.nprod && plan.prod[pid + 1].tile_begin <= int(blockIdx.x)) ++pid;
+  const PrepProd& P = plan.prod[pid];
+  const int local = blockIdx.x - P.tile_begin;
+  constexpr int GROUP_M = 8;
+  const int in_group = GROUP_M * P.tiles_n;
+  const int first_m = (local / in_group) * GROUP_M;
+  const int gsize = min(P.tiles_m - first_m, GROUP_M);
+  const int m0 = (first_m + (local % in_group) % gsize) * 128;
+  const int n0 = ((local % in_group) / gsize) * BN;
+  const int batch = blockIdx.y;
+  const int stages = (P.k + kStageK - 1) / kStageK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(&sb.full[i], 1);
+      mbar_init(&sb.empty[i], 1);
+    }
+    for (int i = 0; i < C::kChunkBufs; ++i) {
+      mbar_init(&sb.chunk_full[i], 1);
+      mbar_init(&sb.chunk_empty[i], C::kFoldWarps);
+    }
+    mbar_init(&sb.mma_done, 1);
+    sb.abort = 0;
+    // Make the initialised barriers visible to the async proxy (TMA, tcgen05).
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                     smem_u32(&sb.tmem_base))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sb.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      Ring r;
+      for (int s = 0; s < stages; ++s, r.next(C::kStages)) {
+        if (s >= C::kStages && !mbar_wait(sb, &sb.empty[r.idx], r.phase ^ 1u)) break;
+        unsigned char* st = smem + r.idx * C::kStageBytes;
+        mbar_expect_tx(&sb.full[r.idx], C::kStageBytes);
+        const int k0 = s * kStageK;
+        tma_load_3d(st, &maps.a, k0, P.a_hi + m0, batch, &sb.full[r.idx]);
+        tma_load_3d(st + C::kABytes, &maps.a, k0, P.a_lo + m0, batch, &sb.full[r.idx]);
+        tma_load_3d(st + 2 * C::kABytes, &maps.b, k0, P.b_hi + n0, batch, &sb.full[r.idx]);
+        tma_load_3d(st + 2 * C::kABytes + C::kBBytes, &maps.b, k0, P.b_lo + n0, batch,
+                    &sb.full[r.idx]);
+        ++issued;
+      }
+      // No copy may outlive the CTA: wait for the latest phase of every stage
+      // that may still be loading.
+      for (int s = max(0, issued - C::kStages); s < issued; ++s)
+        mbar_drain(&sb.full[s % C::kStages], (s / C::kStages) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      Ring r, rc;
+      for (int s = 0; s < stages; ++s, r.next(C::kStages), rc.next(C::kChunkBufs)) {
+        if (s >= C::kChunkBufs && !mbar_wait(sb, &sb.chunk_empty[rc.idx], rc.phase ^ 1u)) break;
+        if (!mbar_wait(sb, &sb.full[r.idx], r.phase)) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + r.idx * C::kStageBytes);
+        const uint32_t d = tmem + uint32_t(rc.idx * BN);
+#pragma unroll
+        for (int j = 0; j < kStageK / 8; ++j) {
+          const uint64_t a_hi = sw128_desc(st + 32 * j);
+          const uint64_t a_lo = sw128_desc(st + C::kABytes + 32 * j);
+          const uint64_t b_hi = sw128_desc(st + 2 * C::kABytes + 32 * j);
+          const uint64_t b_lo = sw128_desc(st + 2 * C::kABytes + C::kBBytes + 32 * j);
+          mma_ss<BN>(d, a_hi, b_hi, j > 0);
+          mma_ss<BN>(d, a_hi, b_lo, true);
+          mma_ss<BN>(d, a_lo, b_hi, true);
+        }
+        mma_commit(&sb.empty[r.idx]);
+        mma_commit(&sb.chunk_full[rc.idx]);
+      }
+      // All issued MMAs must finish before TMEM is released.
+      mma_commit(&sb.mma_done);
+      mbar_drain(&sb.mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    // Fold warp: TMEM lane quadrant q = warp % 4, columns [col0, col0 + 64).
+    const int q = warp % 4, col0 = ((warp - 2) / 4) * 64;
+    const uint32_t lane_base = uint32_t(q * 32) << 16;
+    float total[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) total[i] = 0.f;
+    bool ok = true;
+    Ring rc;
+    for (int c = 0; c < stages; ++c, rc.next(C::kChunkBufs)) {
+      const bool w = mbar_wait(sb, &sb.chunk_full[rc.idx], rc.phase);
+      if (!__all_sync(0xffffffffu, w)) {   // tcgen05.ld below is warp-collective
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t chunk = tmem + lane_base + uint32_t(rc.idx * BN + col0);
+#pragma unroll
+      for (int piece = 0; piece < 4; ++piece) {
+        float v[16];
+        tmem_ld16(chunk + 16 * piece, v);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int i = 0; i < 16; ++i) total[16 * piece + i] = __fadd_rn(total[16 * piece + i], v[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sb.chunk_empty[rc.idx]);
+    }
+    const int r = m0 + q * 32 + lane;
+    if (ok && !*(volatile int*)&sb.abort && r < P.m) {
+      for (int o = 0; o < P.no; ++o) {
+        const Term& T = plan.outs[P.o0 + o];
+        float* base = const_cast<float*>(T.p) + (long long)batch * T.bstride + r;
+        const float coef = T.coef;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const int col = n0 + col0 + i;
+          if (col >= P.n) break;
+          float* dst = base + (long long)col * T.ld;
+          if (T.mode == kOutAtomic) atomicAdd(dst, coef * total[i]);
+          else if (T.mode == kOutAdd) *dst += coef * total[i];
+          else *dst = coef * total[i];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+}
+
+namespace {
+
+using EncodeTiled = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeTiled encode_fn() {
+  static const EncodeTiled fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return EncodeTiled(nullptr);
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+// 3-D map {row_len k, rows, batch} over the prepared region, box 32 k x box_rows.
+bool encode_region(CUtensorMap* m, const float* region, long long row_len, long long rows,
+                   long long bstride, int batch, int box_rows) {
+  const EncodeTiled enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {cuuint64_t(row_len), cuuint64_t(rows), cuuint64_t(batch)};
+  const long long bs = batch > 1 ? bstride : row_len * rows;
+  const cuuint64_t strides[2] = {cuuint64_t(row_len) * 4, cuuint64_t(bs) * 4};
+  const cuuint32_t box[3] = {cuuint32_t(kStageK), cuuint32_t(box_rows), 1u};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(region), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+cudaError_t launch_bn(const PrepLeafPlan& plan, const PrepMaps& maps, int batch,
+                      cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(leaf_prep_kernel<BN>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Cfg<BN>::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  leaf_prep_kernel<BN><<<dim3(plan.ntiles, batch), Cfg<BN>::kThreads, Cfg<BN>::kSmemBytes, stream>>>(
+      plan, maps);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool prep_supported() { return encode_fn() != nullptr; }
+
+int prep_row_align() { return kPrepTile; }   // a multiple of the 32-k stage
+
+cudaError_t launch_prep(const PrepPlan& plan, int batch, cudaStream_t stream) {
+  if (plan.njobs == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
+  prep_kernel<<<dim3(unsigned(plan.ntiles), batch), 256, 0, stream>>>(plan);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int bn, const float* region,
+                             long long row_len, long long rows, long long region_bstride,
+                             int batch, cudaStream_t stream) {
+  if (plan.nprod == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
+  if (bn != 128 && bn != 256) return cudaErrorInvalidValue;
+  PrepMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if (!encode_region(&maps.a, region, row_len, rows, region_bstride, batch, 128) ||
+      !encode_region(&maps.b, region, row_len, rows, region_bstride, batch, bn))
+    return cudaErrorInvalidValue;
+  return bn == 128 ? launch_bn<128>(plan, maps, batch, stream)
+                   : launch_bn<256>(plan, maps, batch, stream);
+}
+
+cudaError_t read_and_clear_tc3_device_error(unsigned* value) {
+  cudaError_t e = cudaMemcpyFromSymbol(value, g_tc3_device_error, sizeof(unsigned));
+  if (e != cudaSuccess) return e;
+  const unsigned zero = 0;
+  return cudaMemcpyToSymbol(g_tc3_device_error, &zero, sizeof(unsigned));
+}
+
+TileShape prep_tile_shape(int bn) { return {128, bn}; }
+
+}  // namespace bag_b200
