@@ -384,20 +384,21 @@ void build_plan(const GemmDesc& g, float* ws, long long ws_bstride, Builder& B,
   int mc = g.m - g.m % align, kc = g.k - g.k % align, nc = g.n - g.n % align;
   if (depth == 0 || mc == 0 || kc == 0 || nc == 0) {
     B.leaves.push_back({g.m, g.n, g.k, {{A, 1.f}}, {{Bv, 1.f}}, {{C, 1.f, kOutAtomic}}});
-    return;
+  } else {
+    B.expand({{A, 1.f}}, {{Bv, 1.f}}, {{C, 1.f, kOutAtomic}}, mc, kc, nc, depth);
+    if (kc < g.k)
+      B.leaves.push_back({mc, nc, g.k - kc, {{{A.p + (long long)kc * A.ld, A.ld, A.bstride}, 1.f}},
+                          {{{Bv.p + kc, Bv.ld, Bv.bstride}, 1.f}}, {{C, 1.f, kOutAtomic}}});
+    if (mc < g.m)
+      B.leaves.push_back({g.m - mc, g.n, g.k, {{{A.p + mc, A.ld, A.bstride}, 1.f}}, {{Bv, 1.f}},
+                          {{{C.p + mc, C.ld, C.bstride}, 1.f, kOutAtomic}}});
+    if (nc < g.n)
+      B.leaves.push_back({mc, g.n - nc, g.k, {{A, 1.f}},
+                          {{{Bv.p + (long long)nc * Bv.ld, Bv.ld, Bv.bstride}, 1.f}},
+                          {{{C.p + (long long)nc * C.ld, C.ld, C.bstride}, 1.f, kOutAtomic}}});
   }
-  B.expand({{A, 1.f}}, {{Bv, 1.f}}, {{C, 1.f, kOutAtomic}}, mc, kc, nc, depth);
+  // Last, so every leaf (peeling strips included) gets its prepared operands.
   if (leaf_operands) B.prepare_leaf_operands(prep_row_align());
-  if (kc < g.k)
-    B.leaves.push_back({mc, nc, g.k - kc, {{{A.p + (long long)kc * A.ld, A.ld, A.bstride}, 1.f}},
-                        {{{Bv.p + kc, Bv.ld, Bv.bstride}, 1.f}}, {{C, 1.f, kOutAtomic}}});
-  if (mc < g.m)
-    B.leaves.push_back({g.m - mc, g.n, g.k, {{{A.p + mc, A.ld, A.bstride}, 1.f}}, {{Bv, 1.f}},
-                        {{{C.p + mc, C.ld, C.bstride}, 1.f, kOutAtomic}}});
-  if (nc < g.n)
-    B.leaves.push_back({mc, g.n - nc, g.k, {{A, 1.f}},
-                        {{{Bv.p + (long long)nc * Bv.ld, Bv.ld, Bv.bstride}, 1.f}},
-                        {{{C.p + (long long)nc * C.ld, C.ld, C.bstride}, 1.f, kOutAtomic}}});
 }
 
 // Workspace elements per batch entry (dry run with a fake base).
@@ -537,6 +538,9 @@ void run_prepared(Builder& B, int batch, cudaStream_t stream) {
       P.tiles_m = (l.m + ts.bm - 1) / ts.bm;
       P.tiles_n = (l.n + ts.bn - 1) / ts.bn;
       P.tile_begin = lp.ntiles;
+      if (l.prep_l < 0 || l.prep_r < 0 || l.prep_l >= int(B.prep.size()) ||
+          l.prep_r >= int(B.prep.size()))
+        fail(BAG_ERR_INTERNAL, "leaf without prepared operands");
       const Builder::PrepOp& L = B.prep[l.prep_l];
       const Builder::PrepOp& R = B.prep[l.prep_r];
       P.a_hi = L.hi_row;

@@ -27,7 +27,10 @@ def _operands(n: int, depth: int, basis: str):
     a = torch.randn(n, n, device="cuda", generator=g)
     b = torch.randn(n, n, device="cuda", generator=g)
     c = torch.zeros(n, n, device="cuda")
-    ws = bag.Workspace.for_problem(n, n, n, depth, basis) if depth >= 2 or basis != "minimal" else None
+    # In 3xTF32 mode a workspace (created in that mode) also holds the prepared
+    # TF32 hi/lo leaf operands, so every depth gets one there.
+    need_ws = depth >= 2 or basis != "minimal" or bag.get_math_mode() == "3xtf32"
+    ws = bag.Workspace.for_problem(n, n, n, depth, basis) if need_ws else None
     return a, b, c, ws
 
 

@@ -130,3 +130,45 @@ def test_tensor_path_against_oracle(tensor_mode):
     exact = O.fp64_matmul(a, b)
     assert O.rel_frobenius(got, exact) <= 1.25 * O.rel_frobenius(ref, exact)
     assert bag.device_error() == 0
+
+
+# Prepared-operand path: a workspace created in 3xTF32 mode also holds every
+# leaf operand as TF32 hi/lo rows (one prepare pass, then TMA/SS-MMA leaves).
+@pytest.mark.parametrize("m,k,n,depth,basis", [
+    (512, 2048, 768, 0, "minimal"), (1032, 4096, 2056, 2, "minimal"),
+    (4096, 4096, 4096, 2, "minimal"), (2048, 4096, 2048, 2, "full"),
+    (2048, 2048, 2048, 1, "classic"), (1000, 2048, 1160, 1, "minimal")])
+def test_prepared_path(tensor_mode, m, k, n, depth, basis):
+    import torch
+    bag = tensor_mode
+    a, b = _operands(torch, m, k, n, seed=m + n + depth)
+    # Column-major problem of the row-major call: C^T(n x m) = B^T A^T.
+    ws = bag.Workspace.for_problem(n, m, k, depth, basis)
+    bag.set_math_mode("ffma")
+    ws_ffma = bag.Workspace.for_problem(n, m, k, depth, basis)
+    assert ws.bytes() > ws_ffma.bytes()   # the prepared region
+    c_tc, path = _sgemm(bag, torch, a, b, depth, basis, ws, "3xtf32")
+    assert path == "3xtf32"
+    assert bag.device_error() == 0
+    c_ff, _ = _sgemm(bag, torch, a, b, depth, basis, ws_ffma, "ffma")
+    err, ffma = _rel(torch, c_tc, a, b), _rel(torch, c_ff, a, b)
+    assert err <= 1e-4
+    assert err <= 1.25 * ffma, (err, ffma)
+
+
+def test_prepared_path_batched_and_accumulating(tensor_mode):
+    import torch
+    bag = tensor_mode
+    batch, n = 2, 2048
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.rand(batch, n, n, device="cuda", generator=g)
+    b = torch.rand(batch, n, n, device="cuda", generator=g)
+    c0 = torch.rand(batch, n, n, device="cuda", generator=g)
+    ws = bag.Workspace.for_problem(n, n, n, 1, batch=batch)
+    c = c0.clone()
+    bag.sgemm_batched(a, b, c, beta=1.0, depth=1, workspace=ws)
+    torch.cuda.synchronize()
+    assert bag.last_leaf_path() == "3xtf32"
+    exact = c0.double() + a.double() @ b.double()
+    assert float((c.double() - exact).norm() / exact.norm()) <= 2e-6
+    assert bag.device_error() == 0
