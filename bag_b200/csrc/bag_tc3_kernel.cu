@@ -7,8 +7,8 @@
 //   operands are transposed on the way through a shared-memory tile) and
 //   zero-padded to the region's row length (a multiple of the 64-k tile).
 //
-// leaf_prep_kernel<BN>: one CTA computes a 128 x BN output tile of one leaf
-//   product straight from the region:
+// leaf_prep_kernel<BN>: persistent (one CTA per SM); each CTA computes 128 x BN
+//   output tiles of the leaf products in turn, straight from the region:
 //  * warp 0, lane 0: per 32-k stage four TMA loads (A hi, A lo: 128 rows x
 //    32 k; B hi, B lo: BN rows x 32 k; 128-byte swizzle, K-major) into a ring
 //    of stages; warp 0 also owns TMEM.
@@ -343,26 +343,42 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ PrepP
 }
 
 // ---- leaf products on prepared operands -------------------------------------
-template <int BN>
-__global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
-    leaf_prep_kernel(const __grid_constant__ PrepLeafPlan plan, const __grid_constant__ PrepMaps maps) {
-  using C = Cfg<BN>;
-  extern __shared__ __align__(1024) unsigned char smem[];
-  Bars& sb = *reinterpret_cast<Bars*>(smem + C::kBarOffset);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Persistent: CTA b processes work items b, b + gridDim.x, ... (item = batch *
+// ntiles + tile); the stage and chunk rings run on across items, so the fold
+// warps' epilogue of one tile overlaps the next tile's loads and MMAs.
+struct TileCoord {
+  const PrepProd* P;
+  int m0, n0, batch, stages;
+};
 
+template <int BN>
+__device__ __forceinline__ TileCoord tile_of(const PrepLeafPlan& plan, int item) {
+  const int batch = item / plan.ntiles, t = item - batch * plan.ntiles;
   int pid = 0;
-  while (pid + 1 < plan.nprod && plan.prod[pid + 1].tile_begin <= int(blockIdx.x)) ++pid;
+  while (pid + 1 < plan.nprod && plan.prod[pid + 1].tile_begin <= t) ++pid;
   const PrepProd& P = plan.prod[pid];
-  const int local = blockIdx.x - P.tile_begin;
+  const int local = t - P.tile_begin;
   constexpr int GROUP_M = 8;
   const int in_group = GROUP_M * P.tiles_n;
   const int first_m = (local / in_group) * GROUP_M;
   const int gsize = min(P.tiles_m - first_m, GROUP_M);
-  const int m0 = (first_m + (local % in_group) % gsize) * 128;
-  const int n0 = ((local % in_group) / gsize) * BN;
-  const int batch = blockIdx.y;
-  const int stages = (P.k + kStageK - 1) / kStageK;
+  TileCoord c;
+  c.P = &P;
+  c.m0 = (first_m + (local % in_group) % gsize) * 128;
+  c.n0 = ((local % in_group) / gsize) * BN;
+  c.batch = batch;
+  c.stages = (P.k + kStageK - 1) / kStageK;
+  return c;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
+    leaf_prep_kernel(const __grid_constant__ PrepLeafPlan plan, const __grid_constant__ PrepMaps maps,
+                     int items) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  Bars& sb = *reinterpret_cast<Bars*>(smem + C::kBarOffset);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::kStages; ++i) {
@@ -391,47 +407,67 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
+      long long issued = 0;
       Ring r;
-      for (int s = 0; s < stages; ++s, r.next(C::kStages)) {
-        if (s >= C::kStages && !mbar_wait(sb, &sb.empty[r.idx], r.phase ^ 1u)) break;
-        unsigned char* st = smem + r.idx * C::kStageBytes;
-        mbar_expect_tx(&sb.full[r.idx], C::kStageBytes);
-        const int k0 = s * kStageK;
-        tma_load_3d(st, &maps.a, k0, P.a_hi + m0, batch, &sb.full[r.idx]);
-        tma_load_3d(st + C::kABytes, &maps.a, k0, P.a_lo + m0, batch, &sb.full[r.idx]);
-        tma_load_3d(st + 2 * C::kABytes, &maps.b, k0, P.b_hi + n0, batch, &sb.full[r.idx]);
-        tma_load_3d(st + 2 * C::kABytes + C::kBBytes, &maps.b, k0, P.b_lo + n0, batch,
-                    &sb.full[r.idx]);
-        ++issued;
+      bool ok = true;
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const TileCoord tc = tile_of<BN>(plan, item);
+        for (int s = 0; s < tc.stages; ++s, r.next(C::kStages)) {
+          if (issued >= C::kStages && !mbar_wait(sb, &sb.empty[r.idx], r.phase ^ 1u)) {
+            ok = false;
+            break;
+          }
+          unsigned char* st = smem + r.idx * C::kStageBytes;
+          mbar_expect_tx(&sb.full[r.idx], C::kStageBytes);
+          const int k0 = s * kStageK;
+          const PrepProd& P = *tc.P;
+          tma_load_3d(st, &maps.a, k0, P.a_hi + tc.m0, tc.batch, &sb.full[r.idx]);
+          tma_load_3d(st + C::kABytes, &maps.a, k0, P.a_lo + tc.m0, tc.batch, &sb.full[r.idx]);
+          tma_load_3d(st + 2 * C::kABytes, &maps.b, k0, P.b_hi + tc.n0, tc.batch, &sb.full[r.idx]);
+          tma_load_3d(st + 2 * C::kABytes + C::kBBytes, &maps.b, k0, P.b_lo + tc.n0, tc.batch,
+                      &sb.full[r.idx]);
+          ++issued;
+        }
       }
       // No copy may outlive the CTA: wait for the latest phase of every stage
-      // that may still be loading.
-      for (int s = max(0, issued - C::kStages); s < issued; ++s)
-        mbar_drain(&sb.full[s % C::kStages], (s / C::kStages) & 1);
+      // slot that may still be loading.
+      for (long long s = issued > C::kStages ? issued - C::kStages : 0; s < issued; ++s)
+        mbar_drain(&sb.full[s % C::kStages], unsigned((s / C::kStages) & 1));
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       Ring r, rc;
-      for (int s = 0; s < stages; ++s, r.next(C::kStages), rc.next(C::kChunkBufs)) {
-        if (s >= C::kChunkBufs && !mbar_wait(sb, &sb.chunk_empty[rc.idx], rc.phase ^ 1u)) break;
-        if (!mbar_wait(sb, &sb.full[r.idx], r.phase)) break;
-        tc_fence_after();
-        const uint32_t st = smem_u32(smem + r.idx * C::kStageBytes);
-        const uint32_t d = tmem + uint32_t(rc.idx * BN);
+      long long chunks = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+        const TileCoord tc = tile_of<BN>(plan, item);
+        for (int s = 0; s < tc.stages; ++s, r.next(C::kStages), rc.next(C::kChunkBufs)) {
+          if (chunks >= C::kChunkBufs && !mbar_wait(sb, &sb.chunk_empty[rc.idx], rc.phase ^ 1u)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(sb, &sb.full[r.idx], r.phase)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + r.idx * C::kStageBytes);
+          const uint32_t d = tmem + uint32_t(rc.idx * BN);
 #pragma unroll
-        for (int j = 0; j < kStageK / 8; ++j) {
-          const uint64_t a_hi = sw128_desc(st + 32 * j);
-          const uint64_t a_lo = sw128_desc(st + C::kABytes + 32 * j);
-          const uint64_t b_hi = sw128_desc(st + 2 * C::kABytes + 32 * j);
-          const uint64_t b_lo = sw128_desc(st + 2 * C::kABytes + C::kBBytes + 32 * j);
-          mma_ss<BN>(d, a_hi, b_hi, j > 0);
-          mma_ss<BN>(d, a_hi, b_lo, true);
-          mma_ss<BN>(d, a_lo, b_hi, true);
+          for (int j = 0; j < kStageK / 8; ++j) {
+            const uint64_t a_hi = sw128_desc(st + 32 * j);
+            const uint64_t a_lo = sw128_desc(st + C::kABytes + 32 * j);
+            const uint64_t b_hi = sw128_desc(st + 2 * C::kABytes + 32 * j);
+            const uint64_t b_lo = sw128_desc(st + 2 * C::kABytes + C::kBBytes + 32 * j);
+            mma_ss<BN>(d, a_hi, b_hi, j > 0);
+            mma_ss<BN>(d, a_hi, b_lo, true);
+            mma_ss<BN>(d, a_lo, b_hi, true);
+          }
+          mma_commit(&sb.empty[r.idx]);
+          mma_commit(&sb.chunk_full[rc.idx]);
+          ++chunks;
         }
-        mma_commit(&sb.empty[r.idx]);
-        mma_commit(&sb.chunk_full[rc.idx]);
       }
       // All issued MMAs must finish before TMEM is released.
       mma_commit(&sb.mma_done);
@@ -442,45 +478,51 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     // Fold warp: TMEM lane quadrant q = warp % 4, columns [col0, col0 + 64).
     const int q = warp % 4, col0 = ((warp - 2) / 4) * 64;
     const uint32_t lane_base = uint32_t(q * 32) << 16;
-    float total[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) total[i] = 0.f;
-    bool ok = true;
     Ring rc;
-    for (int c = 0; c < stages; ++c, rc.next(C::kChunkBufs)) {
-      const bool w = mbar_wait(sb, &sb.chunk_full[rc.idx], rc.phase);
-      if (!__all_sync(0xffffffffu, w)) {   // tcgen05.ld below is warp-collective
-        ok = false;
-        break;
+    bool ok = true;
+    for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+      const TileCoord tc = tile_of<BN>(plan, item);
+      float total[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) total[i] = 0.f;
+      for (int c = 0; c < tc.stages; ++c, rc.next(C::kChunkBufs)) {
+        const bool w = mbar_wait(sb, &sb.chunk_full[rc.idx], rc.phase);
+        if (!__all_sync(0xffffffffu, w)) {   // tcgen05.ld below is warp-collective
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t chunk = tmem + lane_base + uint32_t(rc.idx * BN + col0);
+#pragma unroll
+        for (int piece = 0; piece < 4; ++piece) {
+          float v[16];
+          tmem_ld16(chunk + 16 * piece, v);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            total[16 * piece + i] = __fadd_rn(total[16 * piece + i], v[i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sb.chunk_empty[rc.idx]);
       }
-      tc_fence_after();
-      const uint32_t chunk = tmem + lane_base + uint32_t(rc.idx * BN + col0);
+      if (!ok || *(volatile int*)&sb.abort) break;
+      const PrepProd& P = *tc.P;
+      const int r = tc.m0 + q * 32 + lane;
+      if (r < P.m) {
+        for (int o = 0; o < P.no; ++o) {
+          const Term& T = plan.outs[P.o0 + o];
+          float* base = const_cast<float*>(T.p) + (long long)tc.batch * T.bstride + r;
+          const float coef = T.coef;
 #pragma unroll
-      for (int piece = 0; piece < 4; ++piece) {
-        float v[16];
-        tmem_ld16(chunk + 16 * piece, v);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int i = 0; i < 16; ++i) total[16 * piece + i] = __fadd_rn(total[16 * piece + i], v[i]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sb.chunk_empty[rc.idx]);
-    }
-    const int r = m0 + q * 32 + lane;
-    if (ok && !*(volatile int*)&sb.abort && r < P.m) {
-      for (int o = 0; o < P.no; ++o) {
-        const Term& T = plan.outs[P.o0 + o];
-        float* base = const_cast<float*>(T.p) + (long long)batch * T.bstride + r;
-        const float coef = T.coef;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const int col = n0 + col0 + i;
-          if (col >= P.n) break;
-          float* dst = base + (long long)col * T.ld;
-          if (T.mode == kOutAtomic) atomicAdd(dst, coef * total[i]);
-          else if (T.mode == kOutAdd) *dst += coef * total[i];
-          else *dst = coef * total[i];
+          for (int i = 0; i < 64; ++i) {
+            const int col = tc.n0 + col0 + i;
+            if (col >= P.n) break;
+            float* dst = base + (long long)col * T.ld;
+            if (T.mode == kOutAtomic) atomicAdd(dst, coef * total[i]);
+            else if (T.mode == kOutAdd) *dst += coef * total[i];
+            else *dst = coef * total[i];
+          }
         }
       }
     }
@@ -531,8 +573,15 @@ cudaError_t launch_bn(const PrepLeafPlan& plan, const PrepMaps& maps, int batch,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        Cfg<BN>::kSmemBytes);
   if (e != cudaSuccess) return e;
-  leaf_prep_kernel<BN><<<dim3(plan.ntiles, batch), Cfg<BN>::kThreads, Cfg<BN>::kSmemBytes, stream>>>(
-      plan, maps);
+  int dev = 0, sms = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const long long items = (long long)plan.ntiles * batch;
+  if (items > INT32_MAX) return cudaErrorInvalidValue;
+  const int grid = int(items < sms ? items : sms);   // one resident CTA per SM
+  leaf_prep_kernel<BN><<<grid, Cfg<BN>::kThreads, Cfg<BN>::kSmemBytes, stream>>>(plan, maps,
+                                                                                 int(items));
   return cudaGetLastError();
 }
 
