@@ -784,7 +784,8 @@ std::string dump_plan(int m, int n, int k, long long lda, long long ldb, long lo
              reinterpret_cast<const float*>(2 * unit), ldb, 0,
              reinterpret_cast<float*>(3 * unit), ldc, 0, 1, depth, basis};
   Builder B;
-  build_plan(g, reinterpret_cast<float*>(4 * unit), 0, B);
+  // In 3xTF32 mode the plan also lists the prepared (TF32 hi/lo) operands.
+  build_plan(g, reinterpret_cast<float*>(4 * unit), 0, B, leaf_materialisation_wanted(g));
   auto ref = [&](const View& v) {
     const uintptr_t p = reinterpret_cast<uintptr_t>(v.p);
     const uintptr_t base = p / unit;
@@ -831,6 +832,19 @@ std::string dump_plan(int m, int n, int k, long long lda, long long ldb, long lo
     for (size_t t = 0; t < l.out.size(); ++t)
       s += std::string(t ? "," : "") + "[" + ref(l.out[t].v) + "," +
            std::to_string(int(l.out[t].coef)) + "]";
+    s += "],\"prep_l\":" + std::to_string(l.prep_l) + ",\"prep_r\":" + std::to_string(l.prep_r) +
+         "}";
+  }
+  s += "],\"prepared_row_len\":" + std::to_string(B.prep_row_len) + ",\"prepared\":[";
+  for (size_t i = 0; i < B.prep.size(); ++i) {
+    const Builder::PrepOp& o = B.prep[i];
+    s += i ? "," : "";
+    s += "{\"rows\":" + std::to_string(o.rows) + ",\"cols\":" + std::to_string(o.cols) +
+         ",\"transpose\":" + std::string(o.transpose ? "true" : "false") +
+         ",\"hi_row\":" + std::to_string(o.hi_row) + ",\"terms\":[";
+    for (size_t t = 0; t < o.terms.size(); ++t)
+      s += std::string(t ? "," : "") + "[" + ref(o.terms[t].v) + "," +
+           std::to_string(int(o.terms[t].coef)) + "]";
     s += "]}";
   }
   s += "]}";
