@@ -10,13 +10,15 @@ flush is needed between steps.  The leaf arithmetic is ``--math``: 3xTF32
 checked in the same run to stay within 1.25x the FFMA path's error, the
 reference's numerics) or ffma (sequential FP32 fmaf chains, SIMT).
 
-On N GPUs (one process per GPU, torchrun) every rank owns the same row band
-of each of the 2^depth block-rows of A and C (a compact (M/N) x K shard whose
-BAG recursion is exactly the restriction of the full one) and all of B: the
-units are independent, there is no collective on the data path of ``value``,
-and the total work is fixed (strong scaling).  ``e2e`` goes through the
-public API from pinned host buffers: each rank uploads its A shard and 1/N of
-B, B is all-gathered over NVLink (NCCL), and each rank reads back its C band.
+On N GPUs (one process per GPU, torchrun) the ranks form an R x S grid
+(1x1, 2x1, 2x2, 4x2 for N = 1, 2, 4, 8): rank (i, j) owns row band i of every
+one of the 2^depth block-rows of A and C and column band j of every block-column
+of B and C.  BAG only combines blocks at equal offsets, so the recursion on
+the compact (M/R) x K and K x (N/S) shards is exactly the restriction of the
+full one: the units are independent, there is no collective on the data path,
+and the total work is fixed (strong scaling).  ``e2e`` goes through the public
+API from pinned host buffers: each rank uploads its A and B shards and reads
+back its C shard.
 
 ``--impl reference`` times the reference algorithm's CPU restatement
 (``oracle/bag_oracle.py``, numpy/OpenBLAS, all host threads) on a row-band
@@ -79,8 +81,13 @@ def make_inputs(size: int) -> tuple[np.ndarray, np.ndarray]:
     return a, b
 
 
+def shard_grid(world: int) -> tuple[int, int]:
+    """R x S rank grid: row bands x column bands."""
+    return {1: (1, 1), 2: (2, 1), 4: (2, 2), 8: (4, 2)}.get(world, (world, 1))
+
+
 def band_rows(size: int, depth: int, world: int, rank: int) -> np.ndarray:
-    """Rows of A/C owned by `rank`: its band of each of the 2^depth block-rows."""
+    """Indices owned by band `rank` of `world`: its band of each of the 2^depth blocks."""
     blocks = 1 << depth
     q = size // blocks
     band = q // world
@@ -245,24 +252,26 @@ def run_bag(args) -> None:
     bag.set_math_mode(args.math)
 
     size, depth = args.size, args.depth
-    if size % ((4 << depth) * world):
-        raise SystemExit("size must split into aligned row bands for this GPU count")
+    gr, gc = shard_grid(world)
+    if size % ((4 << depth) * gr) or size % ((4 << depth) * gc):
+        raise SystemExit("size must split into aligned bands for this GPU count")
     a_np, b_np = make_inputs(size)
-    rows = band_rows(size, depth, world, rank)
-    mg = rows.size
+    rows = band_rows(size, depth, gr, rank // gc)
+    cols = band_rows(size, depth, gc, rank % gc)
+    mg, ng = rows.size, cols.size
     a_shard = np.ascontiguousarray(a_np[rows])
+    b_shard = np.ascontiguousarray(b_np[:, cols]) if gc > 1 else b_np
 
     # Pinned host buffers (the e2e inputs) and device buffers (the value inputs).
     a_host = torch.from_numpy(a_shard).pin_memory()
-    b_part_rows = size // world
-    b_host_part = torch.from_numpy(np.ascontiguousarray(
-        b_np[rank * b_part_rows:(rank + 1) * b_part_rows])).pin_memory()
-    c_host = torch.empty((mg, size), dtype=torch.float32).pin_memory()
+    b_host = torch.from_numpy(b_shard).pin_memory()
+    c_host = torch.empty((mg, ng), dtype=torch.float32).pin_memory()
     a_dev = a_host.to(device)
-    b_dev = torch.from_numpy(b_np).to(device)
-    c_dev = torch.zeros((mg, size), dtype=torch.float32, device=device)
+    b_dev = b_host.to(device)
+    c_dev = torch.zeros((mg, ng), dtype=torch.float32, device=device)
     del a_np
-    ws = bag.Workspace.for_problem(size, mg, size, depth, args.basis)
+    # Row-major C(mg x ng) = A B is the column-major ng x mg problem.
+    ws = bag.Workspace.for_problem(ng, mg, size, depth, args.basis)
     stream = torch.cuda.current_stream()
 
     def step():
@@ -316,8 +325,8 @@ def run_bag(args) -> None:
     leaf_ms = reduce_max(sum(s.elapsed_time(e) for s, e in pairs) / args.steps)
     flops_total = 2.0 * size * size * size
     value = flops_total / (ms * 1e-3) / 1e12
-    # Executed leaf FLOPs of this rank's launch: 7^depth products of (mg/2^d)(N/2^d)(K/2^d).
-    f_exec = 7 ** depth * 2.0 * (mg / 2 ** depth) * (size / 2 ** depth) * (size / 2 ** depth)
+    # Executed leaf FLOPs of this rank's launch: 7^depth products of (mg/2^d)(ng/2^d)(K/2^d).
+    f_exec = 7 ** depth * 2.0 * (mg / 2 ** depth) * (ng / 2 ** depth) * (size / 2 ** depth)
     leaf_tflops = f_exec / (leaf_ms * 1e-3) / 1e12
 
     # FP32 FFMA peak: nominal at the max SM clock, and measured by the probe.
@@ -341,17 +350,10 @@ def run_bag(args) -> None:
     probe = fl.value / (p0.elapsed_time(p1) * 1e-3) / 1e12
 
     # End to end through the public API, host buffers in and out.
-    b_parts = torch.empty((size, size), dtype=torch.float32, device=device)
-
     def e2e_step():
         a_dev.copy_(a_host, non_blocking=True)
-        if world > 1:
-            mine = b_parts[rank * b_part_rows:(rank + 1) * b_part_rows]
-            mine.copy_(b_host_part, non_blocking=True)
-            dist.all_gather_into_tensor(b_parts, mine)
-        else:
-            b_parts.copy_(b_host_part, non_blocking=True)
-        bag.sgemm(a_dev, b_parts, c_dev, beta=0.0, depth=depth, basis=args.basis, workspace=ws)
+        b_dev.copy_(b_host, non_blocking=True)
+        bag.sgemm(a_dev, b_dev, c_dev, beta=0.0, depth=depth, basis=args.basis, workspace=ws)
         c_host.copy_(c_dev, non_blocking=True)
 
     for _ in range(min(args.warmup, 2)):
@@ -367,7 +369,7 @@ def run_bag(args) -> None:
     torch.cuda.synchronize()
     barrier()
     e2e_ms = reduce_max(e0.elapsed_time(e1)) / args.steps
-    h2d = 4 * (size * size + size * size)
+    h2d = int(reduce_sum(4.0 * (mg * size + size * ng)))   # all ranks' shards
     d2h = 4 * size * size
 
     # Comparators: cuBLAS SGEMM (torch, IEEE FP32, no TF32) and this library's
@@ -490,7 +492,7 @@ def run_bag(args) -> None:
             "config": {"workload": WORKLOAD, "M": size, "N": size, "K": size, "depth": depth,
                        "basis": args.basis, "layout": "row-major", "leaf_math": leaf_path,
                        "l2": "inputs larger than L2 (1 GiB each); no flush",
-                       "parallelism": f"row-band shards x{world}, B replicated" if world > 1
+                       "parallelism": f"{gr}x{gc} grid of row/column-band shards" if world > 1
                        else "single GPU"},
             "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
