@@ -122,6 +122,18 @@ def _check(status: int) -> None:
         raise BagError(status, msg)
 
 
+DEPTH_AUTO = -1   # BAG_DEPTH_AUTO
+
+
+def _depth(depth) -> int:
+    """An explicit depth, or "auto" / -1 for the library's choice (BAG_DEPTH_AUTO)."""
+    if isinstance(depth, str):
+        if depth != "auto":
+            raise ValueError(f"unknown depth {depth!r}")
+        return DEPTH_AUTO
+    return int(depth)
+
+
 def _basis(basis) -> int:
     if isinstance(basis, int):
         return basis
@@ -134,6 +146,7 @@ def plan_dump(m: int, n: int, k: int, lda: int, ldb: int, ldc: int, depth: int,
               basis="minimal") -> dict:
     """The host plan of a column-major problem as a dict (no GPU needed)."""
     need = ctypes.c_size_t(0)
+    depth = _depth(depth)
     _check(lib().bag_plan_dump(m, n, k, lda, ldb, ldc, depth, _basis(basis), None, 0,
                                ctypes.byref(need)))
     buf = ctypes.create_string_buffer(need.value)
@@ -238,10 +251,10 @@ class Workspace:
         self.k = n if k is None else k
         self.batch = batch
         handle = ctypes.c_void_p()
-        if square and m is None and k is None and batch == 1:
+        if square and m is None and k is None and batch == 1 and _depth(depth) >= 0:
             _check(lib().bag_workspace_create(n, depth, _basis(basis), ctypes.byref(handle)))
         else:
-            _check(lib().bag_workspace_create_ex(self.m, n, self.k, depth, _basis(basis), batch,
+            _check(lib().bag_workspace_create_ex(self.m, n, self.k, _depth(depth), _basis(basis), batch,
                                                  ctypes.byref(handle)))
         self._handle = handle
 
@@ -293,7 +306,7 @@ def sgemm(a, b, c, *, beta: float = 1.0, depth: int = 1, basis="minimal",
         raise ValueError("sgemm needs a, b, c all row-major or all column-major")
     ws = workspace.handle if workspace is not None else None
     _check(lib().bag_sgemm_ex(LAYOUT[la[0]], m, n, k, a.data_ptr(), la[1], b.data_ptr(), lb[1],
-                              c.data_ptr(), lc[1], float(beta), depth, _basis(basis),
+                              c.data_ptr(), lc[1], float(beta), _depth(depth), _basis(basis),
                               _stream_handle(stream), ws))
     return c
 
@@ -310,7 +323,7 @@ def sgemm_batched(a, b, c, *, beta: float = 1.0, depth: int = 1, basis="minimal"
             raise ValueError("sgemm_batched needs contiguous row-major tensors")
     ws = workspace.handle if workspace is not None else None
     _check(lib().bag_sgemm_batched(LAYOUT["row"], m, n, k, a.data_ptr(), k, m * k, b.data_ptr(), n,
-                                   k * n, c.data_ptr(), n, m * n, batch, float(beta), depth,
+                                   k * n, c.data_ptr(), n, m * n, batch, float(beta), _depth(depth),
                                    _basis(basis), _stream_handle(stream), ws))
     return c
 

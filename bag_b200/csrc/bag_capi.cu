@@ -46,6 +46,23 @@ thread_local int g_last_leaf_path = BAG_MATH_FFMA;
 // with K and passes it near K = 256.  Measured on B200 (N(0,1) operands):
 // tensor/FFMA error ratio 2.1 at K = 64, 1.07 at 256, 0.56 at 1024, 0.32 at 4096.
 constexpr int kTcMinK = 1024;
+
+// BAG_DEPTH_AUTO: the depth is chosen from the shape and this thread's math
+// mode.  Measured on B200 (square N(0,1) problems, effective TFLOP/s):
+// 3xTF32 is best with leaves of at least 8192 (N=4096: d0 193, d1 177;
+// N=8192: d0 231, d1 229; N=16384: d0 207, d1 231, d2 224 -- a 16384-long K
+// panel no longer fits L2), FFMA one level deeper per doubling from 2048
+// (N=4096: d1 49, d2 53; N=8192: d2 58, d3 55; N=16384: d2 60, d3 63).
+int resolve_depth(int depth, int m, int n, int k) {
+  if (depth != BAG_DEPTH_AUTO) return depth;
+  const int s = std::min(m, std::min(n, k));
+  if (g_math_mode == BAG_MATH_3XTF32) {
+    int d = 0;
+    while (d < 3 && (s >> (d + 1)) >= 8192) ++d;
+    return d;
+  }
+  return s >= 16384 ? 3 : s >= 2048 ? 2 : s >= 1024 ? 1 : 0;
+}
 thread_local cudaEvent_t g_prof_start = nullptr;
 thread_local cudaEvent_t g_prof_end = nullptr;
 std::atomic<unsigned long long> g_launches{0};
@@ -674,7 +691,8 @@ void check_device_workspace(const bag_workspace* ws) {
 
 void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
   if (g.m < 0 || g.n < 0 || g.k < 0) fail(BAG_ERR_SHAPE, "negative extent");
-  if (g.depth < 0 || g.depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8");
+  g.depth = resolve_depth(g.depth, g.m, g.n, g.k);
+  if (g.depth < 0 || g.depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8 or BAG_DEPTH_AUTO");
   if (g.basis != kMinimal && g.basis != kFull && g.basis != kClassic)
     fail(BAG_ERR_INVALID, "unknown basis");
   if (beta != 0.f && beta != 1.f) fail(BAG_ERR_UNSUPPORTED, "beta must be 0 or 1");
@@ -876,7 +894,8 @@ bag_status bag_workspace_create_ex(int m, int n, int k, int depth, int basis, in
     if (!out) fail(BAG_ERR_INVALID, "null output pointer");
     *out = nullptr;
     if (m < 0 || n < 0 || k < 0 || batch < 0) fail(BAG_ERR_SHAPE, "negative extent");
-    if (depth < 0 || depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8");
+    depth = resolve_depth(depth, m, n, k);
+    if (depth < 0 || depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8 or BAG_DEPTH_AUTO");
     if (basis != kMinimal && basis != kFull && basis != kClassic) fail(BAG_ERR_INVALID, "unknown basis");
     GemmDesc g{m, n, k, nullptr, std::max(1, m), 0, nullptr, std::max(1, k), 0, nullptr,
                std::max(1, m), 0, std::max(batch, 1), depth, basis};
@@ -1020,9 +1039,10 @@ bag_status sgemm_with_scratch(int layout, int m, int n, int k, const float* a, l
                               int depth, int basis, cudaStream_t stream, float* scratch,
                               size_t scratch_elements) {
   return guarded([&] {
-    const GemmDesc g = make_desc(layout, m, n, k, a, lda, 0, b, ldb, 0, c, ldc, 0, 1, depth, basis);
+    GemmDesc g = make_desc(layout, m, n, k, a, lda, 0, b, ldb, 0, c, ldc, 0, 1, depth, basis);
     if (g.m < 0 || g.n < 0 || g.k < 0) fail(BAG_ERR_SHAPE, "negative extent");
-    if (g.depth < 0 || g.depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8");
+    g.depth = resolve_depth(g.depth, g.m, g.n, g.k);
+    if (g.depth < 0 || g.depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8 or BAG_DEPTH_AUTO");
     if (g.basis != kMinimal && g.basis != kFull && g.basis != kClassic)
       fail(BAG_ERR_INVALID, "unknown basis");
     const size_t need = (g.m > 0 && g.n > 0 && g.k > 0) ? plan_workspace_elements(g) : 0;
@@ -1162,7 +1182,8 @@ bag_status bag_plan_dump(int m, int n, int k, long long lda, long long ldb, long
                          int depth, int basis, char* buf, size_t buflen, size_t* needed) {
   return guarded([&] {
     if (m < 0 || n < 0 || k < 0) fail(BAG_ERR_SHAPE, "negative extent");
-    if (depth < 0 || depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8");
+    depth = resolve_depth(depth, m, n, k);
+    if (depth < 0 || depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8 or BAG_DEPTH_AUTO");
     if (basis != kMinimal && basis != kFull && basis != kClassic) fail(BAG_ERR_INVALID, "unknown basis");
     const std::string s = dump_plan(m, n, k, lda, ldb, ldc, depth, basis);
     if (needed) *needed = s.size() + 1;

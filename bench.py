@@ -100,17 +100,21 @@ def band_rows(size: int, depth: int, world: int, rank: int) -> np.ndarray:
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
+    """nvidia-smi clock/throttle samples every 50 ms, each stamped with host time;
+    summary() keeps those inside [window] (the timed region), else the nearest."""
+
     def __init__(self, device_index: int):
         self.device_index = device_index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
         self._thread = None
+        self.window: tuple[float, float] | None = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.device_index)],
+                 "-lms", "50", "-i", str(self.device_index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._thread = threading.Thread(target=self._read, daemon=True)
             self._thread.start()
@@ -120,7 +124,7 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -135,7 +139,18 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, maxes, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        lines = [ln for _, ln in self.lines]
+        in_window = 0
+        if self.window is not None and self.lines:
+            t0, t1 = self.window
+            inside = [ln for t, ln in self.lines if t0 <= t <= t1]
+            in_window = len(inside)
+            if inside:
+                lines = inside
+            else:   # timed region shorter than the sampling period: the nearest samples
+                mid = 0.5 * (t0 + t1)
+                lines = [ln for _, ln in sorted(self.lines, key=lambda x: abs(x[0] - mid))[:2]]
+        for line in lines:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -148,9 +163,11 @@ class ClockSampler:
                 if val.lower().startswith("active"):
                     reasons.add(name)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "samples_in_timed_region": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(maxes),
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "samples_in_timed_region": in_window}
 
 
 # ---------------------------------------------------------------------------
@@ -311,6 +328,8 @@ def run_bag(args) -> None:
     launches0 = bag.launch_count()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        time.sleep(0.15)   # let the sampler start before the timed region
+        host0 = time.time()
         t_start.record()
         for i in range(args.steps):
             bag.profile_events(*pairs[i])
@@ -318,6 +337,8 @@ def run_bag(args) -> None:
         bag.profile_events(None, None)
         t_end.record()
         torch.cuda.synchronize()
+        clocks.window = (host0, time.time())
+        time.sleep(0.12)
     barrier()
     launches = reduce_sum(bag.launch_count() - launches0)
     leaf_path = bag.last_leaf_path()
@@ -498,7 +519,8 @@ def run_bag(args) -> None:
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "roofline": roofline,
             "ffma_probe_tflops": probe,
-            "clocks": {k: csum[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+            "clocks": {k: csum[k] for k in ("sm_mhz", "sm_max_mhz", "reasons",
+                                            "samples_in_timed_region")},
             "gpu_launches": int(launches),
             "executed_tflops": f_exec * world / (ms * 1e-3) / 1e12,
         }

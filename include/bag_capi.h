@@ -55,6 +55,11 @@ enum {
   BAG_STRASSEN_PAIRED_NORMAL = 5, BAG_STRASSEN_FOUR_BATCHED_ATOMIC = 6
 };
 enum { BAG_LAYOUT_COL_MAJOR = 0, BAG_LAYOUT_ROW_MAJOR = 1 };
+/* `depth` of bag_sgemm_ex / _batched / _noalloc, bag_workspace_create_ex and
+ * bag_plan_dump: choose the recursion depth from the shape and the calling
+ * thread's math mode (3XTF32: leaves of at least 8192; FFMA: depth 3 from
+ * 16384, 2 from 2048, 1 from 1024).  New; the reference takes explicit levels. */
+enum { BAG_DEPTH_AUTO = -1 };
 /* Leaf arithmetic (bag_set_math_mode).  FFMA: every output a sequential fmaf
  * chain, the reference's SIMT numerics.  3XTF32: tcgen05 tensor cores on
  * hi/lo TF32 splits (hi*hi + hi*lo + lo*hi) with 32-long K chunks summed in
@@ -92,7 +97,8 @@ bag_status bag_matmul(const float* a, const float* b, float* c, int n, bag_strea
                       bag_workspace* ws, int backend, int schedule);
 
 /* C <- A B + beta C (beta 0 or 1) for any m, n, k >= 0.  depth 0 is a plain
- * GEMM through the same kernel; ragged extents are peeled into plain strips.
+ * GEMM through the same kernel, BAG_DEPTH_AUTO picks one; ragged extents are
+ * peeled into plain strips.
  * ws may be NULL when the plan needs no workspace (Minimal basis, depth <= 1). */
 bag_status bag_sgemm_ex(int layout, int m, int n, int k, const float* a, long long lda,
                         const float* b, long long ldb, float* c, long long ldc, float beta,

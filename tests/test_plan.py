@@ -93,3 +93,19 @@ def test_plan_workspace_alignment(bag):
         for job in stage:
             for ref in job["out"]:
                 assert ref[0] == 3 and ref[1] % 64 == 0 and ref[2] % 4 == 0
+
+
+@pytest.mark.parametrize("mode,n,leaf", [("3xtf32", 4096, 4096), ("3xtf32", 8192, 8192),
+                                         ("3xtf32", 16384, 8192), ("3xtf32", 32768, 8192),
+                                         ("ffma", 4096, 1024), ("ffma", 8192, 2048),
+                                         ("ffma", 16384, 2048), ("ffma", 512, 512)])
+def test_auto_depth_follows_the_measured_policy(built_lib, mode, n, leaf):
+    import bag_b200 as bag
+    bag.set_math_mode(mode)
+    try:
+        pl = bag.plan_dump(n, n, n, n, n, n, "auto", "minimal")
+    finally:
+        bag.set_math_mode("ffma")
+    assert {l["m"] for l in pl["leaves"]} == {leaf}
+    depth = (n // leaf).bit_length() - 1
+    assert len(pl["leaves"]) == 7 ** depth
