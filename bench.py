@@ -48,6 +48,27 @@ SEED = 2
 METRIC = "effective FP32 TFLOP/s (2MNK/t) at N=16384 vs cuBLAS SGEMM, 1/2/4/8 B200"
 WORKLOAD = ("cfg3: C=A@B FP32, M=N=K=16384 row-major, A,B ~ N(0,1) from default_rng(2), "
             "BAG depth 2 (49 leaf products of 4096^3), Minimal basis, C+=A@B per step")
+# The BASELINE configs (A drawn before B from numpy.random.default_rng(seed),
+# row-major).  cfg3 is the headline; the others are reproducible with --config.
+CONFIGS = {
+    "cfg1": dict(m=512, n=512, k=512, batch=1, depth=1, dist=("uniform", -1.0, 1.0), seed=0,
+                 workload="cfg1: C=A@B FP32, M=N=K=512 row-major, A,B ~ U[-1,1) from "
+                          "default_rng(0), BAG depth 1"),
+    "cfg2": dict(m=4096, n=4096, k=4096, batch=1, depth=2, dist=("uniform", -1.0, 1.0), seed=1,
+                 workload="cfg2: C=A@B FP32, M=N=K=4096 row-major, A,B ~ U[-1,1) from "
+                          "default_rng(1), BAG depth 2 (--depth 1: one level)"),
+    "cfg3": dict(m=SIZE, n=SIZE, k=SIZE, batch=1, depth=DEPTH, dist=("normal",), seed=SEED,
+                 workload=WORKLOAD),
+    "cfg4a": dict(m=8192, n=4096, k=16384, batch=1, depth=1, dist=("uniform", -1.0, 1.0), seed=3,
+                  workload="cfg4a: C=A@B FP32, M=8192 K=16384 N=4096 row-major, A,B ~ U[-1,1) "
+                           "from default_rng(3), BAG depth 1"),
+    "cfg4b": dict(m=10000, n=10000, k=10000, batch=1, depth=1, dist=("uniform", -1.0, 1.0), seed=3,
+                  workload="cfg4b: C=A@B FP32, M=N=K=10000 row-major (peeled), A,B ~ U[-1,1) "
+                           "from default_rng(3), BAG depth 1"),
+    "cfg5": dict(m=2048, n=2048, k=2048, batch=64, depth=1, dist=("uniform", 0.0, 1.0), seed=4,
+                 workload="cfg5: 64 independent C=A@B FP32, 2048^3 row-major, A,B ~ U[0,1) from "
+                          "default_rng(4), BAG depth 1 per problem, batch split over GPUs"),
+}
 CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -59,25 +80,40 @@ def parse_args():
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["bag", "reference"], default="bag")
-    p.add_argument("--size", type=int, default=SIZE)
-    p.add_argument("--depth", type=int, default=DEPTH)
+    p.add_argument("--config", default="cfg3", choices=sorted(CONFIGS))
+    p.add_argument("--size", type=int, default=None, help="square size (default: the config's)")
+    p.add_argument("--depth", type=int, default=None, help="BAG depth (default: the config's)")
     p.add_argument("--basis", default="minimal", choices=["minimal", "full", "classic"])
     p.add_argument("--math", default="3xtf32", choices=["3xtf32", "ffma"])
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU time of the bounded CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-comparators", action="store_true")
-    return p.parse_args()
+    args = p.parse_args()
+    cfg = dict(CONFIGS[args.config])
+    if args.size is not None:
+        cfg.update(m=args.size, n=args.size, k=args.size)
+    if args.depth is not None:
+        cfg["depth"] = args.depth
+    args.cfg = cfg
+    args.depth = cfg["depth"]
+    return args
 
 
 # ---------------------------------------------------------------------------
 # Inputs.
 # ---------------------------------------------------------------------------
 
-def make_inputs(size: int) -> tuple[np.ndarray, np.ndarray]:
-    rng = np.random.default_rng(SEED)
-    a = rng.standard_normal((size, size), dtype=np.float32)
-    b = rng.standard_normal((size, size), dtype=np.float32)
+def make_inputs(cfg: dict) -> tuple[np.ndarray, np.ndarray]:
+    """A (batch x) M x K then B (batch x) K x N from default_rng(seed)."""
+    rng = np.random.default_rng(cfg["seed"])
+    lead = (cfg["batch"],) if cfg["batch"] > 1 else ()
+    shapes = (lead + (cfg["m"], cfg["k"]), lead + (cfg["k"], cfg["n"]))
+    if cfg["dist"][0] == "normal":
+        a, b = (rng.standard_normal(shp, dtype=np.float32) for shp in shapes)
+    else:
+        lo, hi = cfg["dist"][1:]
+        a, b = (rng.uniform(lo, hi, shp).astype(np.float32) for shp in shapes)
     return a, b
 
 
@@ -186,58 +222,76 @@ def cpu_threads() -> int:
     return os.cpu_count() or 1
 
 
-def cpu_sample(a: np.ndarray, b: np.ndarray, depth: int, basis: str, rows: int) -> tuple[float, float]:
-    """Run the oracle BAG on `rows` band rows of A (all of B); returns (seconds, flops)."""
+def cpu_sample(a: np.ndarray, b: np.ndarray, depth: int, basis: str, units: int) -> tuple[float, float]:
+    """Run the oracle BAG on `units` band rows of A with all of B (one problem) or
+    on the first `units` problems (a batch); returns (seconds, flops)."""
     from oracle import bag_oracle as O
-    idx = band_rows(a.shape[0], depth, a.shape[0] // rows, 0)
+    if a.ndim == 3:
+        t0 = time.perf_counter()
+        for i in range(units):
+            O.bag_product(a[i], b[i], depth, basis)
+        dt = time.perf_counter() - t0
+        return dt, 2.0 * units * a.shape[1] * a.shape[2] * b.shape[2]
+    idx = band_rows(a.shape[0], depth, a.shape[0] // units, 0)
     a_s = np.ascontiguousarray(a[idx])
     t0 = time.perf_counter()
     O.bag_product(a_s, b, depth, basis)
     dt = time.perf_counter() - t0
-    return dt, 2.0 * rows * b.shape[0] * b.shape[1]
+    return dt, 2.0 * idx.size * b.shape[0] * b.shape[1]
+
+
+def _sample_units(a: np.ndarray, depth: int) -> tuple[int, int]:
+    """(first sample size, largest) in rows or problems."""
+    if a.ndim == 3:
+        return 1, a.shape[0]
+    return max(a.shape[0] // 64, 16 << depth), a.shape[0]
+
+
+def _describe_sample(a, b, units, depth, basis, dt) -> str:
+    what = (f"{units} of the {a.shape[0]} {a.shape[1]}x{a.shape[2]}x{b.shape[2]} problems"
+            if a.ndim == 3 else
+            f"a {units}x{a.shape[1]} row-band shard of A times all of B ({b.shape[0]}x{b.shape[1]})")
+    return (f"oracle/bag_oracle.py bag_product (numpy FP32, OpenBLAS leaves) on {what}, "
+            f"depth {depth}, {basis} basis: {dt:.2f} s")
 
 
 def cpu_baseline(a, b, depth, basis, target_s: float) -> dict:
-    size = a.shape[0]
-    rows = max(size // 64, 16 << depth)
-    dt, flops = cpu_sample(a, b, depth, basis, rows)
-    while dt < target_s / 3 and rows * 2 <= size:
-        rows *= 2
-        dt, flops = cpu_sample(a, b, depth, basis, rows)
+    units, top = _sample_units(a, depth)
+    dt, flops = cpu_sample(a, b, depth, basis, units)
+    while dt < target_s / 3 and units * 2 <= top:
+        units *= 2
+        dt, flops = cpu_sample(a, b, depth, basis, units)
     return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
-            "sample": f"oracle/bag_oracle.py bag_product (numpy FP32, OpenBLAS leaves) on a "
-                      f"{rows}x{size} row-band shard of A times all of B ({size}x{size}), "
-                      f"depth {depth}, {basis} basis: {dt:.2f} s"}
+            "sample": _describe_sample(a, b, units, depth, basis, dt)}
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    a, b = make_inputs(args.size)
-    size, depth = args.size, args.depth
-    rows = max(size // 64, 16 << depth)
-    dt, _ = cpu_sample(a, b, depth, args.basis, rows)
-    while dt < args.cpu_seconds / 3 and rows * 2 <= size:
-        rows *= 2
-        dt, _ = cpu_sample(a, b, depth, args.basis, rows)
+    a, b = make_inputs(args.cfg)
+    depth = args.depth
+    units, top = _sample_units(a, depth)
+    dt, _ = cpu_sample(a, b, depth, args.basis, units)
+    while dt < args.cpu_seconds / 3 and units * 2 <= top:
+        units *= 2
+        dt, _ = cpu_sample(a, b, depth, args.basis, units)
     for _ in range(args.warmup):
-        cpu_sample(a, b, depth, args.basis, rows)
+        cpu_sample(a, b, depth, args.basis, units)
     times = []
     flops = 0.0
     for _ in range(args.steps):
-        dt, flops = cpu_sample(a, b, depth, args.basis, rows)
+        dt, flops = cpu_sample(a, b, depth, args.basis, units)
         times.append(dt)
     step = sum(times) / len(times)
     value = flops / step / 1e12
     base = {"value": value, "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
-            "sample": f"oracle/bag_oracle.py bag_product (numpy FP32, OpenBLAS leaves) on a "
-                      f"{rows}x{size} row-band shard of A times all of B, depth {depth}"}
+            "sample": _describe_sample(a, b, units, depth, args.basis, step)}
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "sample_rows": rows, "depth": depth,
+            "config": {"workload": args.cfg["workload"], "sample_units": units, "depth": depth,
                        "basis": args.basis, "parallelism": "host threads (BLAS)"},
             "cpu_baseline": base,
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -268,31 +322,46 @@ def run_bag(args) -> None:
     torch.backends.cuda.matmul.allow_tf32 = False
     bag.set_math_mode(args.math)
 
-    size, depth = args.size, args.depth
+    cfg, depth = args.cfg, args.depth
+    M, N, K, batch = cfg["m"], cfg["n"], cfg["k"], cfg["batch"]
     gr, gc = shard_grid(world)
-    if size % ((4 << depth) * gr) or size % ((4 << depth) * gc):
-        raise SystemExit("size must split into aligned bands for this GPU count")
-    a_np, b_np = make_inputs(size)
-    rows = band_rows(size, depth, gr, rank // gc)
-    cols = band_rows(size, depth, gc, rank % gc)
-    mg, ng = rows.size, cols.size
-    a_shard = np.ascontiguousarray(a_np[rows])
-    b_shard = np.ascontiguousarray(b_np[:, cols]) if gc > 1 else b_np
+    a_np, b_np = make_inputs(cfg)
+    if batch > 1:
+        # A batch: every rank takes batch/world whole problems.
+        if batch % world:
+            raise SystemExit("the batch must split evenly over the GPUs")
+        nb = batch // world
+        a_shard = np.ascontiguousarray(a_np[rank * nb:(rank + 1) * nb])
+        b_shard = np.ascontiguousarray(b_np[rank * nb:(rank + 1) * nb])
+        mg, ng = M, N
+        parallelism = f"batch split, {nb} problems per GPU"
+    else:
+        if M % ((4 << depth) * gr) or N % ((4 << depth) * gc):
+            raise SystemExit("the problem must split into aligned bands for this GPU count")
+        nb = 1
+        rows = band_rows(M, depth, gr, rank // gc)
+        cols = band_rows(N, depth, gc, rank % gc)
+        mg, ng = rows.size, cols.size
+        a_shard = np.ascontiguousarray(a_np[rows]) if gr > 1 else a_np
+        b_shard = np.ascontiguousarray(b_np[:, cols]) if gc > 1 else b_np
+        parallelism = f"{gr}x{gc} grid of row/column-band shards"
+    lead = (nb,) if batch > 1 else ()
 
     # Pinned host buffers (the e2e inputs) and device buffers (the value inputs).
     a_host = torch.from_numpy(a_shard).pin_memory()
     b_host = torch.from_numpy(b_shard).pin_memory()
-    c_host = torch.empty((mg, ng), dtype=torch.float32).pin_memory()
+    c_host = torch.empty(lead + (mg, ng), dtype=torch.float32).pin_memory()
     a_dev = a_host.to(device)
     b_dev = b_host.to(device)
-    c_dev = torch.zeros((mg, ng), dtype=torch.float32, device=device)
+    c_dev = torch.zeros(lead + (mg, ng), dtype=torch.float32, device=device)
     del a_np
     # Row-major C(mg x ng) = A B is the column-major ng x mg problem.
-    ws = bag.Workspace.for_problem(ng, mg, size, depth, args.basis)
+    ws = bag.Workspace.for_problem(ng, mg, K, depth, args.basis, batch=nb)
     stream = torch.cuda.current_stream()
+    gemm = bag.sgemm_batched if batch > 1 else bag.sgemm
 
     def step():
-        bag.sgemm(a_dev, b_dev, c_dev, beta=1.0, depth=depth, basis=args.basis, workspace=ws)
+        gemm(a_dev, b_dev, c_dev, beta=1.0, depth=depth, basis=args.basis, workspace=ws)
 
     def barrier():
         if world > 1:
@@ -325,15 +394,28 @@ def run_bag(args) -> None:
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
+    # Inputs smaller than twice the 126 MB L2 (cfg1, cfg2) get an L2 flush
+    # (a 256 MiB write) before every timed step, outside its events; larger
+    # ones are timed back to back.
+    input_bytes = 4 * (a_shard.size + b_shard.size)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=device) if input_bytes < (256 << 20) \
+        else None
     launches0 = bag.launch_count()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    step_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
     with ClockSampler(local) as clocks:
         time.sleep(0.15)   # let the sampler start before the timed region
         host0 = time.time()
         t_start.record()
         for i in range(args.steps):
+            if flush is not None:
+                flush.fill_(float(i))
+                step_events[i][0].record()
             bag.profile_events(*pairs[i])
             step()
+            if flush is not None:
+                step_events[i][1].record()
         bag.profile_events(None, None)
         t_end.record()
         torch.cuda.synchronize()
@@ -342,12 +424,19 @@ def run_bag(args) -> None:
     barrier()
     launches = reduce_sum(bag.launch_count() - launches0)
     leaf_path = bag.last_leaf_path()
-    ms = reduce_max(t_start.elapsed_time(t_end)) / args.steps
+    if flush is not None:
+        ms = reduce_max(sum(s0.elapsed_time(s1) for s0, s1 in step_events)) / args.steps
+        l2_note = "inputs smaller than L2: a 256 MiB buffer written before each timed step"
+    else:
+        ms = reduce_max(t_start.elapsed_time(t_end)) / args.steps
+        l2_note = f"inputs larger than L2 ({input_bytes / 2**30:.2f} GiB per GPU); no flush"
+    del flush
     leaf_ms = reduce_max(sum(s.elapsed_time(e) for s, e in pairs) / args.steps)
-    flops_total = 2.0 * size * size * size
+    flops_total = 2.0 * M * N * K * batch
     value = flops_total / (ms * 1e-3) / 1e12
-    # Executed leaf FLOPs of this rank's launch: 7^depth products of (mg/2^d)(ng/2^d)(K/2^d).
-    f_exec = 7 ** depth * 2.0 * (mg / 2 ** depth) * (ng / 2 ** depth) * (size / 2 ** depth)
+    # Executed leaf FLOPs of this rank's launch: nb x 7^depth products of
+    # (mg/2^d)(ng/2^d)(K/2^d) (ragged extents peel into strips of plain work).
+    f_exec = nb * 7 ** depth * 2.0 * (mg / 2 ** depth) * (ng / 2 ** depth) * (K / 2 ** depth)
     leaf_tflops = f_exec / (leaf_ms * 1e-3) / 1e12
 
     # FP32 FFMA peak: nominal at the max SM clock, and measured by the probe.
@@ -374,7 +463,7 @@ def run_bag(args) -> None:
     def e2e_step():
         a_dev.copy_(a_host, non_blocking=True)
         b_dev.copy_(b_host, non_blocking=True)
-        bag.sgemm(a_dev, b_dev, c_dev, beta=0.0, depth=depth, basis=args.basis, workspace=ws)
+        gemm(a_dev, b_dev, c_dev, beta=0.0, depth=depth, basis=args.basis, workspace=ws)
         c_host.copy_(c_dev, non_blocking=True)
 
     for _ in range(min(args.warmup, 2)):
@@ -390,8 +479,8 @@ def run_bag(args) -> None:
     torch.cuda.synchronize()
     barrier()
     e2e_ms = reduce_max(e0.elapsed_time(e1)) / args.steps
-    h2d = int(reduce_sum(4.0 * (mg * size + size * ng)))   # all ranks' shards
-    d2h = 4 * size * size
+    h2d = int(reduce_sum(4.0 * (a_shard.size + b_shard.size)))   # all ranks' shards
+    d2h = 4 * M * N * batch
 
     # Comparators: cuBLAS SGEMM (torch, IEEE FP32, no TF32) and this library's
     # FFMA path on the same inputs.
@@ -401,7 +490,7 @@ def run_bag(args) -> None:
         c_tmp = torch.zeros_like(c_dev)   # c_dev keeps the e2e result for the accuracy check
 
         def ffma_step():
-            bag.sgemm(a_dev, b_dev, c_tmp, beta=1.0, depth=depth, basis=args.basis, workspace=ws)
+            gemm(a_dev, b_dev, c_tmp, beta=1.0, depth=depth, basis=args.basis, workspace=ws)
 
         for _ in range(2):
             ffma_step()
@@ -419,21 +508,28 @@ def run_bag(args) -> None:
                                         "how": "same call, bag_set_math_mode(BAG_MATH_FFMA)"}
         bag.set_math_mode(args.math)
     if rank == 0 and world == 1 and not args.no_comparators:
-        a_full = a_dev
-        c_cmp = torch.zeros((size, size), dtype=torch.float32, device=device)
+        c_cmp = torch.zeros_like(c_dev)
+
+        def cublas_step():
+            if batch > 1:
+                c_cmp.baddbmm_(a_dev, b_dev)
+            else:
+                c_cmp.addmm_(a_dev, b_dev)
+
         for _ in range(2):
-            c_cmp.addmm_(a_full, b_dev)
+            cublas_step()
         torch.cuda.synchronize()
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         c0.record()
         for _ in range(args.steps):
-            c_cmp.addmm_(a_full, b_dev)
+            cublas_step()
         c1.record()
         torch.cuda.synchronize()
         cms = c0.elapsed_time(c1) / args.steps
         comparators["cublas_sgemm_fp32"] = {"tflops": flops_total / (cms * 1e-3) / 1e12,
                                             "ms_per_step": cms,
-                                            "how": "torch addmm_, allow_tf32=False (cuBLAS FP32)"}
+                                            "how": "torch addmm_/baddbmm_, allow_tf32=False "
+                                                   "(cuBLAS FP32)"}
         del c_cmp
 
     # Accuracy of this run's result (the last e2e step computed C = A@B once)
@@ -446,21 +542,24 @@ def run_bag(args) -> None:
         if leaf_path != "ffma":
             bag.set_math_mode("ffma")
             c_ffma = torch.zeros_like(c_dev)
-            bag.sgemm(a_dev, b_dev, c_ffma, beta=0.0, depth=depth, basis=args.basis, workspace=ws)
+            gemm(a_dev, b_dev, c_ffma, beta=0.0, depth=depth, basis=args.basis, workspace=ws)
             bag.set_math_mode(args.math)
-        # FP64 reference on the GPU (cuBLAS DGEMM), column panels to bound memory.
+        # FP64 reference on the GPU (cuBLAS DGEMM), per problem in column panels.
         panel = 2048
         num = num_f = den = 0.0
-        a64 = a_dev.double()
-        for j in range(0, size, panel):
-            ref = a64 @ b_dev[:, j:j + panel].double()
-            diff = c[:, j:j + panel].double() - ref
-            num += float((diff * diff).sum())
-            den += float((ref * ref).sum())
-            if c_ffma is not None:
-                diff = c_ffma[:, j:j + panel].double() - ref
-                num_f += float((diff * diff).sum())
-        del a64
+        for i in range(nb):
+            ai, bi, ci = (a_dev[i], b_dev[i], c[i]) if batch > 1 else (a_dev, b_dev, c)
+            fi = None if c_ffma is None else (c_ffma[i] if batch > 1 else c_ffma)
+            a64 = ai.double()
+            for j in range(0, ng, panel):
+                ref = a64 @ bi[:, j:j + panel].double()
+                diff = ci[:, j:j + panel].double() - ref
+                num += float((diff * diff).sum())
+                den += float((ref * ref).sum())
+                if fi is not None:
+                    diff = fi[:, j:j + panel].double() - ref
+                    num_f += float((diff * diff).sum())
+            del a64
         accuracy = {"rel_frobenius_vs_fp64": (num / den) ** 0.5}
         if c_ffma is not None:
             ffma_err = (num_f / den) ** 0.5
@@ -510,11 +609,10 @@ def run_bag(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "M": size, "N": size, "K": size, "depth": depth,
-                       "basis": args.basis, "layout": "row-major", "leaf_math": leaf_path,
-                       "l2": "inputs larger than L2 (1 GiB each); no flush",
-                       "parallelism": f"{gr}x{gc} grid of row/column-band shards" if world > 1
-                       else "single GPU"},
+            "config": {"workload": cfg["workload"], "M": M, "N": N, "K": K, "batch": batch,
+                       "depth": depth, "basis": args.basis, "layout": "row-major",
+                       "leaf_math": leaf_path, "l2": l2_note,
+                       "parallelism": parallelism if world > 1 else "single GPU"},
             "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "roofline": roofline,
