@@ -5,7 +5,8 @@ Workload: C = A @ B, FP32, M=N=K=16384, row-major, A then B
 drawn N(0,1) from ``numpy.random.default_rng(2)``, two BAG recursion levels
 (49 leaf products of 4096^3), Minimal basis.  A step is one
 ``C <- A@B + C`` call; inputs are 1 GiB each, larger than the 126 MB L2, so no
-flush is needed between steps.  The leaf arithmetic is ``--math``: 3xTF32
+flush is needed between steps (``--config`` selects the other BASELINE
+configs; those smaller than L2 are flushed).  The leaf arithmetic is ``--math``: 3xTF32
 (default; tcgen05 tensor cores on hi/lo TF32 splits with FP32-folded chunks,
 checked in the same run to stay within 1.25x the FFMA path's error, the
 reference's numerics) or ffma (sequential FP32 fmaf chains, SIMT).
@@ -459,26 +460,57 @@ def run_bag(args) -> None:
     torch.cuda.synchronize()
     probe = fl.value / (p0.elapsed_time(p1) * 1e-3) / 1e12
 
-    # End to end through the public API, host buffers in and out.
-    def e2e_step():
-        a_dev.copy_(a_host, non_blocking=True)
-        b_dev.copy_(b_host, non_blocking=True)
-        gemm(a_dev, b_dev, c_dev, beta=0.0, depth=depth, basis=args.basis, workspace=ws)
-        c_host.copy_(c_dev, non_blocking=True)
+    # End to end through the public API, host buffers in and out, pipelined
+    # like a serving loop: step i+1's inputs are uploaded on one copy stream
+    # while step i computes, and step i's C is read back on another while
+    # step i+1 computes (two device and two pinned-host buffer sets).  Every
+    # step still moves its own inputs host->device and its result back.
+    comp = torch.cuda.current_stream()
+    h2d_s, d2h_s = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    a2 = [a_dev, torch.empty_like(a_dev)]
+    b2 = [b_dev, torch.empty_like(b_dev)]
+    c2 = [c_dev, torch.empty_like(c_dev)]
+    ch2 = [c_host, torch.empty(c_host.shape, dtype=torch.float32, pin_memory=True)]
+    up_done = [torch.cuda.Event(), torch.cuda.Event()]
+    comp_done = [torch.cuda.Event(), torch.cuda.Event()]
+    down_done = [torch.cuda.Event(), torch.cuda.Event()]
 
-    for _ in range(min(args.warmup, 2)):
-        e2e_step()
+    def e2e_run(steps: int, start_event=None) -> int:
+        if start_event is not None:
+            h2d_s.wait_event(start_event)
+        for i in range(steps):
+            sl = i % 2
+            with torch.cuda.stream(h2d_s):
+                if i >= 2:
+                    h2d_s.wait_event(comp_done[sl])   # step i-2 no longer reads slot sl
+                a2[sl].copy_(a_host, non_blocking=True)
+                b2[sl].copy_(b_host, non_blocking=True)
+                up_done[sl].record(h2d_s)
+            comp.wait_event(up_done[sl])
+            if i >= 2:
+                comp.wait_event(down_done[sl])        # step i-2's C has been read back
+            gemm(a2[sl], b2[sl], c2[sl], beta=0.0, depth=depth, basis=args.basis, workspace=ws)
+            comp_done[sl].record(comp)
+            with torch.cuda.stream(d2h_s):
+                d2h_s.wait_event(comp_done[sl])
+                ch2[sl].copy_(c2[sl], non_blocking=True)
+                down_done[sl].record(d2h_s)
+        comp.wait_stream(h2d_s)
+        comp.wait_stream(d2h_s)
+        return (steps - 1) % 2
+
+    e2e_run(2)
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
+    e0.record(comp)
+    last = e2e_run(args.steps, start_event=e0)
+    e1.record(comp)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = reduce_max(e0.elapsed_time(e1)) / args.steps
+    c_res = c2[last]   # this run's final C = A@B, for the accuracy check
     h2d = int(reduce_sum(4.0 * (a_shard.size + b_shard.size)))   # all ranks' shards
     d2h = 4 * M * N * batch
 
@@ -537,7 +569,7 @@ def run_bag(args) -> None:
     # on the same inputs at the same depth: the bound is <= 1.25x that and <= 1e-4.
     accuracy = {}
     if rank == 0 and world == 1:
-        c = c_dev
+        c = c_res
         c_ffma = None
         if leaf_path != "ffma":
             bag.set_math_mode("ffma")
@@ -614,7 +646,9 @@ def run_bag(args) -> None:
                        "leaf_math": leaf_path, "l2": l2_note,
                        "parallelism": parallelism if world > 1 else "single GPU"},
             "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                    "how": "public sgemm API from pinned host buffers; uploads of step i+1 and "
+                           "the read-back of step i overlap step i's compute (2 buffer sets)"},
             "roofline": roofline,
             "ffma_probe_tflops": probe,
             "clocks": {k: csum[k] for k in ("sm_mhz", "sm_max_mhz", "reasons",
