@@ -27,7 +27,7 @@ from typing import NamedTuple, Optional
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libbag_b200.so")
 
-BASIS = {"minimal": 0, "full": 1, "classic": 2}
+BASIS = {"minimal": 0, "full": 1, "classic": 2, "winograd": 3}
 SCHEDULE = {"serial": 0, "seven": 1, "seven-stream": 1, "batched": 2}
 LAYOUT = {"col": 0, "row": 1}
 

@@ -130,7 +130,16 @@ struct HostJob {
   std::vector<std::vector<int>> expr;   // signed (input index + 1)
 };
 
-enum BasisKind { kMinimal = BAG_BASIS_MINIMAL, kFull = BAG_BASIS_FULL, kClassic = BAG_BASIS_CLASSIC };
+enum BasisKind {
+  kMinimal = BAG_BASIS_MINIMAL,
+  kFull = BAG_BASIS_FULL,
+  kClassic = BAG_BASIS_CLASSIC,
+  kWinograd = BAG_BASIS_WINOGRAD
+};
+
+bool known_basis(int basis) {
+  return basis == kMinimal || basis == kFull || basis == kClassic || basis == kWinograd;
+}
 
 // One level of each algorithm: operand combinations over quadrants
 // (0=X11, 1=X12, 2=X21, 3=X22) as ordered signed terms, and the signed C
@@ -180,6 +189,23 @@ const LevelProduct kClassic7[7] = {
     {{1, {0}, {1}}, {2, {1, 3}, {1, -1}}, {0, 1, 0, 1}},
     {{1, {3}, {1}}, {2, {2, 0}, {1, -1}}, {1, 0, 1, 0}},
     {{2, {0, 3}, {1, 1}}, {2, {0, 3}, {1, 1}}, {1, 0, 0, 1}},
+};
+
+// Strassen-Winograd, the 15-addition form (Winograd 1971): with
+// S1 = A21+A22, S2 = S1-A11, S3 = A11-A21, S4 = A12-S2 and T1 = B12-B11,
+// T2 = B22-T1, T3 = B22-B12, T4 = T2-B21, the products M1 = A11 B11,
+// M2 = A12 B21, M3 = S4 B22, M4 = A22 T4, M5 = S1 T1, M6 = S2 T2, M7 = S3 T3
+// give C11 = M1+M2, C12 = M1+M6+M5+M3, C21 = M1+M6+M7-M4, C22 = M1+M6+M7+M5.
+// Operands are written as flat signed sums in the order the intermediates
+// form them; outputs by direct decode.
+const LevelProduct kWinograd7[7] = {
+    {{1, {0}, {1}}, {1, {0}, {1}}, {1, 1, 1, 1}},                                  // M1
+    {{1, {1}, {1}}, {1, {2}, {1}}, {1, 0, 0, 0}},                                  // M2
+    {{4, {1, 2, 3, 0}, {1, -1, -1, 1}}, {1, {3}, {1}}, {0, 1, 0, 0}},              // M3
+    {{1, {3}, {1}}, {4, {3, 1, 0, 2}, {1, -1, 1, -1}}, {0, 0, -1, 0}},             // M4
+    {{2, {2, 3}, {1, 1}}, {2, {1, 0}, {1, -1}}, {0, 1, 0, 1}},                     // M5
+    {{3, {2, 3, 0}, {1, 1, -1}}, {3, {3, 1, 0}, {1, -1, 1}}, {0, 1, 1, 1}},        // M6
+    {{2, {0, 2}, {1, -1}}, {2, {3, 1}, {1, -1}}, {0, 0, 1, 1}},                    // M7
 };
 
 struct Builder {
@@ -346,7 +372,10 @@ struct Builder {
     quads(lv, m, k, lq);
     quads(rv, k, n, rq);
     const int h = m / 2, kk = k / 2, w = n / 2;
-    const LevelProduct* table = basis == kFull ? kFull7 : basis == kClassic ? kClassic7 : kMinimal7;
+    const LevelProduct* table = basis == kFull       ? kFull7
+                                : basis == kClassic  ? kClassic7
+                                : basis == kWinograd ? kWinograd7
+                                                     : kMinimal7;
     if (basis == kFull) {
       View lt[4], rt[4];
       full_transform(lq, h, kk, lt);
@@ -693,8 +722,7 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
   if (g.m < 0 || g.n < 0 || g.k < 0) fail(BAG_ERR_SHAPE, "negative extent");
   g.depth = resolve_depth(g.depth, g.m, g.n, g.k);
   if (g.depth < 0 || g.depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8 or BAG_DEPTH_AUTO");
-  if (g.basis != kMinimal && g.basis != kFull && g.basis != kClassic)
-    fail(BAG_ERR_INVALID, "unknown basis");
+  if (!known_basis(g.basis)) fail(BAG_ERR_INVALID, "unknown basis");
   if (beta != 0.f && beta != 1.f) fail(BAG_ERR_UNSUPPORTED, "beta must be 0 or 1");
   if (g.batch < 0) fail(BAG_ERR_INVALID, "negative batch");
   if (g.m == 0 || g.n == 0 || g.batch == 0) return;
@@ -896,7 +924,7 @@ bag_status bag_workspace_create_ex(int m, int n, int k, int depth, int basis, in
     if (m < 0 || n < 0 || k < 0 || batch < 0) fail(BAG_ERR_SHAPE, "negative extent");
     depth = resolve_depth(depth, m, n, k);
     if (depth < 0 || depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8 or BAG_DEPTH_AUTO");
-    if (basis != kMinimal && basis != kFull && basis != kClassic) fail(BAG_ERR_INVALID, "unknown basis");
+    if (!known_basis(basis)) fail(BAG_ERR_INVALID, "unknown basis");
     GemmDesc g{m, n, k, nullptr, std::max(1, m), 0, nullptr, std::max(1, k), 0, nullptr,
                std::max(1, m), 0, std::max(batch, 1), depth, basis};
     // Sized for the calling thread's math mode (3xTF32 adds the prepared
@@ -1043,8 +1071,7 @@ bag_status sgemm_with_scratch(int layout, int m, int n, int k, const float* a, l
     if (g.m < 0 || g.n < 0 || g.k < 0) fail(BAG_ERR_SHAPE, "negative extent");
     g.depth = resolve_depth(g.depth, g.m, g.n, g.k);
     if (g.depth < 0 || g.depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8 or BAG_DEPTH_AUTO");
-    if (g.basis != kMinimal && g.basis != kFull && g.basis != kClassic)
-      fail(BAG_ERR_INVALID, "unknown basis");
+    if (!known_basis(g.basis)) fail(BAG_ERR_INVALID, "unknown basis");
     const size_t need = (g.m > 0 && g.n > 0 && g.k > 0) ? plan_workspace_elements(g) : 0;
     if (need > scratch_elements)
       fail(BAG_ERR_WORKSPACE,
@@ -1184,7 +1211,7 @@ bag_status bag_plan_dump(int m, int n, int k, long long lda, long long ldb, long
     if (m < 0 || n < 0 || k < 0) fail(BAG_ERR_SHAPE, "negative extent");
     depth = resolve_depth(depth, m, n, k);
     if (depth < 0 || depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8 or BAG_DEPTH_AUTO");
-    if (basis != kMinimal && basis != kFull && basis != kClassic) fail(BAG_ERR_INVALID, "unknown basis");
+    if (!known_basis(basis)) fail(BAG_ERR_INVALID, "unknown basis");
     const std::string s = dump_plan(m, n, k, lda, ldb, ldc, depth, basis);
     if (needed) *needed = s.size() + 1;
     if (buf && buflen) {

@@ -84,7 +84,7 @@ def parse_args():
     p.add_argument("--config", default="cfg3", choices=sorted(CONFIGS))
     p.add_argument("--size", type=int, default=None, help="square size (default: the config's)")
     p.add_argument("--depth", type=int, default=None, help="BAG depth (default: the config's)")
-    p.add_argument("--basis", default="minimal", choices=["minimal", "full", "classic"])
+    p.add_argument("--basis", default="minimal", choices=["minimal", "full", "classic", "winograd"])
     p.add_argument("--math", default="3xtf32", choices=["3xtf32", "ffma"])
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU time of the bounded CPU-baseline sample")

@@ -43,8 +43,9 @@ typedef enum bag_status {
 } bag_status;
 
 /* Basis descriptors, bag.cuh:7 (Minimal, Full); CLASSIC is Strassen-1969
- * (strassen.cuh:131-153) run through the same recursion. */
-enum { BAG_BASIS_MINIMAL = 0, BAG_BASIS_FULL = 1, BAG_BASIS_CLASSIC = 2 };
+ * (strassen.cuh:131-153) run through the same recursion; WINOGRAD is the
+ * 15-addition Strassen-Winograd variant (new; no reference counterpart). */
+enum { BAG_BASIS_MINIMAL = 0, BAG_BASIS_FULL = 1, BAG_BASIS_CLASSIC = 2, BAG_BASIS_WINOGRAD = 3 };
 /* bag_cuda::Schedule, bag.cuh:8.  Every schedule runs as one grouped launch on
  * the caller stream here; the value is validated and otherwise a hint. */
 enum { BAG_SCHEDULE_SERIAL = 0, BAG_SCHEDULE_SEVEN_STREAM = 1, BAG_SCHEDULE_BATCHED = 2 };

@@ -261,6 +261,53 @@ def strassen_one_level(a: np.ndarray, b: np.ndarray, c: np.ndarray | None = None
     return out
 
 
+def winograd_product(a: np.ndarray, b: np.ndarray, depth: int) -> np.ndarray:
+    """``A@B`` by ``depth`` levels of Strassen-Winograd, the published
+    15-addition form (S. Winograd 1971; e.g. Boyer et al. 2009, Table 1):
+
+    S1 = A21+A22, S2 = S1-A11, S3 = A11-A21, S4 = A12-S2,
+    T1 = B12-B11, T2 = B22-T1, T3 = B22-B12, T4 = T2-B21,
+    M1 = A11 B11, M2 = A12 B21, M3 = S4 B22, M4 = A22 T4, M5 = S1 T1,
+    M6 = S2 T2, M7 = S3 T3, U2 = M1+M6, U3 = U2+M7, U4 = U2+M5,
+    C11 = M1+M2, C12 = U4+M3, C21 = U3-M4, C22 = U3+M5,
+
+    each intermediate rounded to FP32, leaves by numpy FP32 GEMM.  The
+    reference has no Winograd variant; this is the checker for this build's
+    ``BAG_BASIS_WINOGRAD``.
+    """
+    a = a.astype(F32)
+    b = b.astype(F32)
+    if depth == 0:
+        return _mm32(a, b)
+    m, k = a.shape
+    n = b.shape[1]
+    if m % 2 or k % 2 or n % 2:
+        raise ValueError("each level needs even extents")
+    a11, a12, a21, a22 = quadrants(a)
+    b11, b12, b21, b22 = quadrants(b)
+    s1 = (a21 + a22).astype(F32)
+    s2 = (s1 - a11).astype(F32)
+    s3 = (a11 - a21).astype(F32)
+    s4 = (a12 - s2).astype(F32)
+    t1 = (b12 - b11).astype(F32)
+    t2 = (b22 - t1).astype(F32)
+    t3 = (b22 - b12).astype(F32)
+    t4 = (t2 - b21).astype(F32)
+    mm = lambda x, y: winograd_product(x, y, depth - 1)  # noqa: E731
+    m1, m2, m3, m4 = mm(a11, b11), mm(a12, b21), mm(s4, b22), mm(a22, t4)
+    m5, m6, m7 = mm(s1, t1), mm(s2, t2), mm(s3, t3)
+    u2 = (m1 + m6).astype(F32)
+    u3 = (u2 + m7).astype(F32)
+    u4 = (u2 + m5).astype(F32)
+    out = np.empty((m, n), F32)
+    h, w = m // 2, n // 2
+    out[:h, :w] = m1 + m2
+    out[:h, w:] = u4 + m3
+    out[h:, :w] = u3 - m4
+    out[h:, w:] = u3 + m5
+    return out
+
+
 def primitive(x, y, v, w, d, e, *, delta: int, eps: int, gamma_d: int, gamma_e: int):
     """The BAG primitive on numpy arrays, returning new (d, e).
 

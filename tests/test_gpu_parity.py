@@ -412,3 +412,27 @@ def test_no_bounded_wait_timed_out(bag, torch_mod):
     torch = torch_mod
     torch.cuda.synchronize()
     assert bag.device_error() == 0
+
+
+# ---------------------------------------------------------------------------
+# Strassen-Winograd (15 additions), this build's extra basis.
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("n,depth", [(256, 1), (512, 2), (1000, 1)])
+def test_winograd_basis_matches_its_oracle(bag, torch_mod, n, depth):
+    torch = torch_mod
+    rng = np.random.default_rng(n + depth)
+    a = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    b = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    ws = bag.Workspace.for_problem(n, n, n, depth, "winograd")
+    c = torch.zeros(n, n, device="cuda")
+    bag.sgemm(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda(), c, beta=0.0, depth=depth,
+              basis="winograd", workspace=ws)
+    torch.cuda.synchronize()
+    got = c.cpu().numpy()
+    exact = O.fp64_matmul(a, b)
+    # Peeled shapes (1000 = 992 + 8) run the peeling strips as plain products.
+    want = O.winograd_product(a, b, depth) if n % (4 << depth) == 0 else None
+    if want is not None:
+        assert O.rel_frobenius(got, want.astype(np.float64)) < 5e-6
+    assert O.rel_frobenius(got, exact) < 1e-5

@@ -137,7 +137,8 @@ def test_tensor_path_against_oracle(tensor_mode):
 @pytest.mark.parametrize("m,k,n,depth,basis", [
     (512, 2048, 768, 0, "minimal"), (1032, 4096, 2056, 2, "minimal"),
     (4096, 4096, 4096, 2, "minimal"), (2048, 4096, 2048, 2, "full"),
-    (2048, 2048, 2048, 1, "classic"), (1000, 2048, 1160, 1, "minimal")])
+    (2048, 2048, 2048, 1, "classic"), (1000, 2048, 1160, 1, "minimal"),
+    (2048, 4096, 2048, 2, "winograd")])
 def test_prepared_path(tensor_mode, m, k, n, depth, basis):
     import torch
     bag = tensor_mode

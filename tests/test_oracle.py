@@ -137,3 +137,12 @@ def test_config_inputs_are_seeded():
     assert a1.dtype == np.float32 and a1.min() >= -1 and a1.max() < 1
     a3, _ = O.config_inputs(8, 8, 8, 2, "normal")
     assert a3.dtype == np.float32
+
+
+def test_winograd_oracle_is_a_matmul():
+    rng = np.random.default_rng(5)
+    a = rng.uniform(-1, 1, (64, 96)).astype(np.float32)
+    b = rng.uniform(-1, 1, (96, 32)).astype(np.float32)
+    exact = O.fp64_matmul(a, b)
+    for depth in (1, 2, 3):
+        assert O.rel_frobenius(O.winograd_product(a, b, depth), exact) < 1e-5

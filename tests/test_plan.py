@@ -109,3 +109,14 @@ def test_auto_depth_follows_the_measured_policy(built_lib, mode, n, leaf):
     assert {l["m"] for l in pl["leaves"]} == {leaf}
     depth = (n // leaf).bit_length() - 1
     assert len(pl["leaves"]) == 7 ** depth
+
+
+def test_winograd_plan_has_the_15_addition_structure(built_lib):
+    import bag_b200 as bag
+    pl = bag.plan_dump(64, 64, 64, 64, 64, 64, 1, "winograd")
+    leaves = pl["leaves"]
+    assert len(leaves) == 7
+    # Operand term counts (S/T intermediates flattened) and C updates per product.
+    assert [(len(l["left"]), len(l["right"]), len(l["out"])) for l in leaves] == [
+        (1, 1, 4), (1, 1, 1), (4, 1, 1), (1, 4, 1), (2, 2, 2), (3, 3, 3), (2, 2, 2)]
+    assert len(bag.plan_dump(64, 64, 64, 64, 64, 64, 2, "winograd")["leaves"]) == 49
