@@ -84,8 +84,10 @@ SIGNATURES = {
     "bag_set_math_mode": (_I, [_I]),
     "bag_get_math_mode": (_I, []),
     "bag_last_leaf_path": (_I, []),
+    "bag_last_leaf_kernel": (_I, []),
 }
 MATH = {"ffma": 0, "3xtf32": 1}
+LEAF_KERNELS = {0: "ffma", 1: "tf32_fused", 2: "tf32_single", 3: "tf32_pair"}
 
 _lib = None
 
@@ -180,6 +182,14 @@ def get_math_mode() -> str:
 def last_leaf_path() -> str:
     """Leaf arithmetic ("ffma" or "3xtf32") the last call on this thread used."""
     return {v: k for k, v in MATH.items()}[int(lib().bag_last_leaf_path())]
+
+
+def last_leaf_kernel() -> str:
+    """Leaf kernel the last call on this thread ran: "ffma", "tf32_fused"
+    (transforms in the tensor kernel's prologue), "tf32_single" (prepared
+    operands, 128 x 256 tiles per SM) or "tf32_pair" (prepared operands,
+    256 x 128 tiles per cluster of two SMs)."""
+    return LEAF_KERNELS[int(lib().bag_last_leaf_kernel())]
 
 
 def device_error() -> int:

@@ -40,6 +40,8 @@ namespace {
 thread_local std::string g_last_error;
 thread_local int g_math_mode = BAG_MATH_FFMA;
 thread_local int g_last_leaf_path = BAG_MATH_FFMA;
+// Leaf kernel of the last call's prepared-operand path (BAG_LEAF_KERNEL_*).
+thread_local int g_last_prep_kind = -1;
 // Shortest leaf K the 3xTF32 path takes.  Its tensor-core partial sums carry a
 // fixed error of about 1.4e-7 (hi/lo split and round-toward-zero
 // accumulation within a 32-long chunk); an FP32 FFMA dot product's error grows
@@ -535,8 +537,14 @@ Term make_term(const View& v, float coef, int mode) {
 bool view_vec_ok(const View& v) { return aligned16(v.p) && v.ld % 4 == 0 && v.bstride % 4 == 0; }
 
 // 3xTF32 leaf products on prepared operands: the prepare pass, then the leaf
-// launches (CTA tile 128 x kPrepBN).
-constexpr int kPrepBN = 256;
+// launches -- 256 x 128 tiles on clusters of two SMs where the device
+// schedules them, else 128 x 256 tiles on one SM (BAG_B200_PREP_KERNEL=single
+// selects the latter for comparisons).
+int prep_leaf_kind() {
+  const char* env = std::getenv("BAG_B200_PREP_KERNEL");
+  if (env && std::strcmp(env, "single") == 0) return kPrepLeafSingle;
+  return prep_pair_supported() ? kPrepLeafPair : kPrepLeafSingle;
+}
 
 void run_prepared(Builder& B, int batch, cudaStream_t stream) {
   const int tile = prep_row_align();
@@ -567,7 +575,9 @@ void run_prepared(Builder& B, int batch, cudaStream_t stream) {
     ++g_launches;
   }
   if (g_prof_start) cuda_check(cudaEventRecord(g_prof_start, stream), "cudaEventRecord");
-  const TileShape ts = prep_tile_shape(kPrepBN);
+  const int kind = prep_leaf_kind();
+  g_last_prep_kind = kind;
+  const TileShape ts = prep_tile_shape(kind);
   size_t i = 0;
   while (i < B.leaves.size()) {
     PrepLeafPlan lp;
@@ -605,7 +615,7 @@ void run_prepared(Builder& B, int batch, cudaStream_t stream) {
       ++i;
     }
     if (lp.nprod == 0 && i < B.leaves.size()) fail(BAG_ERR_INTERNAL, "plan chunking failed");
-    cuda_check(launch_leaf_prep(lp, kPrepBN, B.prep_region.p, B.prep_row_len, B.prep_rows,
+    cuda_check(launch_leaf_prep(lp, kind, B.prep_region.p, B.prep_row_len, B.prep_rows,
                                 B.ws_bstride, batch, stream),
                "prepared leaf launch");
     if (lp.nprod) ++g_launches;
@@ -659,6 +669,7 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream,
   for (const HostLeaf& l : B.leaves)
     tensor = tensor && l.k >= kTcMinK && tc_supported(int(l.left.size()), int(l.right.size()));
   g_last_leaf_path = tensor ? BAG_MATH_3XTF32 : BAG_MATH_FFMA;
+  g_last_prep_kind = -1;
   if (tensor && !B.prep.empty() && prep_supported()) {
     run_prepared(B, batch, stream);
     return;
@@ -1183,6 +1194,13 @@ bag_status bag_set_math_mode(int mode) {
 
 int bag_get_math_mode(void) { return g_math_mode; }
 int bag_last_leaf_path(void) { return g_last_leaf_path; }
+
+int bag_last_leaf_kernel(void) {
+  if (g_last_leaf_path != BAG_MATH_3XTF32) return BAG_LEAF_KERNEL_FFMA;
+  if (g_last_prep_kind == kPrepLeafPair) return BAG_LEAF_KERNEL_TF32_PAIR;
+  if (g_last_prep_kind == kPrepLeafSingle) return BAG_LEAF_KERNEL_TF32_SINGLE;
+  return BAG_LEAF_KERNEL_TF32_FUSED;
+}
 
 bag_status bag_device_error(unsigned* code) {
   return guarded([&] {

@@ -60,13 +60,17 @@ cudaError_t read_and_clear_tc_device_error(unsigned* value);
 
 // Prepared-operand 3xTF32 path (bag_tc3_kernel.cu): prep_kernel writes each
 // leaf operand's TF32 hi/lo rows into a workspace region (rows of row_len k,
-// row_len a multiple of prep_row_align()); leaf_prep_kernel runs the products
-// on them with 128 x bn tiles (bn 128 or 256).
+// row_len a multiple of prep_row_align()); the leaf kernels run the products
+// on them: leaf_prep_kernel with 128 x 256 tiles on one SM each
+// (kPrepLeafSingle), leaf_pair_kernel with 256 x 128 tiles on a cluster of two
+// SMs (kPrepLeafPair, where the device schedules such clusters).
+enum : int { kPrepLeafSingle = 0, kPrepLeafPair = 1 };
 bool prep_supported();
+bool prep_pair_supported();
 int prep_row_align();
-TileShape prep_tile_shape(int bn);
+TileShape prep_tile_shape(int kind);
 cudaError_t launch_prep(const PrepPlan& plan, int batch, cudaStream_t stream);
-cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int bn, const float* region,
+cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* region,
                              long long row_len, long long rows, long long region_bstride,
                              int batch, cudaStream_t stream);
 cudaError_t read_and_clear_tc3_device_error(unsigned* value);

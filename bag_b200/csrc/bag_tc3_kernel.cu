@@ -119,13 +119,13 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 // Bounded wait; on timeout (or when another role gave up) sets the error word
 // and the CTA's abort flag and returns false.
-__device__ __forceinline__ bool mbar_wait(Bars& sb, unsigned long long* bar, unsigned parity) {
+__device__ __forceinline__ bool mbar_wait(int& abort, unsigned long long* bar, unsigned parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - start > kWaitLimitNs || *(volatile int*)&sb.abort) {
+    if (global_ns() - start > kWaitLimitNs || *(volatile int*)&abort) {
       atomicOr(&g_tc3_device_error, 1u);
-      *(volatile int*)&sb.abort = 1;
+      *(volatile int*)&abort = 1;
       return false;
     }
   }
@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
       for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
         const TileCoord tc = tile_of<BN>(plan, item);
         for (int s = 0; s < tc.stages; ++s, r.next(C::kStages)) {
-          if (issued >= C::kStages && !mbar_wait(sb, &sb.empty[r.idx], r.phase ^ 1u)) {
+          if (issued >= C::kStages && !mbar_wait(sb.abort, &sb.empty[r.idx], r.phase ^ 1u)) {
             ok = false;
             break;
           }
@@ -443,11 +443,11 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
       for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
         const TileCoord tc = tile_of<BN>(plan, item);
         for (int s = 0; s < tc.stages; ++s, r.next(C::kStages), rc.next(C::kChunkBufs)) {
-          if (chunks >= C::kChunkBufs && !mbar_wait(sb, &sb.chunk_empty[rc.idx], rc.phase ^ 1u)) {
+          if (chunks >= C::kChunkBufs && !mbar_wait(sb.abort, &sb.chunk_empty[rc.idx], rc.phase ^ 1u)) {
             ok = false;
             break;
           }
-          if (!mbar_wait(sb, &sb.full[r.idx], r.phase)) {
+          if (!mbar_wait(sb.abort, &sb.full[r.idx], r.phase)) {
             ok = false;
             break;
           }
@@ -486,7 +486,7 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 64; ++i) total[i] = 0.f;
       for (int c = 0; c < tc.stages; ++c, rc.next(C::kChunkBufs)) {
-        const bool w = mbar_wait(sb, &sb.chunk_full[rc.idx], rc.phase);
+        const bool w = mbar_wait(sb.abort, &sb.chunk_full[rc.idx], rc.phase);
         if (!__all_sync(0xffffffffu, w)) {   // tcgen05.ld below is warp-collective
           ok = false;
           break;
@@ -533,6 +533,321 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
   }
+}
+
+// ---- leaf products on prepared operands, CTA pairs ---------------------------
+// A cluster of two CTAs (one per SM) computes 256 x 256 output tiles with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 8, issued by the even CTA):
+// CTA r of the pair stages rows [128r, 128r + 128) of both the A and the B
+// tile, and its TMEM receives output rows [128r, 128r + 128) x 256 columns.
+// Per SM that is the single-CTA kernel's 128 x 256 tile at two thirds of its
+// operand bytes (each CTA loads half of B) and the same MMA instruction size.
+//  * warp 0, lane 0 (each CTA): per 32-k stage TMA loads of its A hi/lo and
+//    B hi/lo rows into its own 3-stage ring, tracked by its own full barrier;
+//    warp 0 also allocates the pair's TMEM (cta_group::2).
+//  * warp 1, lane 0: in the even CTA, the MMA thread: it waits for its own
+//    full barrier and for the odd CTA's relay of its own (peer_full), issues
+//    the stage's twelve MMAs into one of two 256-column TMEM chunk
+//    accumulators, then commits to the stage's empty and the chunk's full
+//    barrier in both CTAs; in the odd CTA, the relay.
+//  * warps 2-17 (fold): TMEM lane quadrant warp % 4, 64 columns each; add
+//    each finished 32-k chunk into 64 FP32 running sums (round-to-nearest),
+//    release it to the even CTA's chunk_empty barrier, and per tile add
+//    coef * sum into every target C block (red.global, coalesced along the
+//    column).
+namespace pairk {
+constexpr int kStages = 3;
+constexpr int kABytes = 128 * kStageK * 4;                 // 16 KB: 128 rows x 32 k
+constexpr int kBBytes = 128 * kStageK * 4;                 // 16 KB: 128 rows x 32 k
+constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;     // 64 KB
+constexpr int kChunks = 2;
+constexpr int kChunkCols = 256;
+constexpr int kFoldWarps = 16;
+constexpr int kThreads = (2 + kFoldWarps) * 32;            // 576
+constexpr int kBarOffset = kStages * kStageBytes;
+constexpr int kSmemBytes = kBarOffset + 1024;
+constexpr int kTileM = 256, kTileN = 256;
+// F32 accumulate, TF32 A and B, both K-major, N = 256, M = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(kTileN >> 3) << 17) |
+                            (uint32_t(kTileM >> 4) << 24);
+}  // namespace pairk
+
+struct PairBars {
+  unsigned long long full[pairk::kStages], empty[pairk::kStages];
+  unsigned long long peer_full[pairk::kStages];   // even CTA: the odd CTA's copies landed
+  unsigned long long chunk_full[pairk::kChunks], chunk_empty[pairk::kChunks];
+  unsigned long long mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the same shared-memory object in CTA `rank`.
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier of either CTA of the cluster (default semantics:
+// release at CTA scope; a cluster-scope release costs ~0.5 us per arrive).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Completion of this thread's earlier cta_group::2 MMAs, signalled on the
+// mbarrier at a shared::cluster address (either CTA of the pair).
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         bool accumulate) {
+  const uint32_t acc = accumulate ? 1u : 0u;
+  const uint32_t zero = 0u;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;"
+      "\n\t}"
+      :
+      : "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(pairk::kIdesc), "r"(acc), "r"(zero)
+      : "memory");
+}
+
+// Work item (pair tile) -> product and coordinates; same grouped order as the
+// single-CTA kernel, over 256 x 128 tiles.
+__device__ __forceinline__ TileCoord pair_tile_of(const PrepLeafPlan& plan, int item) {
+  const int batch = item / plan.ntiles, t = item - batch * plan.ntiles;
+  int pid = 0;
+  while (pid + 1 < plan.nprod && plan.prod[pid + 1].tile_begin <= t) ++pid;
+  const PrepProd& P = plan.prod[pid];
+  const int local = t - P.tile_begin;
+  constexpr int GROUP_M = 8;
+  const int in_group = GROUP_M * P.tiles_n;
+  const int first_m = (local / in_group) * GROUP_M;
+  const int gsize = min(P.tiles_m - first_m, GROUP_M);
+  TileCoord c;
+  c.P = &P;
+  c.m0 = (first_m + (local % in_group) % gsize) * pairk::kTileM;
+  c.n0 = ((local % in_group) / gsize) * pairk::kTileN;
+  c.batch = batch;
+  c.stages = (P.k + kStageK - 1) / kStageK;
+  return c;
+}
+
+__global__ void __launch_bounds__(pairk::kThreads, 1)
+    leaf_pair_kernel(const __grid_constant__ PrepLeafPlan plan,
+                     const __grid_constant__ PrepMaps maps, int items) {
+  using namespace pairk;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  PairBars& sb = *reinterpret_cast<PairBars*>(smem + kBarOffset);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cid = int(cluster_id_x()), ncl = int(cluster_count_x());
+  const int nparts = cid < items ? (items - 1 - cid) / ncl + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&sb.full[i], 1);
+      mbar_init(&sb.empty[i], 1);
+      mbar_init(&sb.peer_full[i], 1);
+    }
+    for (int i = 0; i < kChunks; ++i) {
+      mbar_init(&sb.chunk_full[i], 1);
+      mbar_init(&sb.chunk_empty[i], 2 * kFoldWarps);   // fold warps of both CTAs
+    }
+    mbar_init(&sb.mma_done, 1);
+    sb.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                     smem_u32(&sb.tmem_base))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();   // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = sb.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      long long issued = 0;
+      Ring r;
+      bool ok = true;
+      for (int p = 0; p < nparts && ok; ++p) {
+        const TileCoord tc = pair_tile_of(plan, cid + p * ncl);
+        const PrepProd& P = *tc.P;
+        const int arow = tc.m0 + 128 * int(rank), brow = tc.n0 + 128 * int(rank);
+        for (int s = 0; s < tc.stages; ++s, r.next(kStages)) {
+          if (issued >= kStages && !mbar_wait(sb.abort, &sb.empty[r.idx], r.phase ^ 1u)) {
+            ok = false;
+            break;
+          }
+          unsigned char* st = smem + r.idx * kStageBytes;
+          mbar_expect_tx(&sb.full[r.idx], kStageBytes);
+          const int k0 = s * kStageK;
+          tma_load_3d(st, &maps.a, k0, P.a_hi + arow, tc.batch, &sb.full[r.idx]);
+          tma_load_3d(st + kABytes, &maps.a, k0, P.a_lo + arow, tc.batch, &sb.full[r.idx]);
+          tma_load_3d(st + 2 * kABytes, &maps.b, k0, P.b_hi + brow, tc.batch, &sb.full[r.idx]);
+          tma_load_3d(st + 2 * kABytes + kBBytes, &maps.b, k0, P.b_lo + brow, tc.batch,
+                      &sb.full[r.idx]);
+          ++issued;
+        }
+      }
+      // No copy may outlive the CTA: wait for the latest phase of every stage
+      // slot that may still be loading.
+      for (long long s = issued > kStages ? issued - kStages : 0; s < issued; ++s)
+        mbar_drain(&sb.full[s % kStages], unsigned((s / kStages) & 1));
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      Ring r, rc;
+      long long chunks = 0;
+      bool ok = true;
+      for (int p = 0; p < nparts && ok; ++p) {
+        const TileCoord tc = pair_tile_of(plan, cid + p * ncl);
+        for (int s = 0; s < tc.stages; ++s, r.next(kStages), rc.next(kChunks)) {
+          if (chunks >= kChunks &&
+              !mbar_wait(sb.abort, &sb.chunk_empty[rc.idx], rc.phase ^ 1u)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(sb.abort, &sb.full[r.idx], r.phase) ||
+              !mbar_wait(sb.abort, &sb.peer_full[r.idx], r.phase)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + r.idx * kStageBytes);
+          const uint32_t d = tmem + uint32_t(rc.idx * kChunkCols);
+#pragma unroll
+          for (int j = 0; j < kStageK / 8; ++j) {
+            const uint64_t a_hi = sw128_desc(st + 32 * j);
+            const uint64_t a_lo = sw128_desc(st + kABytes + 32 * j);
+            const uint64_t b_hi = sw128_desc(st + 2 * kABytes + 32 * j);
+            const uint64_t b_lo = sw128_desc(st + 2 * kABytes + kBBytes + 32 * j);
+            mma_pair(d, a_hi, b_hi, j > 0);
+            mma_pair(d, a_hi, b_lo, true);
+            mma_pair(d, a_lo, b_hi, true);
+          }
+          mma_commit_pair(peer_addr(&sb.empty[r.idx], 0));
+          mma_commit_pair(peer_addr(&sb.empty[r.idx], 1));
+          mma_commit_pair(peer_addr(&sb.chunk_full[rc.idx], 0));
+          mma_commit_pair(peer_addr(&sb.chunk_full[rc.idx], 1));
+          ++chunks;
+        }
+      }
+      // All issued MMAs (which write both CTAs' TMEM and read both CTAs'
+      // shared memory) must finish before either CTA frees TMEM or exits.
+      mma_commit_pair(peer_addr(&sb.mma_done, 0));
+      mma_commit_pair(peer_addr(&sb.mma_done, 1));
+    } else if (lane == 0 && !leader) {
+      // Odd CTA: relay "my copies of this stage have landed" to the even CTA.
+      Ring r;
+      const uint32_t stride = uint32_t(sizeof(unsigned long long));
+      const uint32_t full0 = peer_addr(&sb.peer_full[0], 0);
+      for (int p = 0; p < nparts; ++p) {
+        const TileCoord tc = pair_tile_of(plan, cid + p * ncl);
+        bool ok = true;
+        for (int s = 0; s < tc.stages; ++s, r.next(kStages)) {
+          if (!mbar_wait(sb.abort, &sb.full[r.idx], r.phase)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_remote(full0 + uint32_t(r.idx) * stride);
+        }
+        if (!ok) break;
+      }
+    }
+    __syncwarp();
+  } else {
+    // Fold warp: TMEM lane quadrant q = warp % 4, columns [col0, col0 + 64).
+    const int q = warp % 4, col0 = ((warp - 2) / 4) * 64;
+    const uint32_t lane_base = uint32_t(q * 32) << 16;
+    const uint32_t empty0 = peer_addr(&sb.chunk_empty[0], 0);
+    const uint32_t stride = uint32_t(sizeof(unsigned long long));
+    Ring rc;
+    bool ok = true;
+    for (int p = 0; p < nparts && ok; ++p) {
+      const TileCoord tc = pair_tile_of(plan, cid + p * ncl);
+      float total[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) total[i] = 0.f;
+      for (int c = 0; c < tc.stages; ++c, rc.next(kChunks)) {
+        const bool w = mbar_wait(sb.abort, &sb.chunk_full[rc.idx], rc.phase);
+        if (!__all_sync(0xffffffffu, w)) {   // tcgen05.ld below is warp-collective
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t chunk = tmem + lane_base + uint32_t(rc.idx * kChunkCols + col0);
+#pragma unroll
+        for (int piece = 0; piece < 4; ++piece) {
+          float v[16];
+          tmem_ld16(chunk + 16 * piece, v);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            total[16 * piece + i] = __fadd_rn(total[16 * piece + i], v[i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(empty0 + uint32_t(rc.idx) * stride);
+      }
+      if (!ok || *(volatile int*)&sb.abort) break;
+      const PrepProd& P = *tc.P;
+      const int r = tc.m0 + 128 * int(rank) + q * 32 + lane;
+      if (r < P.m) {
+        for (int o = 0; o < P.no; ++o) {
+          const Term& T = plan.outs[P.o0 + o];
+          float* base = const_cast<float*>(T.p) + (long long)tc.batch * T.bstride + r;
+          const float coef = T.coef;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const int col = tc.n0 + col0 + i;
+            if (col >= P.n) break;
+            float* dst = base + (long long)col * T.ld;
+            if (T.mode == kOutAtomic) atomicAdd(dst, coef * total[i]);
+            else if (T.mode == kOutAdd) *dst += coef * total[i];
+            else *dst = coef * total[i];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    // The even CTA's MMAs write this CTA's TMEM and read its shared memory.
+    if (lane == 0) mbar_drain(&sb.mma_done, 0);
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+  // Neither CTA leaves while the other may still arrive on its barriers.
+  cluster_sync_all();
 }
 
 namespace {
@@ -585,9 +900,62 @@ cudaError_t launch_bn(const PrepLeafPlan& plan, const PrepMaps& maps, int batch,
   return cudaGetLastError();
 }
 
+// Clusters of two leaf_pair_kernel CTAs that fit on the device at once (0 if
+// none do); cached per device.
+int pair_clusters() {
+  static int cache[64];
+  static bool known[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (known[dev]) return cache[dev];
+  int n = 0;
+  if (cudaFuncSetAttribute(leaf_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           pairk::kSmemBytes) == cudaSuccess) {
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(pairk::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = pairk::kSmemBytes;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, leaf_pair_kernel, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();   // a refused query leaves no sticky error behind
+  cache[dev] = n;
+  known[dev] = true;
+  return n;
+}
+
+cudaError_t launch_pair(const PrepLeafPlan& plan, const PrepMaps& maps, int batch,
+                        cudaStream_t stream) {
+  const int clusters = pair_clusters();
+  if (clusters < 1) return cudaErrorNotSupported;
+  const long long items = (long long)plan.ntiles * batch;
+  if (items > INT32_MAX) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(unsigned(2 * (items < clusters ? items : clusters)), 1, 1);
+  cfg.blockDim = dim3(pairk::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = pairk::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, leaf_pair_kernel, plan, maps, int(items));
+}
+
 }  // namespace
 
 bool prep_supported() { return encode_fn() != nullptr; }
+
+bool prep_pair_supported() { return prep_supported() && pair_clusters() > 0; }
 
 int prep_row_align() { return kPrepTile; }   // a multiple of the 32-k stage
 
@@ -597,18 +965,19 @@ cudaError_t launch_prep(const PrepPlan& plan, int batch, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int bn, const float* region,
+cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* region,
                              long long row_len, long long rows, long long region_bstride,
                              int batch, cudaStream_t stream) {
   if (plan.nprod == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
-  if (bn != 128 && bn != 256) return cudaErrorInvalidValue;
+  if (kind != kPrepLeafSingle && kind != kPrepLeafPair) return cudaErrorInvalidValue;
+  const int b_rows = kind == kPrepLeafPair ? 128 : 256;
   PrepMaps maps;
   std::memset(&maps, 0, sizeof(maps));
   if (!encode_region(&maps.a, region, row_len, rows, region_bstride, batch, 128) ||
-      !encode_region(&maps.b, region, row_len, rows, region_bstride, batch, bn))
+      !encode_region(&maps.b, region, row_len, rows, region_bstride, batch, b_rows))
     return cudaErrorInvalidValue;
-  return bn == 128 ? launch_bn<128>(plan, maps, batch, stream)
-                   : launch_bn<256>(plan, maps, batch, stream);
+  return kind == kPrepLeafPair ? launch_pair(plan, maps, batch, stream)
+                               : launch_bn<256>(plan, maps, batch, stream);
 }
 
 cudaError_t read_and_clear_tc3_device_error(unsigned* value) {
@@ -618,6 +987,8 @@ cudaError_t read_and_clear_tc3_device_error(unsigned* value) {
   return cudaMemcpyToSymbol(g_tc3_device_error, &zero, sizeof(unsigned));
 }
 
-TileShape prep_tile_shape(int bn) { return {128, bn}; }
+TileShape prep_tile_shape(int kind) {
+  return kind == kPrepLeafPair ? TileShape{pairk::kTileM, pairk::kTileN} : TileShape{128, 256};
+}
 
 }  // namespace bag_b200

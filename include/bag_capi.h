@@ -164,6 +164,17 @@ int bag_get_math_mode(void);
  * and every leaf K is >= 1024 (below that the FFMA path is the more accurate).
  * New; no reference counterpart. */
 int bag_last_leaf_path(void);
+/* Leaf kernel the last call on this host thread ran: the FFMA kernels; the
+ * 3xTF32 kernel with the basis transforms fused into its prologue (no
+ * prepared-operand workspace); or, on prepared operands, 128 x 256 tiles on
+ * one SM or 256 x 128 tiles on a cluster of two SMs.  New; diagnostic. */
+enum {
+  BAG_LEAF_KERNEL_FFMA = 0,
+  BAG_LEAF_KERNEL_TF32_FUSED = 1,
+  BAG_LEAF_KERNEL_TF32_SINGLE = 2,
+  BAG_LEAF_KERNEL_TF32_PAIR = 3
+};
+int bag_last_leaf_kernel(void);
 
 /* Reads and clears the device error word (synchronous): non-zero when a
  * bounded in-kernel wait gave up instead of hanging (1) or a product reached a

@@ -173,3 +173,44 @@ def test_prepared_path_batched_and_accumulating(tensor_mode):
     exact = c0.double() + a.double() @ b.double()
     assert float((c.double() - exact).norm() / exact.norm()) <= 2e-6
     assert bag.device_error() == 0
+
+
+# The two prepared-operand leaf kernels: 256 x 256 tiles on a cluster of two
+# SMs (tcgen05.mma.cta_group::2, the default) and 128 x 256 tiles on one SM
+# (BAG_B200_PREP_KERNEL=single).  Same operands, same 32-k chunk folding:
+# both within the FFMA bound, and close to each other.  Shapes cover ragged
+# M/N (partial pair tiles), fewer tiles than clusters, and batches.
+@pytest.mark.parametrize("m,k,n,depth,batch", [
+    (512, 2048, 768, 0, 1), (1032, 4096, 2056, 2, 1), (4096, 4096, 4096, 2, 1),
+    (1000, 2048, 1160, 1, 2), (300, 1024, 104, 0, 3)])
+def test_pair_and_single_leaf_kernels(tensor_mode, monkeypatch, m, k, n, depth, batch):
+    import torch
+    bag = tensor_mode
+    g = torch.Generator(device="cuda").manual_seed(m * 3 + n + depth)
+    a = torch.randn(batch, m, k, device="cuda", generator=g)
+    b = torch.randn(batch, k, n, device="cuda", generator=g)
+    ws = bag.Workspace.for_problem(n, m, k, depth, batch=batch)
+    out = {}
+    for kernel in ("tf32_pair", "tf32_single"):
+        if kernel == "tf32_single":
+            monkeypatch.setenv("BAG_B200_PREP_KERNEL", "single")
+        c = torch.zeros(batch, m, n, device="cuda")
+        bag.sgemm_batched(a, b, c, beta=0.0, depth=depth, workspace=ws)
+        torch.cuda.synchronize()
+        assert bag.last_leaf_kernel() == kernel
+        assert bag.device_error() == 0
+        out[kernel] = c
+    monkeypatch.delenv("BAG_B200_PREP_KERNEL")
+    exact = a.double() @ b.double()
+    errs = {kk: float((c.double() - exact).norm() / exact.norm()) for kk, c in out.items()}
+    bag.set_math_mode("ffma")
+    ws_ffma = bag.Workspace.for_problem(n, m, k, depth, batch=batch)
+    c_ff = torch.zeros(batch, m, n, device="cuda")
+    bag.sgemm_batched(a, b, c_ff, beta=0.0, depth=depth, workspace=ws_ffma)
+    torch.cuda.synchronize()
+    bag.set_math_mode("3xtf32")
+    ffma = float((c_ff.double() - exact).norm() / exact.norm())
+    for kk, e in errs.items():
+        assert e <= min(1.25 * ffma, 1e-4), (kk, e, ffma)
+    diff = float((out["tf32_pair"] - out["tf32_single"]).double().norm() / exact.norm())
+    assert diff <= 1e-6, diff
