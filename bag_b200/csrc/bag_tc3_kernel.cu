@@ -160,6 +160,18 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// Tile load for a CTA pair: the copy lands in this CTA's shared memory and
+// completes on the mbarrier at `bar`, a shared::cluster address in either CTA
+// of the pair (.cta_group::2; no multicast).
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int x, int y,
+                                                 int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
 // K-major, 128-byte-swizzled operand tile (rows of 32 k = 128 B, 8-row atoms of
 // 1024 B): start address in 16-byte units, LBO 16 B (unused for this layout),
 // SBO 1024 B, version 1 (bit 46), layout SWIZZLE_128B (2 at bits 61-63).  A
@@ -542,14 +554,14 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
 // tile, and its TMEM receives output rows [128r, 128r + 128) x 256 columns.
 // Per SM that is the single-CTA kernel's 128 x 256 tile at two thirds of its
 // operand bytes (each CTA loads half of B) and the same MMA instruction size.
-//  * warp 0, lane 0 (each CTA): per 32-k stage TMA loads of its A hi/lo and
-//    B hi/lo rows into its own 3-stage ring, tracked by its own full barrier;
-//    warp 0 also allocates the pair's TMEM (cta_group::2).
-//  * warp 1, lane 0: in the even CTA, the MMA thread: it waits for its own
-//    full barrier and for the odd CTA's relay of its own (peer_full), issues
-//    the stage's twelve MMAs into one of two 256-column TMEM chunk
-//    accumulators, then commits to the stage's empty and the chunk's full
-//    barrier in both CTAs; in the odd CTA, the relay.
+//  * warp 0, lane 0 (each CTA): per stage TMA loads (.cta_group::2) of its A
+//    hi/lo and B hi/lo rows into its own stage ring; both CTAs' copies
+//    complete on the even CTA's full barrier, whose expected byte count the
+//    even CTA sets for both.  Warp 0 also allocates the pair's TMEM.
+//  * warp 1, lane 0 of the even CTA: the MMA thread: it waits for the full
+//    barrier, issues the stage's twelve MMAs into one of two 256-column TMEM
+//    chunk accumulators (a 32-k stage is one accumulation chunk), then
+//    commits to the stage's empty and the chunk's full barrier in both CTAs.
 //  * warps 2-17 (fold): TMEM lane quadrant warp % 4, 64 columns each; add
 //    each finished 32-k chunk into 64 FP32 running sums (round-to-nearest),
 //    release it to the even CTA's chunk_empty barrier, and per tile add
@@ -573,8 +585,8 @@ constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(kTile
 }  // namespace pairk
 
 struct PairBars {
+  // full: the even CTA's counts both CTAs' copies of the stage.
   unsigned long long full[pairk::kStages], empty[pairk::kStages];
-  unsigned long long peer_full[pairk::kStages];   // even CTA: the odd CTA's copies landed
   unsigned long long chunk_full[pairk::kChunks], chunk_empty[pairk::kChunks];
   unsigned long long mma_done;
   uint32_t tmem_base;
@@ -633,7 +645,7 @@ __device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t a_desc, uint6
 }
 
 // Work item (pair tile) -> product and coordinates; same grouped order as the
-// single-CTA kernel, over 256 x 128 tiles.
+// single-CTA kernel, over 256 x 256 tiles.
 __device__ __forceinline__ TileCoord pair_tile_of(const PrepLeafPlan& plan, int item) {
   const int batch = item / plan.ntiles, t = item - batch * plan.ntiles;
   int pid = 0;
@@ -669,7 +681,6 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sb.full[i], 1);
       mbar_init(&sb.empty[i], 1);
-      mbar_init(&sb.peer_full[i], 1);
     }
     for (int i = 0; i < kChunks; ++i) {
       mbar_init(&sb.chunk_full[i], 1);
@@ -705,20 +716,26 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
             break;
           }
           unsigned char* st = smem + r.idx * kStageBytes;
-          mbar_expect_tx(&sb.full[r.idx], kStageBytes);
+          if (leader) mbar_expect_tx(&sb.full[r.idx], 2 * kStageBytes);
+          const uint32_t bar = peer_addr(&sb.full[r.idx], 0);
           const int k0 = s * kStageK;
-          tma_load_3d(st, &maps.a, k0, P.a_hi + arow, tc.batch, &sb.full[r.idx]);
-          tma_load_3d(st + kABytes, &maps.a, k0, P.a_lo + arow, tc.batch, &sb.full[r.idx]);
-          tma_load_3d(st + 2 * kABytes, &maps.b, k0, P.b_hi + brow, tc.batch, &sb.full[r.idx]);
-          tma_load_3d(st + 2 * kABytes + kBBytes, &maps.b, k0, P.b_lo + brow, tc.batch,
-                      &sb.full[r.idx]);
+          tma_load_3d_pair(st, &maps.a, k0, P.a_hi + arow, tc.batch, bar);
+          tma_load_3d_pair(st + kABytes, &maps.a, k0, P.a_lo + arow, tc.batch, bar);
+          tma_load_3d_pair(st + 2 * kABytes, &maps.b, k0, P.b_hi + brow, tc.batch, bar);
+          tma_load_3d_pair(st + 2 * kABytes + kBBytes, &maps.b, k0, P.b_lo + brow, tc.batch, bar);
           ++issued;
         }
       }
-      // No copy may outlive the CTA: wait for the latest phase of every stage
-      // slot that may still be loading.
-      for (long long s = issued > kStages ? issued - kStages : 0; s < issued; ++s)
-        mbar_drain(&sb.full[s % kStages], unsigned((s / kStages) & 1));
+      // No copy may outlive the CTA.  The even CTA waits for the latest phase
+      // of every full barrier that may still be loading (they count both
+      // CTAs' copies); the odd CTA, whose copies complete on the even CTA's
+      // barriers, for the empty phase that follows each of its last stages
+      // (the MMA consumed it, so its copies had landed) -- bounded, and on
+      // the abort path long after any copy could still be in flight.
+      for (long long s = issued > kStages ? issued - kStages : 0; s < issued; ++s) {
+        const unsigned ph = unsigned((s / kStages) & 1);
+        mbar_drain(leader ? &sb.full[s % kStages] : &sb.empty[s % kStages], ph);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -734,8 +751,7 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
             ok = false;
             break;
           }
-          if (!mbar_wait(sb.abort, &sb.full[r.idx], r.phase) ||
-              !mbar_wait(sb.abort, &sb.peer_full[r.idx], r.phase)) {
+          if (!mbar_wait(sb.abort, &sb.full[r.idx], r.phase)) {
             ok = false;
             break;
           }
@@ -763,23 +779,6 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
       // shared memory) must finish before either CTA frees TMEM or exits.
       mma_commit_pair(peer_addr(&sb.mma_done, 0));
       mma_commit_pair(peer_addr(&sb.mma_done, 1));
-    } else if (lane == 0 && !leader) {
-      // Odd CTA: relay "my copies of this stage have landed" to the even CTA.
-      Ring r;
-      const uint32_t stride = uint32_t(sizeof(unsigned long long));
-      const uint32_t full0 = peer_addr(&sb.peer_full[0], 0);
-      for (int p = 0; p < nparts; ++p) {
-        const TileCoord tc = pair_tile_of(plan, cid + p * ncl);
-        bool ok = true;
-        for (int s = 0; s < tc.stages; ++s, r.next(kStages)) {
-          if (!mbar_wait(sb.abort, &sb.full[r.idx], r.phase)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_remote(full0 + uint32_t(r.idx) * stride);
-        }
-        if (!ok) break;
-      }
     }
     __syncwarp();
   } else {
