@@ -162,7 +162,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 
 // Tile load for a CTA pair: the copy lands in this CTA's shared memory and
 // completes on the mbarrier at `bar`, a shared::cluster address in either CTA
-// of the pair (.cta_group::2; no multicast).
+// of the pair (.cta_group::2): a plain load into this CTA's own tile.
 __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int x, int y,
                                                  int z, uint32_t bar) {
   asm volatile(
