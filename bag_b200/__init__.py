@@ -85,6 +85,7 @@ SIGNATURES = {
     "bag_get_math_mode": (_I, []),
     "bag_last_leaf_path": (_I, []),
     "bag_last_leaf_kernel": (_I, []),
+    "bag_selftest_bounded_wait": (_I, [ctypes.c_ulonglong, ctypes.POINTER(_I)]),
 }
 MATH = {"ffma": 0, "3xtf32": 1}
 LEAF_KERNELS = {0: "ffma", 1: "tf32_fused", 2: "tf32_single", 3: "tf32_pair"}
@@ -190,6 +191,15 @@ def last_leaf_kernel() -> str:
     operands, 128 x 256 tiles per SM) or "tf32_pair" (prepared operands,
     256 x 128 tiles per cluster of two SMs)."""
     return LEAF_KERNELS[int(lib().bag_last_leaf_kernel())]
+
+
+def selftest_bounded_wait(limit_ns: int = 1_000_000) -> bool:
+    """Run the bounded-wait self-test (a wait on an mbarrier nothing arrives on,
+    giving up after ``limit_ns``); True when the wait gave up and the kernel
+    returned.  Leaves the device error word at 1 (see ``device_error``)."""
+    flag = _I(0)
+    _check(lib().bag_selftest_bounded_wait(int(limit_ns), ctypes.byref(flag)))
+    return bool(flag.value)
 
 
 def device_error() -> int:

@@ -1213,6 +1213,22 @@ bag_status bag_device_error(unsigned* code) {
   });
 }
 
+bag_status bag_selftest_bounded_wait(unsigned long long limit_ns, int* gave_up) {
+  return guarded([&] {
+    if (!gave_up) fail(BAG_ERR_INVALID, "null output pointer");
+    if (limit_ns == 0 || limit_ns > 100000000ull) fail(BAG_ERR_INVALID, "limit must be in (0, 0.1 s]");
+    int* flag = nullptr;
+    cuda_check(cudaMalloc(&flag, sizeof(int)), "cudaMalloc");
+    cudaError_t e = run_wait_selftest(limit_ns, flag, nullptr);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
+    int host = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&host, flag, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(flag);
+    cuda_check(e, "bounded-wait self-test");
+    *gave_up = host;
+  });
+}
+
 bag_status bag_ffma_probe(float* sink, int iterations, bag_stream_t stream, double* flops) {
   return guarded([&] {
     if (!sink || !flops || iterations <= 0) fail(BAG_ERR_INVALID, "bad probe arguments");

@@ -74,6 +74,9 @@ cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* re
                              long long row_len, long long rows, long long region_bstride,
                              int batch, cudaStream_t stream);
 cudaError_t read_and_clear_tc3_device_error(unsigned* value);
+// One launch of the bounded-wait self-test (bag_tc3_kernel.cu).
+cudaError_t run_wait_selftest(unsigned long long limit_ns, int* gave_up_device,
+                              cudaStream_t stream);
 
 // Reads and clears the device error word that bounded waits set on timeout.
 cudaError_t read_and_clear_device_error(unsigned* value);

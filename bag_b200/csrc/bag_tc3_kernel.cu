@@ -119,11 +119,12 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 // Bounded wait; on timeout (or when another role gave up) sets the error word
 // and the CTA's abort flag and returns false.
-__device__ __forceinline__ bool mbar_wait(int& abort, unsigned long long* bar, unsigned parity) {
+__device__ __forceinline__ bool mbar_wait(int& abort, unsigned long long* bar, unsigned parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - start > kWaitLimitNs || *(volatile int*)&abort) {
+    if (global_ns() - start > limit_ns || *(volatile int*)&abort) {
       atomicOr(&g_tc3_device_error, 1u);
       *(volatile int*)&abort = 1;
       return false;
@@ -849,6 +850,22 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
   cluster_sync_all();
 }
 
+// Self-test of the bounded wait the leaf kernels use: thread 0 waits on an
+// mbarrier that nothing arrives on, with a short limit; the wait must give
+// up, set this file's device error word and the CTA's abort flag, and the
+// kernel must return (the context stays usable).  *gave_up = 1 when it did.
+__global__ void wait_selftest_kernel(unsigned long long limit_ns, int* gave_up) {
+  __shared__ unsigned long long bar;
+  __shared__ int abort;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *gave_up = mbar_wait(abort, &bar, 0, limit_ns) ? 0 : 1;
+}
+
 namespace {
 
 using EncodeTiled = PFN_cuTensorMapEncodeTiled_v12000;
@@ -977,6 +994,12 @@ cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* re
     return cudaErrorInvalidValue;
   return kind == kPrepLeafPair ? launch_pair(plan, maps, batch, stream)
                                : launch_bn<256>(plan, maps, batch, stream);
+}
+
+cudaError_t run_wait_selftest(unsigned long long limit_ns, int* gave_up_device,
+                              cudaStream_t stream) {
+  wait_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns, gave_up_device);
+  return cudaGetLastError();
 }
 
 cudaError_t read_and_clear_tc3_device_error(unsigned* value) {

@@ -180,6 +180,13 @@ int bag_last_leaf_kernel(void);
  * bounded in-kernel wait gave up instead of hanging (1) or a product reached a
  * kernel it was not planned for (2).  New; no reference counterpart. */
 bag_status bag_device_error(unsigned* code);
+/* Self-test of that mechanism (synchronous): one tiny launch whose only
+ * thread waits, through the leaf kernels' bounded-wait routine, on an
+ * mbarrier that nothing arrives on, giving up after limit_ns nanoseconds.
+ * *gave_up receives 1 when the wait gave up and the kernel returned; the
+ * device error word is then 1 (read it with bag_device_error).  New;
+ * diagnostic. */
+bag_status bag_selftest_bounded_wait(unsigned long long limit_ns, int* gave_up);
 /* FP32 FFMA throughput probe (a roofline denominator): one launch of
  * 4 x SM-count CTAs x 256 threads of register-only fmaf chains; `sink` must
  * hold 1024 x SM-count floats.  *flops receives the launch's FLOP count. */

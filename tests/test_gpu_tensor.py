@@ -214,3 +214,23 @@ def test_pair_and_single_leaf_kernels(tensor_mode, monkeypatch, m, k, n, depth, 
         assert e <= min(1.25 * ffma, 1e-4), (kk, e, ffma)
     diff = float((out["tf32_pair"] - out["tf32_single"]).double().norm() / exact.norm())
     assert diff <= 1e-6, diff
+
+
+# Failure detection without a GPU fault: a wait on an mbarrier that nothing
+# arrives on gives up after its limit, sets the device error word, and the
+# context keeps working (the next product runs and is correct).
+def test_bounded_wait_gives_up_and_context_survives(tensor_mode):
+    import torch
+    bag = tensor_mode
+    assert bag.device_error() == 0
+    assert bag.selftest_bounded_wait(2_000_000) is True
+    assert bag.device_error() == 1
+    assert bag.device_error() == 0   # read and cleared
+    a, b = _operands(torch, 512, 2048, 512, seed=11)
+    ws = bag.Workspace.for_problem(512, 512, 2048, 1)
+    c, path = _sgemm(bag, torch, a, b, 1, "minimal", ws, "3xtf32")
+    assert path == "3xtf32" and bag.last_leaf_kernel() == "tf32_pair"
+    assert _rel(torch, c, a, b) <= 2e-6
+    assert bag.device_error() == 0
+    with pytest.raises(ValueError):   # BAG_ERR_INVALID
+        bag.selftest_bounded_wait(0)
