@@ -86,6 +86,12 @@ SIGNATURES = {
     "bag_last_leaf_path": (_I, []),
     "bag_last_leaf_kernel": (_I, []),
     "bag_selftest_bounded_wait": (_I, [ctypes.c_ulonglong, ctypes.POINTER(_I)]),
+    "bag_multi_grid": (_I, [_I, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "bag_multi_workspace_create": (_I, [_I, ctypes.POINTER(_I), _I, _I, _I, _I, _I, _I,
+                                        ctypes.POINTER(_VP)]),
+    "bag_multi_workspace_destroy": (_I, [_VP]),
+    "bag_sgemm_multi": (_I, [_I, ctypes.POINTER(_I), _I, _I, _I, _I, _VP, _LL, _VP, _LL, _VP, _LL,
+                             _F, _I, _I, _VP, _VP]),
 }
 MATH = {"ffma": 0, "3xtf32": 1}
 LEAF_KERNELS = {0: "ffma", 1: "tf32_fused", 2: "tf32_single", 3: "tf32_pair"}
@@ -331,6 +337,63 @@ def sgemm(a, b, c, *, beta: float = 1.0, depth: int = 1, basis="minimal",
     return c
 
 
+def multi_grid(ngpus: int) -> tuple[int, int]:
+    """The R x S device grid ``sgemm_multi`` uses for ``ngpus`` devices."""
+    r, c = _I(0), _I(0)
+    _check(lib().bag_multi_grid(int(ngpus), ctypes.byref(r), ctypes.byref(c)))
+    return r.value, c.value
+
+
+class MultiWorkspace:
+    """Shard buffers, per-device workspaces and streams for ``sgemm_multi`` of
+    one row-major problem ``C(m x n) = A(m x k) B(k x n)`` over ``devices``
+    (the first holds A, B and C).  Created in the calling thread's math mode."""
+
+    def __init__(self, devices, m: int, n: int, k: int, depth: int = 1, basis="minimal"):
+        self.devices = [int(d) for d in devices]
+        self.shape, self.depth, self.basis = (m, n, k), depth, basis
+        self._devs = (_I * len(self.devices))(*self.devices)
+        handle = ctypes.c_void_p()
+        _check(lib().bag_multi_workspace_create(len(self.devices), self._devs, LAYOUT["row"], m, n, k,
+                                                _depth(depth), _basis(basis), ctypes.byref(handle)))
+        self._handle = handle
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._handle
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None) and self._handle.value:
+            lib().bag_multi_workspace_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def sgemm_multi(a, b, c, workspace: MultiWorkspace, *, beta: float = 1.0, stream=None):
+    """``c <- a @ b + beta*c`` over ``workspace.devices`` (row-major FP32 tensors
+    on the first device): each device computes its row/column bands of C from
+    peer-copied shards; ``stream`` (of the first device) waits for all of them."""
+    m, k = a.shape
+    k2, n = b.shape
+    if k2 != k or tuple(c.shape) != (m, n) or (m, n, k) != workspace.shape:
+        raise ValueError("shape differs from the multi-GPU workspace's")
+    for t in (a, b, c):
+        if not t.is_contiguous():
+            raise ValueError("sgemm_multi needs contiguous row-major tensors")
+    ws = workspace
+    if stream is None:
+        stream = _torch().cuda.current_stream(ws.devices[0])
+    _check(lib().bag_sgemm_multi(len(ws.devices), ws._devs, LAYOUT["row"], m, n, k, a.data_ptr(), k,
+                                 b.data_ptr(), n, c.data_ptr(), n, float(beta), _depth(ws.depth),
+                                 _basis(ws.basis), _stream_handle(stream), ws.handle))
+    return c
+
+
 def sgemm_batched(a, b, c, *, beta: float = 1.0, depth: int = 1, basis="minimal",
                   workspace: Optional[Workspace] = None, stream=None):
     """Batched ``c[i] <- a[i] @ b[i] + beta*c[i]`` for contiguous 3-D row-major tensors."""
@@ -538,5 +601,6 @@ def bag_primitive(x, y, v, w, d, e, *, delta: int, epsilon: int, gamma_d: int, g
 __all__ = [
     "BagError", "BagWorkspace", "Workspace", "allocate_bag_workspace", "bag_matmul",
     "bag_primitive", "lib", "local_elements", "matmul", "plan_dump", "sgemm", "sgemm_batched",
+    "MultiWorkspace", "multi_grid", "sgemm_multi",
     "strassen_one_level", "valid_shape",
 ]

@@ -1257,3 +1257,247 @@ bag_status bag_plan_dump(int m, int n, int k, long long lda, long long ldb, long
 }
 
 }  // extern "C"
+
+// ---- several GPUs of one process --------------------------------------------
+// bag_sgemm_multi: the devices form an R x S grid; device (i, j) computes, on
+// compact copies of its shards, row band i of every one of the 2^depth
+// block-rows of C and column band j of every block-column.  BAG combines only
+// blocks at equal offsets (the forward transforms and the inverse transform
+// act on whole blocks), so the recursion on the shards is exactly the full
+// recursion restricted to those rows and columns: no reduction between
+// devices.  The shards travel by 2-D peer copies from and to the caller's
+// device (NVLink where peer access is available).
+
+struct bag_multi_workspace {
+  int ngpus, rows, cols;             // the R x S device grid
+  int m, n, k, depth, basis;         // column-major problem (after the layout swap)
+  std::vector<int> devices;
+  std::vector<bag_workspace*> ws;    // one per device, for its shard problem
+  std::vector<float*> a, b, c;       // shard buffers: (m/R) x k, k x (n/S), (m/R) x (n/S)
+  std::vector<cudaStream_t> streams;
+  std::vector<cudaEvent_t> done;
+  cudaEvent_t start = nullptr;
+};
+
+namespace bag_b200 {
+namespace {
+
+void multi_grid(int ngpus, int* rows, int* cols) {
+  switch (ngpus) {
+    case 2: *rows = 2; *cols = 1; break;
+    case 4: *rows = 2; *cols = 2; break;
+    case 8: *rows = 4; *cols = 2; break;
+    default: *rows = ngpus; *cols = 1; break;
+  }
+}
+
+// Restores the calling thread's current device on scope exit.
+struct DeviceGuard {
+  int saved = 0;
+  bool ok = false;
+  DeviceGuard() { ok = cudaGetDevice(&saved) == cudaSuccess; }
+  ~DeviceGuard() {
+    if (ok) cudaSetDevice(saved);
+  }
+};
+
+void multi_free(bag_multi_workspace* w) {
+  if (!w) return;
+  DeviceGuard guard;
+  for (size_t g = 0; g < w->devices.size(); ++g) {
+    cudaSetDevice(w->devices[g]);
+    if (g < w->ws.size() && w->ws[g]) bag_workspace_destroy(w->ws[g]);
+    if (g < w->a.size() && w->a[g]) cudaFree(w->a[g]);
+    if (g < w->b.size() && w->b[g]) cudaFree(w->b[g]);
+    if (g < w->c.size() && w->c[g]) cudaFree(w->c[g]);
+    if (g < w->streams.size() && w->streams[g]) cudaStreamDestroy(w->streams[g]);
+    if (g < w->done.size() && w->done[g]) cudaEventDestroy(w->done[g]);
+  }
+  if (w->start) {
+    cudaSetDevice(w->devices[0]);
+    cudaEventDestroy(w->start);
+  }
+  delete w;
+}
+
+// Copies the band rows [b0, b0 + band) of each of `blocks` row blocks of q
+// rows (a column-major matrix, `ncols` columns, leading dimension ld) between
+// the full matrix and a compact matrix (leading dimension blocks * band).
+void copy_row_bands(float* dst, long long ldd, const float* src, long long lds, int blocks, int q,
+                    int band, int b0, int ncols, bool to_compact, cudaStream_t s) {
+  for (int bi = 0; bi < blocks; ++bi) {
+    const long long full_row = (long long)bi * q + b0, compact_row = (long long)bi * band;
+    const float* from = to_compact ? src + full_row : src + compact_row;
+    float* to = to_compact ? dst + compact_row : dst + full_row;
+    cuda_check(cudaMemcpy2DAsync(to, size_t(ldd) * 4, from, size_t(lds) * 4, size_t(band) * 4,
+                                 size_t(ncols), cudaMemcpyDefault, s),
+               "shard copy");
+  }
+}
+
+}  // namespace
+}  // namespace bag_b200
+
+extern "C" {
+
+bag_status bag_multi_grid(int ngpus, int* rows, int* cols) {
+  return guarded([&] {
+    if (ngpus < 1 || !rows || !cols) fail(BAG_ERR_INVALID, "bad grid arguments");
+    multi_grid(ngpus, rows, cols);
+  });
+}
+
+bag_status bag_multi_workspace_create(int ngpus, const int* devices, int layout, int m, int n,
+                                      int k, int depth, int basis, bag_multi_workspace** out) {
+  bag_multi_workspace* w = nullptr;
+  const bag_status st = guarded([&] {
+    if (!out) fail(BAG_ERR_INVALID, "null output pointer");
+    *out = nullptr;
+    if (ngpus < 1 || ngpus > 64 || !devices) fail(BAG_ERR_INVALID, "need 1..64 devices");
+    if (layout != BAG_LAYOUT_COL_MAJOR && layout != BAG_LAYOUT_ROW_MAJOR)
+      fail(BAG_ERR_INVALID, "unknown layout");
+    if (m < 0 || n < 0 || k < 0) fail(BAG_ERR_SHAPE, "negative extent");
+    if (layout == BAG_LAYOUT_ROW_MAJOR) std::swap(m, n);   // C^T = B^T A^T
+    depth = resolve_depth(depth, m, n, k);
+    if (depth < 0 || depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8 or BAG_DEPTH_AUTO");
+    if (!known_basis(basis)) fail(BAG_ERR_INVALID, "unknown basis");
+    int rows = 1, cols = 1;
+    multi_grid(ngpus, &rows, &cols);
+    const long long bm = (long long)rows << depth, bn = (long long)cols << depth;
+    if (m % bm || n % bn)
+      fail(BAG_ERR_SHAPE, "multi-GPU shards need M divisible by 2^depth x grid rows and N by "
+                          "2^depth x grid columns (in the column-major problem)");
+    w = new bag_multi_workspace{};
+    w->ngpus = ngpus;
+    w->rows = rows;
+    w->cols = cols;
+    w->m = m;
+    w->n = n;
+    w->k = k;
+    w->depth = depth;
+    w->basis = basis;
+    w->devices.assign(devices, devices + ngpus);
+    w->ws.assign(ngpus, nullptr);
+    w->a.assign(ngpus, nullptr);
+    w->b.assign(ngpus, nullptr);
+    w->c.assign(ngpus, nullptr);
+    w->streams.assign(ngpus, nullptr);
+    w->done.assign(ngpus, nullptr);
+    DeviceGuard guard;
+    const int home = devices[0];
+    const int ms = m / rows, ns = n / cols;
+    for (int g = 0; g < ngpus; ++g) {
+      const int dev = devices[g];
+      cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+      if (dev != home) {
+        // NVLink peer access both ways where the pair supports it; copies fall
+        // back to staging through the host otherwise.
+        int can = 0;
+        cuda_check(cudaDeviceCanAccessPeer(&can, dev, home), "cudaDeviceCanAccessPeer");
+        if (can) {
+          cudaError_t e = cudaDeviceEnablePeerAccess(home, 0);
+          if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+            cuda_check(e, "cudaDeviceEnablePeerAccess");
+          cudaGetLastError();
+          cuda_check(cudaSetDevice(home), "cudaSetDevice");
+          e = cudaDeviceEnablePeerAccess(dev, 0);
+          if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+            cuda_check(e, "cudaDeviceEnablePeerAccess");
+          cudaGetLastError();
+          cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+        }
+      }
+      cuda_check(cudaMalloc(&w->a[g], std::max<size_t>(1, size_t(ms) * k) * 4), "shard allocation");
+      cuda_check(cudaMalloc(&w->b[g], std::max<size_t>(1, size_t(k) * ns) * 4), "shard allocation");
+      cuda_check(cudaMalloc(&w->c[g], std::max<size_t>(1, size_t(ms) * ns) * 4), "shard allocation");
+      cuda_check(cudaStreamCreateWithFlags(&w->streams[g], cudaStreamNonBlocking), "stream");
+      cuda_check(cudaEventCreateWithFlags(&w->done[g], cudaEventDisableTiming), "event");
+      // The shard problem's workspace, on this device, in this thread's math mode.
+      const bag_status s = bag_workspace_create_ex(ms, ns, k, depth, basis, 1, &w->ws[g]);
+      if (s != BAG_OK) fail(s, g_last_error);
+    }
+    cuda_check(cudaSetDevice(home), "cudaSetDevice");
+    cuda_check(cudaEventCreateWithFlags(&w->start, cudaEventDisableTiming), "event");
+    *out = w;
+  });
+  if (st != BAG_OK && w && (!out || *out != w)) {
+    const std::string msg = g_last_error;
+    multi_free(w);
+    g_last_error = msg;
+  }
+  return st;
+}
+
+bag_status bag_multi_workspace_destroy(bag_multi_workspace* ws) {
+  return guarded([&] { multi_free(ws); });
+}
+
+bag_status bag_sgemm_multi(int ngpus, const int* devices, int layout, int m, int n, int k,
+                           const float* a, long long lda, const float* b, long long ldb, float* c,
+                           long long ldc, float beta, int depth, int basis, bag_stream_t stream,
+                           bag_multi_workspace* ws) {
+  return guarded([&] {
+    if (!ws) fail(BAG_ERR_WORKSPACE, "null multi-GPU workspace");
+    if (ngpus != ws->ngpus || !devices) fail(BAG_ERR_WORKSPACE, "device list differs from the workspace's");
+    for (int g = 0; g < ngpus; ++g)
+      if (devices[g] != ws->devices[g]) fail(BAG_ERR_WORKSPACE, "device list differs from the workspace's");
+    if (beta != 0.f && beta != 1.f) fail(BAG_ERR_INVALID, "beta must be 0 or 1");
+    const GemmDesc g0 = make_desc(layout, m, n, k, a, lda, 0, b, ldb, 0, c, ldc, 0, 1, depth, basis);
+    const int dres = resolve_depth(depth, g0.m, g0.n, g0.k);
+    if (g0.m != ws->m || g0.n != ws->n || g0.k != ws->k || dres != ws->depth || basis != ws->basis)
+      fail(BAG_ERR_WORKSPACE, "problem differs from the multi-GPU workspace's");
+    if (g0.k > 0 && (!g0.a || !g0.b)) fail(BAG_ERR_INVALID, "A and B are required");
+    if (!g0.c) fail(BAG_ERR_INVALID, "C is required");
+    if (g0.lda < std::max(1, g0.m) || g0.ldb < std::max(1, g0.k) || g0.ldc < std::max(1, g0.m))
+      fail(BAG_ERR_SHAPE, "leading dimension too small");
+    const int blocks = 1 << ws->depth;
+    const int ms = ws->m / ws->rows, ns = ws->n / ws->cols;
+    const int qm = ws->m / blocks, qn = ws->n / blocks;
+    const int bandm = qm / ws->rows, bandn = qn / ws->cols;
+    DeviceGuard guard;
+    const cudaStream_t caller = reinterpret_cast<cudaStream_t>(stream);
+    cuda_check(cudaSetDevice(ws->devices[0]), "cudaSetDevice");
+    cuda_check(cudaEventRecord(ws->start, caller), "cudaEventRecord");
+    for (int r = 0; r < ngpus; ++r) {
+      const int i = r / ws->cols, j = r % ws->cols;
+      const cudaStream_t s = ws->streams[r];
+      cuda_check(cudaSetDevice(ws->devices[r]), "cudaSetDevice");
+      cuda_check(cudaStreamWaitEvent(s, ws->start, 0), "cudaStreamWaitEvent");
+      // A shard: row band i of each block-row, all k columns.
+      if (g0.k > 0)
+        copy_row_bands(ws->a[r], ms, g0.a, g0.lda, blocks, qm, bandm, i * bandm, g0.k, true, s);
+      // B shard: column band j of each block-column (rows of B^T): whole
+      // columns, so one 2-D copy per block-column.
+      for (int bj = 0; bj < blocks && g0.k > 0; ++bj) {
+        const long long col = (long long)bj * qn + (long long)j * bandn;
+        cuda_check(cudaMemcpy2DAsync(ws->b[r] + (long long)bj * bandn * g0.k, size_t(g0.k) * 4,
+                                     g0.b + col * g0.ldb, size_t(g0.ldb) * 4, size_t(g0.k) * 4,
+                                     size_t(bandn), cudaMemcpyDefault, s),
+                   "shard copy");
+      }
+      // C shard when it accumulates: row band i of each block-row, for each
+      // column band j of each block-column.
+      for (int bj = 0; bj < blocks && beta != 0.f; ++bj) {
+        const long long col = (long long)bj * qn + (long long)j * bandn;
+        copy_row_bands(ws->c[r] + (long long)bj * bandn * ms, ms, g0.c + col * g0.ldc, g0.ldc,
+                       blocks, qm, bandm, i * bandm, bandn, true, s);
+      }
+      const bag_status st = bag_sgemm_ex(BAG_LAYOUT_COL_MAJOR, ms, ns, g0.k, ws->a[r], ms,
+                                         ws->b[r], std::max(1, g0.k), ws->c[r], ms, beta,
+                                         ws->depth, ws->basis, reinterpret_cast<bag_stream_t>(s),
+                                         ws->ws[r]);
+      if (st != BAG_OK) fail(st, g_last_error);
+      for (int bj = 0; bj < blocks; ++bj) {
+        const long long col = (long long)bj * qn + (long long)j * bandn;
+        copy_row_bands(g0.c + col * g0.ldc, g0.ldc, ws->c[r] + (long long)bj * bandn * ms, ms,
+                       blocks, qm, bandm, i * bandm, bandn, false, s);
+      }
+      cuda_check(cudaEventRecord(ws->done[r], s), "cudaEventRecord");
+    }
+    cuda_check(cudaSetDevice(ws->devices[0]), "cudaSetDevice");
+    for (int r = 0; r < ngpus; ++r)
+      cuda_check(cudaStreamWaitEvent(caller, ws->done[r], 0), "cudaStreamWaitEvent");
+  });
+}
+
+}  // extern "C"

@@ -3,6 +3,8 @@
     python -m bag_b200.profile_case --n 4096 --depth 1          # one small case for ncu
     python -m bag_b200.profile_case --sweep                      # time the current tile config
     python -m bag_b200.profile_case --math 3xtf32 ...            # tensor-core leaf variant
+    python -m bag_b200.profile_case --devices 0,1 --n 16384 --depth 2 --math 3xtf32
+                                                                 # time sgemm_multi
 
 The case mode builds N(0,1) FP32 operands on cuda:0 (torch generator, seed 0)
 and calls ``bag_b200.sgemm`` ``--calls`` times, so an ``ncu -k regex:leaf_gemm
@@ -79,6 +81,42 @@ def run_sweep(reps: int = 3) -> dict:
     return out
 
 
+def run_multi(devices: list[int], n: int, depth: int, basis: str, calls: int) -> dict:
+    """Time ``sgemm_multi`` over ``devices`` (inputs and output on the first):
+    CUDA events on the first device's stream around ``calls`` calls after a
+    warm-up; the single-device call on the same inputs beside it."""
+    import torch
+
+    import bag_b200 as bag
+    torch.cuda.set_device(devices[0])
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(n, n, device="cuda", generator=g)
+    b = torch.randn(n, n, device="cuda", generator=g)
+    c = torch.zeros(n, n, device="cuda")
+
+    def timed(fn) -> float:
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(calls):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / calls
+
+    mws = bag.MultiWorkspace(devices, n, n, n, depth=depth, basis=basis)
+    ms_multi = timed(lambda: bag.sgemm_multi(a, b, c, mws, beta=0.0))
+    del mws
+    ws = bag.Workspace.for_problem(n, n, n, depth, basis)
+    ms_one = timed(lambda: bag.sgemm(a, b, c, beta=0.0, depth=depth, basis=basis, workspace=ws))
+    flops = 2.0 * n ** 3
+    return {"devices": devices, "grid": bag.multi_grid(len(devices)), "n": n, "depth": depth,
+            "math": bag.get_math_mode(), "multi_ms": round(ms_multi, 3),
+            "multi_tflops": round(flops / ms_multi / 1e9, 1), "one_gpu_ms": round(ms_one, 3),
+            "one_gpu_tflops": round(flops / ms_one / 1e9, 1), "device_error": bag.device_error()}
+
+
 def main() -> None:
     p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     p.add_argument("--n", type=int, default=4096)
@@ -87,10 +125,14 @@ def main() -> None:
     p.add_argument("--calls", type=int, default=3)
     p.add_argument("--sweep", action="store_true")
     p.add_argument("--math", default="ffma", choices=("ffma", "3xtf32"))
+    p.add_argument("--devices", default=None, help="comma-separated: time sgemm_multi over them")
     args = p.parse_args()
     import bag_b200 as bag
     bag.set_math_mode(args.math)
-    if args.sweep:
+    if args.devices:
+        devs = [int(x) for x in args.devices.split(",")]
+        print(json.dumps(run_multi(devs, args.n, args.depth, args.basis, args.calls)), flush=True)
+    elif args.sweep:
         print(json.dumps(run_sweep()), flush=True)
     else:
         run_case(args.n, args.depth, args.basis, args.calls)

@@ -18,6 +18,7 @@
  *   bag_sgemm_ex / bag_sgemm_batched      new: rectangular, ragged, row-major and batched problems
  *                                         (BASELINE configs 4 and 5); no reference counterpart
  *   bag_plan_dump                         new: the host plan as JSON, for tests of the plan builder
+ *   bag_sgemm_multi                       new: one process, several GPUs (row/column-band shards)
  */
 #ifndef BAG_CAPI_H
 #define BAG_CAPI_H
@@ -191,6 +192,31 @@ bag_status bag_selftest_bounded_wait(unsigned long long limit_ns, int* gave_up);
  * 4 x SM-count CTAs x 256 threads of register-only fmaf chains; `sink` must
  * hold 1024 x SM-count floats.  *flops receives the launch's FLOP count. */
 bag_status bag_ffma_probe(float* sink, int iterations, bag_stream_t stream, double* flops);
+
+/* Several GPUs of one process (the proposed bag_sgemm_multi): C <- A B +
+ * beta C with A, B, C on devices[0].  The devices form an R x S grid
+ * (bag_multi_grid: 1x1, 2x1, 2x2, 4x2 for 1, 2, 4, 8 devices, else n x 1);
+ * device (i, j) receives by peer copies row band i of every one of the
+ * 2^depth block-rows of A (and of C when beta is 1) and column band j of every
+ * block-column of B, runs the single-GPU path on those compact shards with its
+ * own workspace and stream, and its C bands are copied back.  BAG combines only
+ * blocks at equal offsets, so every device computes exactly the full product
+ * restricted to its bands: no reduction between devices.  Needs M divisible by
+ * 2^depth x R and N by 2^depth x S (of the column-major problem; row-major
+ * swaps M and N).  Asynchronous: ordered after earlier work on `stream`
+ * (devices[0]), and `stream` waits for every device.  The workspace is created
+ * for one problem shape, device list and the calling thread's math mode, and
+ * enables peer access between devices[0] and the others.  New; the reference
+ * has no multi-GPU path. */
+typedef struct bag_multi_workspace bag_multi_workspace;
+bag_status bag_multi_grid(int ngpus, int* rows, int* cols);
+bag_status bag_multi_workspace_create(int ngpus, const int* devices, int layout, int m, int n,
+                                      int k, int depth, int basis, bag_multi_workspace** out);
+bag_status bag_multi_workspace_destroy(bag_multi_workspace* ws);
+bag_status bag_sgemm_multi(int ngpus, const int* devices, int layout, int m, int n, int k,
+                           const float* a, long long lda, const float* b, long long ldb, float* c,
+                           long long ldc, float beta, int depth, int basis, bag_stream_t stream,
+                           bag_multi_workspace* ws);
 
 /* Describe the plan for a column-major problem as JSON (no GPU needed).
  * Pointers are reported as {base, offset}: base 0=A, 1=B, 2=C, 3=workspace.
