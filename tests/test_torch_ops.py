@@ -1,0 +1,68 @@
+"""PyTorch custom operators over the C ABI (bag_b200.torch_ops): registration,
+shape inference without a GPU, and on the GPU results, autograd, the in-place
+form and tracing by torch.compile (eager backend: dynamo only)."""
+
+from __future__ import annotations
+
+import pytest
+
+torch = pytest.importorskip("torch")
+import bag_b200.torch_ops  # noqa: E402,F401  (registers torch.ops.bag_b200.*)
+
+
+def test_ops_are_registered():
+    assert hasattr(torch.ops.bag_b200, "matmul")
+    assert hasattr(torch.ops.bag_b200, "sgemm_")
+
+
+def test_shape_inference_on_meta_tensors():
+    a = torch.empty(96, 40, device="meta")
+    b = torch.empty(40, 72, device="meta")
+    c = torch.ops.bag_b200.matmul(a, b, 1, "minimal", "ffma")
+    assert c.shape == (96, 72) and c.device.type == "meta"
+    with pytest.raises(Exception):
+        torch.ops.bag_b200.matmul(a, torch.empty(41, 72, device="meta"))
+
+
+def _rel(x, ref):
+    return float((x.double() - ref).norm() / ref.norm())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,k,n,depth,math", [(512, 512, 512, 1, "ffma"), (1000, 768, 520, 2, "ffma"),
+                                              (2048, 2048, 2048, 1, "3xtf32")])
+def test_matmul_op(cuda, m, k, n, depth, math):
+    g = torch.Generator(device="cuda").manual_seed(m + k + n)
+    a = torch.randn(m, k, device="cuda", generator=g)
+    b = torch.randn(k, n, device="cuda", generator=g)
+    c = torch.ops.bag_b200.matmul(a, b, depth, "minimal", math)
+    ref = a.double() @ b.double()
+    assert c.shape == (m, n) and _rel(c, ref) <= 1e-5
+    c2 = torch.randn(m, n, device="cuda", generator=g)
+    c2_ref = c2.double() + ref
+    torch.ops.bag_b200.sgemm_(c2, a, b, 1.0, depth, "minimal", math)
+    assert _rel(c2, c2_ref) <= 1e-5
+
+
+@pytest.mark.gpu
+def test_autograd_through_the_op(cuda):
+    g = torch.Generator(device="cuda").manual_seed(7)
+    a = torch.randn(256, 384, device="cuda", generator=g, requires_grad=True)
+    b = torch.randn(384, 320, device="cuda", generator=g, requires_grad=True)
+    w = torch.randn(256, 320, device="cuda", generator=g)
+    (torch.ops.bag_b200.matmul(a, b, 1, "minimal", "ffma") * w).sum().backward()
+    wd = w.double()
+    assert _rel(a.grad, wd @ b.detach().double().t()) <= 1e-5
+    assert _rel(b.grad, a.detach().double().t() @ wd) <= 1e-5
+
+
+@pytest.mark.gpu
+def test_traced_by_torch_compile(cuda):
+    def f(x, y):
+        return torch.ops.bag_b200.matmul(x, y, 1, "minimal", "ffma") + 1.0
+
+    compiled = torch.compile(f, backend="eager", fullgraph=True)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(512, 256, device="cuda", generator=g)
+    y = torch.randn(256, 384, device="cuda", generator=g)
+    assert _rel(compiled(x, y), x.double() @ y.double() + 1.0) <= 1e-5
