@@ -55,12 +55,7 @@ __device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned coun
 }
 
 __device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
-  unsigned long long state;
-  asm volatile("mbarrier.arrive.shared::cta.b64 %0, [%1];"
-               : "=l"(state)
-               : "r"(smem_u32(bar))
-               : "memory");
-  (void)state;
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // One try_wait; the thread may sleep up to `suspend_ns` for the phase to

@@ -179,10 +179,12 @@ def test_prepared_path_batched_and_accumulating(tensor_mode):
 # SMs (tcgen05.mma.cta_group::2, the default) and 128 x 256 tiles on one SM
 # (BAG_B200_PREP_KERNEL=single).  Same operands, same 32-k chunk folding:
 # both within the FFMA bound, and close to each other.  Shapes cover ragged
-# M/N (partial pair tiles), fewer tiles than clusters, and batches.
+# M/N (partial pair tiles), K tails that are not a multiple of the 32-k
+# stage, fewer tiles than clusters, and batches.
 @pytest.mark.parametrize("m,k,n,depth,batch", [
     (512, 2048, 768, 0, 1), (1032, 4096, 2056, 2, 1), (4096, 4096, 4096, 2, 1),
-    (1000, 2048, 1160, 1, 2), (300, 1024, 104, 0, 3)])
+    (1000, 2048, 1160, 1, 2), (300, 1024, 104, 0, 3),
+    (200, 1032, 136, 0, 1), (132, 1100, 260, 0, 2), (1536, 2064, 1032, 1, 1)])
 def test_pair_and_single_leaf_kernels(tensor_mode, monkeypatch, m, k, n, depth, batch):
     import torch
     bag = tensor_mode
