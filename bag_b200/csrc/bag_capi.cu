@@ -333,6 +333,54 @@ struct Builder {
     prep_region = alloc(prep_row_len, std::max(prep_rows, 1), int(stages.size()) + 1);
   }
 
+  // Deferred inverse transform (prepared path): when products update several
+  // C blocks each, every product instead stores its result once into its
+  // own workspace buffer and one pass (decode_kernel) adds the buffers into
+  // their C blocks -- each buffer read once, each block written once, in
+  // plan order -- instead of ~4 atomic read-modify-writes per output element.
+  struct Decode {
+    bool on = false;
+    bool overwrite = false;   // C = sum (beta 0) instead of C += sum
+    int m = 0, n = 0;
+    std::vector<View> targets;
+    std::vector<View> buffers;                               // one per leaf
+    std::vector<std::vector<std::pair<int, float>>> terms;   // per leaf: (target, coef)
+  } decode;
+
+  void defer_decode() {
+    if (leaves.empty() || leaves.size() > size_t(kMaxDecodeProducts)) return;
+    size_t outs = 0;
+    for (const HostLeaf& l : leaves) outs += l.out.size();
+    if (outs < 3 * leaves.size()) return;   // a store + a pass pays from ~3 targets a product
+    const int m = leaves[0].m, n = leaves[0].n;
+    std::vector<View> targets;
+    for (const HostLeaf& l : leaves) {
+      if (l.m != m || l.n != n) return;
+      for (size_t i = 0; i < l.out.size(); ++i) {
+        const Target& t = l.out[i];
+        if (t.mode != kOutAtomic || (t.coef != 1.f && t.coef != -1.f)) return;
+        for (size_t j = 0; j < i; ++j)
+          if (l.out[j].v == t.v) return;   // one coefficient per (product, block)
+        if (std::find(targets.begin(), targets.end(), t.v) == targets.end()) targets.push_back(t.v);
+      }
+    }
+    if (targets.size() > size_t(kMaxDecodeTargets)) return;
+    decode.on = true;
+    decode.m = m;
+    decode.n = n;
+    decode.targets = targets;
+    for (HostLeaf& l : leaves) {
+      const View buf = alloc(m, n, int(stages.size()) + 1);
+      std::vector<std::pair<int, float>> terms;
+      for (const Target& t : l.out)
+        terms.push_back({int(std::find(targets.begin(), targets.end(), t.v) - targets.begin()),
+                         t.coef});
+      decode.buffers.push_back(buf);
+      decode.terms.push_back(terms);
+      l.out = {{buf, 1.f, kOutOverwrite}};
+    }
+  }
+
   // Reduce an operand to a single unit-coefficient block.  A lone negated
   // block keeps its data; the sign moves to the outputs (exact).
   View single(const Expr& e, int rows, int cols, float* sign) {
@@ -446,7 +494,10 @@ void build_plan(const GemmDesc& g, float* ws, long long ws_bstride, Builder& B,
                           {{{C.p + (long long)nc * C.ld, C.ld, C.bstride}, 1.f, kOutAtomic}}});
   }
   // Last, so every leaf (peeling strips included) gets its prepared operands.
-  if (leaf_operands) B.prepare_leaf_operands(prep_row_align());
+  if (leaf_operands) {
+    B.prepare_leaf_operands(prep_row_align());
+    B.defer_decode();
+  }
 }
 
 // Workspace elements per batch entry (dry run with a fake base).
@@ -621,6 +672,26 @@ void run_prepared(Builder& B, int batch, cudaStream_t stream) {
     if (lp.nprod) ++g_launches;
   }
   if (g_prof_end) cuda_check(cudaEventRecord(g_prof_end, stream), "cudaEventRecord");
+  if (B.decode.on) {
+    const Builder::Decode& d = B.decode;
+    DecodePlan dp;
+    std::memset(&dp, 0, sizeof(dp));
+    dp.np = int(d.buffers.size());
+    dp.nt = int(d.targets.size());
+    dp.accumulate = d.overwrite ? 0 : 1;
+    dp.m = d.m;
+    dp.n = d.n;
+    for (int p = 0; p < dp.np; ++p) {
+      dp.in[p] = make_term(d.buffers[p], 1.f, 0);
+      for (const auto& tc : d.terms[p]) {
+        const int t = tc.first;
+        dp.list[t][dp.count[t]++] = static_cast<signed char>(tc.second > 0 ? p + 1 : -(p + 1));
+      }
+    }
+    for (int t = 0; t < dp.nt; ++t) dp.out[t] = make_term(d.targets[t], 1.f, 0);
+    cuda_check(launch_decode(dp, batch, stream), "decode launch");
+    ++g_launches;
+  }
 }
 
 // `sources` lists the whole operand matrices (A, B) the tensor-core path may
@@ -740,13 +811,16 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
   if (!g.a || !g.b || !g.c) fail(BAG_ERR_INVALID, "null matrix pointer");
   if (g.lda < std::max(1, g.m) || g.ldb < std::max(1, g.k) || g.ldc < std::max(1, g.m))
     fail(BAG_ERR_INVALID, "leading dimension smaller than the row count");
-  if (beta == 0.f) {
+  auto zero_c = [&] {
     for (int i = 0; i < g.batch; ++i)
       cuda_check(cudaMemset2DAsync(g.c + (long long)i * g.sc, size_t(g.ldc) * sizeof(float), 0,
                                    size_t(g.m) * sizeof(float), size_t(g.n), stream),
                  "cudaMemset2DAsync");
+  };
+  if (g.k == 0) {
+    if (beta == 0.f) zero_c();
+    return;
   }
-  if (g.k == 0) return;
   // 3xTF32 mode prepares the leaf operands when the workspace was sized for
   // it (created in that mode); otherwise the prologue stays fused.
   bool leaf_operands = leaf_materialisation_wanted(g);
@@ -767,6 +841,13 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
   build_plan(g, base ? base : reinterpret_cast<float*>(uintptr_t(1) << 44), (long long)need, B,
              leaf_operands);
   if (B.ws_used != need) fail(BAG_ERR_INTERNAL, "plan size changed between passes");
+  // With the deferred decode every C block is written once by the decode
+  // pass (no peeled strips: all leaves share one shape), so C = A B needs no
+  // zeroing -- the pass overwrites instead of accumulating.
+  if (beta == 0.f) {
+    if (B.decode.on) B.decode.overwrite = true;
+    else zero_c();
+  }
   const std::vector<TcSource> sources = {{g.a, g.lda, g.sa, g.m, g.k}, {g.b, g.ldb, g.sb, g.k, g.n}};
   execute_plan(B, g.batch, stream, sources);
 }
@@ -892,7 +973,10 @@ std::string dump_plan(int m, int n, int k, long long lda, long long ldb, long lo
     s += "],\"prep_l\":" + std::to_string(l.prep_l) + ",\"prep_r\":" + std::to_string(l.prep_r) +
          "}";
   }
-  s += "],\"prepared_row_len\":" + std::to_string(B.prep_row_len) + ",\"prepared\":[";
+  s += "],\"decode\":{\"deferred\":" + std::string(B.decode.on ? "true" : "false") +
+       ",\"products\":" + std::to_string(B.decode.buffers.size()) + ",\"targets\":" +
+       std::to_string(B.decode.targets.size()) + "}";
+  s += ",\"prepared_row_len\":" + std::to_string(B.prep_row_len) + ",\"prepared\":[";
   for (size_t i = 0; i < B.prep.size(); ++i) {
     const Builder::PrepOp& o = B.prep[i];
     s += i ? "," : "";

@@ -81,6 +81,10 @@ cudaError_t run_wait_selftest(unsigned long long limit_ns, int* gave_up_device,
 // Reads and clears the device error word that bounded waits set on timeout.
 cudaError_t read_and_clear_device_error(unsigned* value);
 
+// The deferred inverse transform: out[t] += sum_p coef[p][t] * in[p] over
+// m x n blocks (column-major, 16-byte aligned, ld % 4 == 0).
+cudaError_t launch_decode(const DecodePlan& plan, int batch, cudaStream_t stream);
+
 // One launch of every materialisation job in `plan`.
 cudaError_t launch_materialize(const MatPlan& plan, int batch, cudaStream_t stream, int sm_count);
 

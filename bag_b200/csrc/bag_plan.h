@@ -128,7 +128,26 @@ struct PrepLeafPlan {
   Term outs[kMaxTerms];
 };
 
+// Deferred inverse transform (prepared 3xTF32 path, several C blocks per
+// product): the leaf kernel stores each product once into its own buffer
+// M_p, then one pass adds every product into its C blocks, out[t] +=
+// sum_p coef[p][t] * M_p, reading each M_p once and writing each block once.
+// All products and targets share the extent m x n.
+constexpr int kMaxDecodeProducts = 64;
+constexpr int kMaxDecodeTargets = 16;
+
+struct DecodePlan {
+  int np, nt, m, n;
+  int accumulate;                  // 1: out[t] += sum; 0: out[t] = sum
+  Term in[kMaxDecodeProducts];     // M_p (coef unused)
+  Term out[kMaxDecodeTargets];     // C blocks (coef unused)
+  // Per target, its products in plan order: +-(p + 1); count[t] of them.
+  signed char list[kMaxDecodeTargets][kMaxDecodeProducts];
+  int count[kMaxDecodeTargets];
+};
+
 static_assert(sizeof(LeafPlan) < 32000, "kernel parameter limit");
+static_assert(sizeof(DecodePlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(MatPlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(PrepPlan) < 32000, "kernel parameter limit");
 
