@@ -700,8 +700,9 @@ def read_traffic(name: str):
         with open(path) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_full_launch:"):
-                    return float(line.split(":", 1)[1])
-    except OSError:
+                    fields = line.split(":", 1)[1].split()
+                    return float(fields[0]) if fields else None
+    except (OSError, ValueError):
         pass
     return None
 
