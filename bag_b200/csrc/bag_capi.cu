@@ -599,30 +599,72 @@ int prep_leaf_kind() {
 
 void run_prepared(Builder& B, int batch, cudaStream_t stream) {
   const int tile = prep_row_align();
-  for (size_t j0 = 0; j0 < B.prep.size(); j0 += kMaxPrepJobs) {
-    PrepPlan pp{};
+  // Group the prepared operands that are sums of the same few blocks, so a
+  // source block is read once per tile for all of them.
+  struct HostGroup {
+    int rows, cols;
+    bool transpose;
+    std::vector<View> in;
+    std::vector<int> ops;   // indices into B.prep
+  };
+  std::vector<HostGroup> groups;
+  for (size_t j = 0; j < B.prep.size(); ++j) {
+    const Builder::PrepOp& o = B.prep[j];
+    if (o.terms.empty() || o.terms.size() > size_t(kMaxOperandTerms))
+      fail(BAG_ERR_INTERNAL, "prepared operand has an unsupported term count");
+    HostGroup* home = nullptr;
+    for (HostGroup& g : groups) {
+      if (g.rows != o.rows || g.cols != o.cols || g.transpose != o.transpose ||
+          g.ops.size() >= size_t(kMaxPrepGroupOut))
+        continue;
+      size_t fresh = 0;
+      for (const STerm& t : o.terms)
+        if (std::find(g.in.begin(), g.in.end(), t.v) == g.in.end()) ++fresh;
+      if (g.in.size() + fresh <= size_t(kMaxPrepGroupIn)) {
+        home = &g;
+        break;
+      }
+    }
+    if (!home) {
+      groups.push_back({o.rows, o.cols, o.transpose, {}, {}});
+      home = &groups.back();
+    }
+    for (const STerm& t : o.terms)
+      if (std::find(home->in.begin(), home->in.end(), t.v) == home->in.end()) home->in.push_back(t.v);
+    home->ops.push_back(int(j));
+  }
+  for (size_t g0 = 0; g0 < groups.size(); g0 += kMaxPrepGroups) {
+    PrepGroupPlan pp;
+    std::memset(&pp, 0, sizeof(pp));
     pp.row_len = B.prep_row_len;
     pp.region = const_cast<float*>(B.prep_region.p);
     pp.region_bstride = B.ws_bstride;
     long long tiles = 0;
-    for (size_t j = j0; j < std::min(B.prep.size(), j0 + kMaxPrepJobs); ++j) {
-      const Builder::PrepOp& o = B.prep[j];
-      PrepJob& J = pp.job[pp.njobs++];
-      J.rows = o.rows;
-      J.cols = o.cols;
-      J.nterms = int(o.terms.size());
-      J.transpose = o.transpose ? 1 : 0;
-      if (J.nterms < 1 || J.nterms > kMaxOperandTerms)
-        fail(BAG_ERR_INTERNAL, "prepared operand has an unsupported term count");
-      for (int t = 0; t < J.nterms; ++t) J.in[t] = make_term(o.terms[t].v, o.terms[t].coef, 0);
-      J.out_hi = o.hi_row;
-      J.out_lo = o.hi_row + o.rows;
-      J.tile_begin = tiles;
-      tiles += (long long)((o.rows + tile - 1) / tile) * (B.prep_row_len / tile);
+    for (size_t gi = g0; gi < std::min(groups.size(), g0 + kMaxPrepGroups); ++gi) {
+      const HostGroup& hg = groups[gi];
+      PrepGroup& G = pp.group[pp.ngroups++];
+      G.rows = hg.rows;
+      G.cols = hg.cols;
+      G.transpose = hg.transpose ? 1 : 0;
+      G.nin = int(hg.in.size());
+      for (int u = 0; u < G.nin; ++u) G.in[u] = make_term(hg.in[u], 1.f, 0);
+      G.nout = int(hg.ops.size());
+      for (int q = 0; q < G.nout; ++q) {
+        const Builder::PrepOp& o = B.prep[hg.ops[q]];
+        G.out_hi[q] = o.hi_row;
+        for (size_t t = 0; t < o.terms.size(); ++t) {
+          const int u = int(std::find(hg.in.begin(), hg.in.end(), o.terms[t].v) - hg.in.begin());
+          if (o.terms[t].coef != 1.f && o.terms[t].coef != -1.f)
+            fail(BAG_ERR_INTERNAL, "prepared operand term coefficient is not +-1");
+          G.expr[q][t] = static_cast<signed char>(o.terms[t].coef > 0 ? u + 1 : -(u + 1));
+        }
+      }
+      G.tile_begin = tiles;
+      tiles += (long long)((hg.rows + tile - 1) / tile) * (B.prep_row_len / tile);
     }
     pp.ntiles = tiles;
     if (tiles > INT32_MAX) fail(BAG_ERR_SHAPE, "problem too large");
-    cuda_check(launch_prep(pp, batch, stream), "prepare launch");
+    cuda_check(launch_prep_groups(pp, batch, stream), "prepare launch");
     ++g_launches;
   }
   if (g_prof_start) cuda_check(cudaEventRecord(g_prof_start, stream), "cudaEventRecord");

@@ -112,6 +112,33 @@ struct PrepPlan {
   PrepJob job[kMaxPrepJobs];
 };
 
+// Prepare groups: operands that are signed sums of the same few source
+// blocks -- the 7 leaf operands of one outer product at depth 2, the 7 made
+// of A's (or B's) quadrants at depth 1 -- are prepared together, each source
+// block read once per tile.  expr[o]: output o's terms, signed (input index
+// + 1), in the prologue's order (the first with its sign, then fmaf); 0 ends.
+constexpr int kMaxPrepGroupIn = 4;
+constexpr int kMaxPrepGroupOut = 8;
+constexpr int kMaxPrepGroups = 24;
+
+struct PrepGroup {
+  int rows, cols;
+  int transpose, nin, nout;
+  Term in[kMaxPrepGroupIn];                                // coef unused
+  int out_hi[kMaxPrepGroupOut];                            // lo rows at out_hi + rows
+  signed char expr[kMaxPrepGroupOut][kMaxOperandTerms];
+  long long tile_begin;                                    // first work item of the group
+};
+
+struct PrepGroupPlan {
+  int ngroups;
+  int row_len;                 // floats per region row (k, padded to the stage length)
+  float* region;
+  long long region_bstride;    // floats between batch entries' regions
+  long long ntiles;
+  PrepGroup group[kMaxPrepGroups];
+};
+
 // Leaf products on prepared operands: A rows a_hi.., B rows b_hi.. of the
 // region; outputs as in LeafPlan.
 struct PrepProd {
@@ -150,5 +177,6 @@ static_assert(sizeof(LeafPlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(DecodePlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(MatPlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(PrepPlan) < 32000, "kernel parameter limit");
+static_assert(sizeof(PrepGroupPlan) < 32000, "kernel parameter limit");
 
 }  // namespace bag_b200

@@ -355,6 +355,120 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ PrepP
   }
 }
 
+// ---- prepare groups ---------------------------------------------------------
+// One CTA (256 threads) writes a 64-row x 64-k tile of every operand of a
+// group: each thread loads its 4 rows x 4 k of every input block once, then
+// evaluates each output's signed sum in the prologue's order, splits it into
+// TF32 hi/lo and stores both (left operands through a shared-memory
+// transpose, one output at a time).
+__device__ __forceinline__ float4 group_eval(const signed char (&e)[kMaxOperandTerms],
+                                             const float4 (&x)[kMaxPrepGroupIn]) {
+  auto pick = [&](int code) {
+    const int u = (code > 0 ? code : -code) - 1;
+    float4 r = x[0];
+#pragma unroll
+    for (int i = 1; i < kMaxPrepGroupIn; ++i)
+      if (u == i) r = x[i];
+    return r;
+  };
+  float4 v = pick(e[0]);
+  if (e[0] < 0) v = make_float4(-v.x, -v.y, -v.z, -v.w);
+#pragma unroll
+  for (int t = 1; t < kMaxOperandTerms; ++t) {
+    if (e[t] == 0) break;
+    const float4 y = pick(e[t]);
+    const float c = e[t] > 0 ? 1.f : -1.f;
+    v = make_float4(fmaf(c, y.x, v.x), fmaf(c, y.y, v.y), fmaf(c, y.z, v.z), fmaf(c, y.w, v.w));
+  }
+  return v;
+}
+
+// 4 consecutive elements starting at element a + b * ld of input u, those at
+// a + q >= lim read as zero (a + 3 < lim: one 16-byte load).
+__device__ __forceinline__ float4 group_load(const PrepGroup& G, int u, long long batch,
+                                             long long a, long long b, long long lim) {
+  const Term& T = G.in[u];
+  const float* p = T.p + batch * T.bstride + a + b * T.ld;
+  if (a + 3 < lim) return load4(p);
+  float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    if (a + q < lim) e[q] = p[q];
+  return make_float4(e[0], e[1], e[2], e[3]);
+}
+
+__global__ void __launch_bounds__(256) prep_group_kernel(const __grid_constant__ PrepGroupPlan plan) {
+  __shared__ float tile[2][kPrepTile][kPrepTile + 1];   // [hi/lo][k][row] (transposed path)
+  const long long item = blockIdx.x;
+  int gi = 0;
+  while (gi + 1 < plan.ngroups && plan.group[gi + 1].tile_begin <= item) ++gi;
+  const PrepGroup& G = plan.group[gi];
+  const long long local = item - G.tile_begin;
+  const int ktiles = plan.row_len / kPrepTile;
+  const int r0 = int(local / ktiles) * kPrepTile, k0 = int(local % ktiles) * kPrepTile;
+  const long long batch = blockIdx.y;
+  const int t4 = (threadIdx.x % 16) * 4, t16 = threadIdx.x / 16;
+  float* region = plan.region + batch * plan.region_bstride;
+  const long long ld = plan.row_len;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (G.transpose) {
+    // Left operands: element (r, k) at p + r + k*ld; each thread holds rows
+    // r0 + t4 .. +3 of k columns k0 + t16 + 16i.
+    float4 x[4][kMaxPrepGroupIn];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = k0 + t16 + 16 * i, r = r0 + t4;
+#pragma unroll
+      for (int u = 0; u < kMaxPrepGroupIn; ++u)
+        x[i][u] = u < G.nin && k < G.cols && r < G.rows ? group_load(G, u, batch, r, k, G.rows)
+                                                         : zero;
+    }
+    for (int o = 0; o < G.nout; ++o) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int kk = t16 + 16 * i;
+        const float4 v = group_eval(G.expr[o], x[i]);
+        const float4 h = hi4(v), l = lo4(v, h);
+        tile[0][kk][t4 + 0] = h.x; tile[0][kk][t4 + 1] = h.y;
+        tile[0][kk][t4 + 2] = h.z; tile[0][kk][t4 + 3] = h.w;
+        tile[1][kk][t4 + 0] = l.x; tile[1][kk][t4 + 1] = l.y;
+        tile[1][kk][t4 + 2] = l.z; tile[1][kk][t4 + 3] = l.w;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int rr = t16 + 16 * i, r = r0 + rr;
+        if (r >= G.rows) continue;
+        const float4 h = make_float4(tile[0][t4][rr], tile[0][t4 + 1][rr], tile[0][t4 + 2][rr],
+                                     tile[0][t4 + 3][rr]);
+        const float4 l = make_float4(tile[1][t4][rr], tile[1][t4 + 1][rr], tile[1][t4 + 2][rr],
+                                     tile[1][t4 + 3][rr]);
+        *reinterpret_cast<float4*>(region + (long long)(G.out_hi[o] + r) * ld + k0 + t4) = h;
+        *reinterpret_cast<float4*>(region + (long long)(G.out_hi[o] + G.rows + r) * ld + k0 + t4) = l;
+      }
+      __syncthreads();   // the next output reuses the tile
+    }
+  } else {
+    // Right operands: element (k, n) at p + k + n*ld; read and write along k.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = r0 + t16 + 16 * i, k = k0 + t4;
+      if (r >= G.rows) continue;
+      float4 x[kMaxPrepGroupIn];
+#pragma unroll
+      for (int u = 0; u < kMaxPrepGroupIn; ++u)
+        x[u] = u < G.nin && k < G.cols ? group_load(G, u, batch, k, r, G.cols) : zero;
+      for (int o = 0; o < G.nout; ++o) {
+        const float4 v = group_eval(G.expr[o], x);
+        const float4 h = hi4(v);
+        *reinterpret_cast<float4*>(region + (long long)(G.out_hi[o] + r) * ld + k) = h;
+        *reinterpret_cast<float4*>(region + (long long)(G.out_hi[o] + G.rows + r) * ld + k) =
+            lo4(v, h);
+      }
+    }
+  }
+}
+
 // ---- leaf products on prepared operands -------------------------------------
 // Persistent: CTA b processes work items b, b + gridDim.x, ... (item = batch *
 // ntiles + tile); the stage and chunk rings run on across items, so the fold
@@ -974,6 +1088,12 @@ bool prep_supported() { return encode_fn() != nullptr; }
 bool prep_pair_supported() { return prep_supported() && pair_clusters() > 0; }
 
 int prep_row_align() { return kPrepTile; }   // a multiple of the 32-k stage
+
+cudaError_t launch_prep_groups(const PrepGroupPlan& plan, int batch, cudaStream_t stream) {
+  if (plan.ngroups == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
+  prep_group_kernel<<<dim3(unsigned(plan.ntiles), batch), 256, 0, stream>>>(plan);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_prep(const PrepPlan& plan, int batch, cudaStream_t stream) {
   if (plan.njobs == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
