@@ -69,7 +69,6 @@ bool prep_supported();
 bool prep_pair_supported();
 int prep_row_align();
 TileShape prep_tile_shape(int kind);
-cudaError_t launch_prep(const PrepPlan& plan, int batch, cudaStream_t stream);
 cudaError_t launch_prep_groups(const PrepGroupPlan& plan, int batch, cudaStream_t stream);
 cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* region,
                              long long row_len, long long rows, long long region_bstride,

@@ -86,37 +86,18 @@ struct MatPlan {
   MatJob job[kMaxJobs];
 };
 
-// Prepared-operand jobs (3xTF32 path): each writes one leaf operand -- the
-// signed sum of its terms, in the fused prologue's order -- as TF32 hi and lo
-// rows of `cols` k values (k contiguous, zero-padded to the region's row
-// length) at rows [out_hi, out_hi + rows) and [out_lo, out_lo + rows) of the
-// prepared region.  A left operand (column-major rows x cols, rows contiguous)
-// is transposed on the way; a right operand (column-major cols x rows, k
-// contiguous) keeps its orientation.
-constexpr int kMaxPrepJobs = 32;
-
-struct PrepJob {
-  int rows, cols;
-  int nterms, transpose;
-  Term in[kMaxOperandTerms];   // coef: +1 / -1
-  int out_hi, out_lo;          // region rows
-  long long tile_begin;        // first work item of this job
-};
-
-struct PrepPlan {
-  int njobs;
-  int row_len;                 // floats per region row (k, padded to the stage length)
-  float* region;
-  long long region_bstride;    // floats between batch entries' regions
-  long long ntiles;
-  PrepJob job[kMaxPrepJobs];
-};
-
-// Prepare groups: operands that are signed sums of the same few source
-// blocks -- the 7 leaf operands of one outer product at depth 2, the 7 made
-// of A's (or B's) quadrants at depth 1 -- are prepared together, each source
-// block read once per tile.  expr[o]: output o's terms, signed (input index
-// + 1), in the prologue's order (the first with its sign, then fmaf); 0 ends.
+// Prepared operands (3xTF32 path): every distinct leaf operand -- the signed
+// sum of its blocks, in the fused prologue's order -- is written as TF32 hi
+// and lo rows of `cols` k values (k contiguous, zero-padded to the region's
+// row length) at rows [out_hi, out_hi + rows) and [out_hi + rows, out_hi +
+// 2 rows) of the prepared region; a left operand (column-major rows x cols,
+// rows contiguous) is transposed on the way, a right operand (k contiguous)
+// keeps its orientation.  Operands that are signed sums of the same few
+// source blocks -- the 7 leaf operands of one outer product at depth 2, the 7
+// made of A's (or B's) quadrants at depth 1 -- form a group and are prepared
+// together, each source block read once per tile.  expr[o]: output o's terms,
+// signed (input index + 1), in the prologue's order (the first with its sign,
+// then fmaf); 0 ends.
 constexpr int kMaxPrepGroupIn = 4;
 constexpr int kMaxPrepGroupOut = 8;
 constexpr int kMaxPrepGroups = 24;
@@ -176,7 +157,6 @@ struct DecodePlan {
 static_assert(sizeof(LeafPlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(DecodePlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(MatPlan) < 32000, "kernel parameter limit");
-static_assert(sizeof(PrepPlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(PrepGroupPlan) < 32000, "kernel parameter limit");
 
 }  // namespace bag_b200

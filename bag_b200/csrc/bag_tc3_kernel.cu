@@ -1,11 +1,13 @@
 // Prepared-operand 3xTF32 path of the BAG FP32 matmul (sm_100a).
 //
-// prep_kernel: one HBM-speed pass writes every distinct leaf operand of the
-//   plan -- the signed sum of its blocks, in the fused prologue's order
+// prep_group_kernel: one HBM-speed pass writes every distinct leaf operand of
+//   the plan -- the signed sum of its blocks, in the fused prologue's order
 //   (x + delta*y, bag.cuh:69-73) -- as TF32 hi = rn_tf32(x) and
 //   lo = rn_tf32(x - hi) rows of a workspace region, k contiguous (left
 //   operands are transposed on the way through a shared-memory tile) and
-//   zero-padded to the region's row length (a multiple of the 64-k tile).
+//   zero-padded to the region's row length (a multiple of the 64-k tile);
+//   operands made of the same source blocks are written together, each block
+//   read once per tile.
 //
 // leaf_prep_kernel<BN>: persistent (one CTA per SM); each CTA computes 128 x BN
 //   output tiles of the leaf products in turn, straight from the region:
@@ -232,20 +234,6 @@ struct Ring {
   }
 };
 
-// Signed sum of a job's terms at element (r, k) of the operand, in the fused
-// prologue's order: the first term with its sign, then fmaf(coef, x, acc).
-__device__ __forceinline__ float operand_sum(const PrepJob& J, long long batch, long long off_r,
-                                             long long k) {
-  const Term& T0 = J.in[0];
-  const float x0 = T0.p[batch * T0.bstride + off_r + k * T0.ld];
-  float v = T0.coef < 0.f ? -x0 : x0;
-  for (int t = 1; t < J.nterms; ++t) {
-    const Term& T = J.in[t];
-    v = fmaf(T.coef, T.p[batch * T.bstride + off_r + k * T.ld], v);
-  }
-  return v;
-}
-
 }  // namespace
 
 // ---- prepare pass ---------------------------------------------------------
@@ -255,104 +243,12 @@ __device__ __forceinline__ float4 load4(const float* p) {
   return *reinterpret_cast<const float4*>(p);
 }
 
-// Signed sum of the job's terms over the 4 consecutive elements starting at
-// element a + b*ld of each term (its own ld; all 16-byte aligned).
-__device__ __forceinline__ float4 sum4(const PrepJob& J, long long batch, long long a, long long b) {
-  const Term& T0 = J.in[0];
-  float4 v = load4(T0.p + batch * T0.bstride + a + b * T0.ld);
-  if (T0.coef < 0.f) v = make_float4(-v.x, -v.y, -v.z, -v.w);
-  for (int t = 1; t < J.nterms; ++t) {
-    const Term& T = J.in[t];
-    const float4 x = load4(T.p + batch * T.bstride + a + b * T.ld);
-    v = make_float4(fmaf(T.coef, x.x, v.x), fmaf(T.coef, x.y, v.y), fmaf(T.coef, x.z, v.z),
-                    fmaf(T.coef, x.w, v.w));
-  }
-  return v;
-}
-
 __device__ __forceinline__ float4 hi4(float4 v) {
   return make_float4(tf32_rn(v.x), tf32_rn(v.y), tf32_rn(v.z), tf32_rn(v.w));
 }
 __device__ __forceinline__ float4 lo4(float4 v, float4 h) {
   return make_float4(tf32_rn(v.x - h.x), tf32_rn(v.y - h.y), tf32_rn(v.z - h.z),
                      tf32_rn(v.w - h.w));
-}
-
-__global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ PrepPlan plan) {
-  __shared__ float tile[2][kPrepTile][kPrepTile + 1];   // [hi/lo][k][row] (transposed path)
-  const long long item = blockIdx.x;
-  int j = 0;
-  while (j + 1 < plan.njobs && plan.job[j + 1].tile_begin <= item) ++j;
-  const PrepJob& J = plan.job[j];
-  const long long local = item - J.tile_begin;
-  const int ktiles = plan.row_len / kPrepTile;
-  const int r0 = int(local / ktiles) * kPrepTile, k0 = int(local % ktiles) * kPrepTile;
-  const long long batch = blockIdx.y;
-  const int t4 = (threadIdx.x % 16) * 4, t16 = threadIdx.x / 16;
-  float* region = plan.region + batch * plan.region_bstride;
-  const long long ld = plan.row_len;
-  if (J.transpose) {
-    // Left operand: element (r, k) at p + r + k*ld.  Read 4 rows of one k
-    // column per thread, split, transpose through shared memory.
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int kk = t16 + 16 * i, r = r0 + t4, k = k0 + kk;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k < J.cols) {
-        if (r + 3 < J.rows) {
-          v = sum4(J, batch, r, k);
-        } else {
-          float e[4] = {0.f, 0.f, 0.f, 0.f};
-          for (int q = 0; q < 4 && r + q < J.rows; ++q) e[q] = operand_sum(J, batch, r + q, k);
-          v = make_float4(e[0], e[1], e[2], e[3]);
-        }
-      }
-      const float4 h = hi4(v), l = lo4(v, h);
-      tile[0][kk][t4 + 0] = h.x; tile[0][kk][t4 + 1] = h.y;
-      tile[0][kk][t4 + 2] = h.z; tile[0][kk][t4 + 3] = h.w;
-      tile[1][kk][t4 + 0] = l.x; tile[1][kk][t4 + 1] = l.y;
-      tile[1][kk][t4 + 2] = l.z; tile[1][kk][t4 + 3] = l.w;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int rr = t16 + 16 * i, r = r0 + rr;
-      if (r >= J.rows) continue;
-      const float4 h = make_float4(tile[0][t4][rr], tile[0][t4 + 1][rr], tile[0][t4 + 2][rr],
-                                   tile[0][t4 + 3][rr]);
-      const float4 l = make_float4(tile[1][t4][rr], tile[1][t4 + 1][rr], tile[1][t4 + 2][rr],
-                                   tile[1][t4 + 3][rr]);
-      *reinterpret_cast<float4*>(region + (long long)(J.out_hi + r) * ld + k0 + t4) = h;
-      *reinterpret_cast<float4*>(region + (long long)(J.out_lo + r) * ld + k0 + t4) = l;
-    }
-  } else {
-    // Right operand: element (k, n) at p + k + n*ld; read and write along k.
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int rr = t16 + 16 * i, r = r0 + rr, k = k0 + t4;
-      if (r >= J.rows) continue;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k + 3 < J.cols) {
-        v = sum4(J, batch, k, r);
-      } else if (k < J.cols) {
-        float e[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int q = 0; q < 4 && k + q < J.cols; ++q) {
-          const Term& T0 = J.in[0];
-          const float x0 = T0.p[batch * T0.bstride + k + q + (long long)r * T0.ld];
-          float acc = T0.coef < 0.f ? -x0 : x0;
-          for (int t = 1; t < J.nterms; ++t) {
-            const Term& T = J.in[t];
-            acc = fmaf(T.coef, T.p[batch * T.bstride + k + q + (long long)r * T.ld], acc);
-          }
-          e[q] = acc;
-        }
-        v = make_float4(e[0], e[1], e[2], e[3]);
-      }
-      const float4 h = hi4(v);
-      *reinterpret_cast<float4*>(region + (long long)(J.out_hi + r) * ld + k) = h;
-      *reinterpret_cast<float4*>(region + (long long)(J.out_lo + r) * ld + k) = lo4(v, h);
-    }
-  }
 }
 
 // ---- prepare groups ---------------------------------------------------------
@@ -1092,12 +988,6 @@ int prep_row_align() { return kPrepTile; }   // a multiple of the 32-k stage
 cudaError_t launch_prep_groups(const PrepGroupPlan& plan, int batch, cudaStream_t stream) {
   if (plan.ngroups == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
   prep_group_kernel<<<dim3(unsigned(plan.ntiles), batch), 256, 0, stream>>>(plan);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_prep(const PrepPlan& plan, int batch, cudaStream_t stream) {
-  if (plan.njobs == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
-  prep_kernel<<<dim3(unsigned(plan.ntiles), batch), 256, 0, stream>>>(plan);
   return cudaGetLastError();
 }
 
