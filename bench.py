@@ -619,8 +619,10 @@ def run_bag(args) -> None:
             tf32 = peaks.get("bf16_tflops", 1590.0) / 2.0
             sustained = peaks.get("bf16_tflops_sustained", 1400.0) / 2.0
             # The workspace was created in 3xTF32 mode, so the call runs the
-            # prepare pass (prep_kernel) and then the leaf kernel on the
-            # prepared operands; the leaf events bracket the leaf launches only.
+            # prepare pass (prep_group_kernel), the leaf kernel on the prepared
+            # operands and, at depth 2, the deferred decode; the leaf events
+            # bracket the leaf launches only ("prepare_and_materialise_ms" is
+            # the rest of the call).
             kernels = {
                 "tf32_pair": ("leaf_pair_kernel (3xTF32 tcgen05.mma.cta_group::2, 256x256 tiles "
                               "on SM pairs, prepared TF32 hi/lo operands)",
