@@ -264,3 +264,26 @@ def test_deferred_decode(tensor_mode, m, n, beta):
     bag.sgemm(a, b, c2, beta=beta, depth=2, workspace=ws)
     torch.cuda.synchronize()
     assert torch.equal(c, c2)
+
+
+# Depth 3 on the prepared path: 343 products over several leaf launches and
+# prepare-group launches (the decode stays fused: more products than the
+# deferred pass takes).
+def test_prepared_depth3(tensor_mode):
+    import torch
+    bag = tensor_mode
+    n = 8192
+    dump = bag.plan_dump(n, n, n, n, n, n, depth=3)
+    assert len(dump["prepared"]) > 0 and not dump["decode"]["deferred"]
+    a, b = _operands(torch, n, n, n, seed=33)
+    ws = bag.Workspace.for_problem(n, n, n, 3)
+    c, path = _sgemm(bag, torch, a, b, 3, "minimal", ws, "3xtf32")
+    assert path == "3xtf32" and bag.last_leaf_kernel() == "tf32_pair" and bag.device_error() == 0
+    exact = a.double() @ b.double()
+    err = float((c.double() - exact).norm() / exact.norm())
+    bag.set_math_mode("ffma")
+    ws_f = bag.Workspace.for_problem(n, n, n, 3)
+    c_f, _ = _sgemm(bag, torch, a, b, 3, "minimal", ws_f, "ffma")
+    bag.set_math_mode("3xtf32")
+    ffma = float((c_f.double() - exact).norm() / exact.norm())
+    assert err <= min(1.25 * ffma, 1e-4), (err, ffma)
