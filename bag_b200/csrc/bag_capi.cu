@@ -331,6 +331,57 @@ struct Builder {
       l.prep_r = prep_index(l.right, l.n, l.k, false);
     }
     prep_region = alloc(prep_row_len, std::max(prep_rows, 1), int(stages.size()) + 1);
+    group_prepared();
+  }
+
+  // Prepare groups: prepared operands of one shape that are sums of the same
+  // few source blocks share a group, so prep_group_kernel reads each source
+  // block once per tile for all of them.  First fit, in prep order; each
+  // output keeps its operand's term order (expr codes: +-(input index + 1)).
+  struct PrepGroupHost {
+    int rows, cols;
+    bool transpose;
+    std::vector<View> in;
+    std::vector<int> ops;                  // indices into prep
+    std::vector<std::vector<int>> expr;    // per output, its terms as input codes
+  };
+  std::vector<PrepGroupHost> prep_groups;
+
+  void group_prepared() {
+    prep_groups.clear();
+    for (size_t j = 0; j < prep.size(); ++j) {
+      const PrepOp& o = prep[j];
+      if (o.terms.empty() || o.terms.size() > size_t(kMaxOperandTerms))
+        fail(BAG_ERR_INTERNAL, "prepared operand has an unsupported term count");
+      PrepGroupHost* home = nullptr;
+      for (PrepGroupHost& g : prep_groups) {
+        if (g.rows != o.rows || g.cols != o.cols || g.transpose != o.transpose ||
+            g.ops.size() >= size_t(kMaxPrepGroupOut))
+          continue;
+        size_t fresh = 0;
+        for (const STerm& t : o.terms)
+          if (std::find(g.in.begin(), g.in.end(), t.v) == g.in.end()) ++fresh;
+        if (g.in.size() + fresh <= size_t(kMaxPrepGroupIn)) {
+          home = &g;
+          break;
+        }
+      }
+      if (!home) {
+        prep_groups.push_back({o.rows, o.cols, o.transpose, {}, {}, {}});
+        home = &prep_groups.back();
+      }
+      std::vector<int> codes;
+      for (const STerm& t : o.terms) {
+        auto it = std::find(home->in.begin(), home->in.end(), t.v);
+        if (it == home->in.end()) it = home->in.insert(home->in.end(), t.v);
+        if (t.coef != 1.f && t.coef != -1.f)
+          fail(BAG_ERR_INTERNAL, "prepared operand term coefficient is not +-1");
+        const int u = int(it - home->in.begin());
+        codes.push_back(t.coef > 0 ? u + 1 : -(u + 1));
+      }
+      home->ops.push_back(int(j));
+      home->expr.push_back(codes);
+    }
   }
 
   // Deferred inverse transform (prepared path): when products update several
@@ -599,40 +650,7 @@ int prep_leaf_kind() {
 
 void run_prepared(Builder& B, int batch, cudaStream_t stream) {
   const int tile = prep_row_align();
-  // Group the prepared operands that are sums of the same few blocks, so a
-  // source block is read once per tile for all of them.
-  struct HostGroup {
-    int rows, cols;
-    bool transpose;
-    std::vector<View> in;
-    std::vector<int> ops;   // indices into B.prep
-  };
-  std::vector<HostGroup> groups;
-  for (size_t j = 0; j < B.prep.size(); ++j) {
-    const Builder::PrepOp& o = B.prep[j];
-    if (o.terms.empty() || o.terms.size() > size_t(kMaxOperandTerms))
-      fail(BAG_ERR_INTERNAL, "prepared operand has an unsupported term count");
-    HostGroup* home = nullptr;
-    for (HostGroup& g : groups) {
-      if (g.rows != o.rows || g.cols != o.cols || g.transpose != o.transpose ||
-          g.ops.size() >= size_t(kMaxPrepGroupOut))
-        continue;
-      size_t fresh = 0;
-      for (const STerm& t : o.terms)
-        if (std::find(g.in.begin(), g.in.end(), t.v) == g.in.end()) ++fresh;
-      if (g.in.size() + fresh <= size_t(kMaxPrepGroupIn)) {
-        home = &g;
-        break;
-      }
-    }
-    if (!home) {
-      groups.push_back({o.rows, o.cols, o.transpose, {}, {}});
-      home = &groups.back();
-    }
-    for (const STerm& t : o.terms)
-      if (std::find(home->in.begin(), home->in.end(), t.v) == home->in.end()) home->in.push_back(t.v);
-    home->ops.push_back(int(j));
-  }
+  const std::vector<Builder::PrepGroupHost>& groups = B.prep_groups;
   for (size_t g0 = 0; g0 < groups.size(); g0 += kMaxPrepGroups) {
     PrepGroupPlan pp;
     std::memset(&pp, 0, sizeof(pp));
@@ -641,7 +659,7 @@ void run_prepared(Builder& B, int batch, cudaStream_t stream) {
     pp.region_bstride = B.ws_bstride;
     long long tiles = 0;
     for (size_t gi = g0; gi < std::min(groups.size(), g0 + kMaxPrepGroups); ++gi) {
-      const HostGroup& hg = groups[gi];
+      const Builder::PrepGroupHost& hg = groups[gi];
       PrepGroup& G = pp.group[pp.ngroups++];
       G.rows = hg.rows;
       G.cols = hg.cols;
@@ -650,14 +668,9 @@ void run_prepared(Builder& B, int batch, cudaStream_t stream) {
       for (int u = 0; u < G.nin; ++u) G.in[u] = make_term(hg.in[u], 1.f, 0);
       G.nout = int(hg.ops.size());
       for (int q = 0; q < G.nout; ++q) {
-        const Builder::PrepOp& o = B.prep[hg.ops[q]];
-        G.out_hi[q] = o.hi_row;
-        for (size_t t = 0; t < o.terms.size(); ++t) {
-          const int u = int(std::find(hg.in.begin(), hg.in.end(), o.terms[t].v) - hg.in.begin());
-          if (o.terms[t].coef != 1.f && o.terms[t].coef != -1.f)
-            fail(BAG_ERR_INTERNAL, "prepared operand term coefficient is not +-1");
-          G.expr[q][t] = static_cast<signed char>(o.terms[t].coef > 0 ? u + 1 : -(u + 1));
-        }
+        G.out_hi[q] = B.prep[hg.ops[q]].hi_row;
+        for (size_t t = 0; t < hg.expr[q].size(); ++t)
+          G.expr[q][t] = static_cast<signed char>(hg.expr[q][t]);
       }
       G.tile_begin = tiles;
       tiles += (long long)((hg.rows + tile - 1) / tile) * (B.prep_row_len / tile);
@@ -1015,9 +1028,44 @@ std::string dump_plan(int m, int n, int k, long long lda, long long ldb, long lo
     s += "],\"prep_l\":" + std::to_string(l.prep_l) + ",\"prep_r\":" + std::to_string(l.prep_r) +
          "}";
   }
-  s += "],\"decode\":{\"deferred\":" + std::string(B.decode.on ? "true" : "false") +
-       ",\"products\":" + std::to_string(B.decode.buffers.size()) + ",\"targets\":" +
-       std::to_string(B.decode.targets.size()) + "}";
+  // Deferred decode: target t of C = its old value + sum over products p (in
+  // plan order) of coef * buffer p, where terms[p] lists (t, coef).
+  const Builder::Decode& d = B.decode;
+  s += "],\"decode\":{\"deferred\":" + std::string(d.on ? "true" : "false") +
+       ",\"products\":" + std::to_string(d.buffers.size()) + ",\"targets\":" +
+       std::to_string(d.targets.size()) + ",\"m\":" + std::to_string(d.m) +
+       ",\"n\":" + std::to_string(d.n) + ",\"target_refs\":[";
+  for (size_t t = 0; t < d.targets.size(); ++t) s += (t ? "," : "") + ref(d.targets[t]);
+  s += "],\"buffers\":[";
+  for (size_t p = 0; p < d.buffers.size(); ++p) s += (p ? "," : "") + ref(d.buffers[p]);
+  s += "],\"terms\":[";
+  for (size_t p = 0; p < d.terms.size(); ++p) {
+    s += p ? ",[" : "[";
+    for (size_t e = 0; e < d.terms[p].size(); ++e)
+      s += std::string(e ? "," : "") + "[" + std::to_string(d.terms[p][e].first) + "," +
+           std::to_string(int(d.terms[p][e].second)) + "]";
+    s += "]";
+  }
+  s += "]},\"prep_groups\":[";
+  for (size_t gi = 0; gi < B.prep_groups.size(); ++gi) {
+    const Builder::PrepGroupHost& g = B.prep_groups[gi];
+    s += gi ? "," : "";
+    s += "{\"rows\":" + std::to_string(g.rows) + ",\"cols\":" + std::to_string(g.cols) +
+         ",\"transpose\":" + std::string(g.transpose ? "true" : "false") + ",\"in\":[";
+    for (size_t u = 0; u < g.in.size(); ++u) s += (u ? "," : "") + ref(g.in[u]);
+    s += "],\"ops\":[";
+    for (size_t q = 0; q < g.ops.size(); ++q) s += (q ? "," : "") + std::to_string(g.ops[q]);
+    s += "],\"expr\":[";
+    for (size_t q = 0; q < g.expr.size(); ++q) {
+      s += q ? ",[" : "[";
+      for (size_t t = 0; t < g.expr[q].size(); ++t)
+        s += (t ? "," : "") + std::to_string(g.expr[q][t]);
+      s += "]";
+    }
+    s += "]}";
+  }
+  s += "]";
+  s += ",\"prepared_region\":" + (B.prep_region.p ? ref(B.prep_region) : std::string("null"));
   s += ",\"prepared_row_len\":" + std::to_string(B.prep_row_len) + ",\"prepared\":[";
   for (size_t i = 0; i < B.prep.size(); ++i) {
     const Builder::PrepOp& o = B.prep[i];

@@ -3,6 +3,10 @@
 This checks the C++ plan builder on CPU: every materialisation job and every
 leaf product of the plan is evaluated in FP32 with numpy, in plan order, on
 column-major buffers laid out exactly as the kernels would address them.
+Plans of the prepared (3xTF32) path also carry the prepare groups and, at
+depth >= 2, the deferred decode; both are executed as the kernels order them
+(prep_group_kernel: each output's terms in its own order, the first with its
+sign; decode_kernel: per target, old value plus the products in plan order).
 """
 
 from __future__ import annotations
@@ -10,6 +14,7 @@ from __future__ import annotations
 import numpy as np
 
 F32 = np.float32
+C_BUF, WS_BUF = 2, 3
 
 
 def _view(buf: np.ndarray, ref, rows: int, cols: int) -> np.ndarray:
@@ -20,6 +25,79 @@ def _view(buf: np.ndarray, ref, rows: int, cols: int) -> np.ndarray:
     assert span <= buf.size, f"plan reference {ref} {rows}x{cols} overruns a buffer of {buf.size}"
     return np.lib.stride_tricks.as_strided(buf[off:], shape=(rows, cols),
                                            strides=(buf.itemsize, buf.itemsize * ld))
+
+
+def _signed_sum(xs, signs):
+    acc = None
+    for x, s in zip(xs, signs):
+        x = (x.astype(F32) * F32(s)).astype(F32)
+        acc = x if acc is None else (acc + x).astype(F32)
+    return acc
+
+
+def check_prep_groups(plan: dict) -> None:
+    """Structural rules of the prepare groups: every prepared operand sits in
+    exactly one group of its own shape, a group has at most 4 source blocks
+    and 8 outputs, each output's codes name its terms in order, and the
+    operands' hi/lo row ranges of the prepared region do not overlap."""
+    prepared, groups = plan["prepared"], plan["prep_groups"]
+    seen = []
+    for g in groups:
+        assert 1 <= len(g["in"]) <= 4 and 1 <= len(g["ops"]) <= 8
+        assert len(g["expr"]) == len(g["ops"])
+        for j, codes in zip(g["ops"], g["expr"]):
+            op = prepared[j]
+            assert (op["rows"], op["cols"], op["transpose"]) == (g["rows"], g["cols"], g["transpose"])
+            assert len(codes) == len(op["terms"])
+            for code, (ref, coef) in zip(codes, op["terms"]):
+                assert g["in"][abs(code) - 1] == ref and (1 if code > 0 else -1) == coef
+            seen.append(j)
+    assert sorted(seen) == list(range(len(prepared)))
+    spans = sorted((op["hi_row"], op["hi_row"] + 2 * op["rows"]) for op in prepared)
+    for (_, end), (begin, _) in zip(spans, spans[1:]):
+        assert end <= begin, "prepared operands overlap in the prepared region"
+    for op in prepared:
+        assert op["cols"] <= plan["prepared_row_len"]
+
+
+def _write_prepared(plan: dict, bufs) -> None:
+    """Evaluate every prepare group and store its operands in the prepared
+    region of the workspace as the kernels lay it out: operand j occupies
+    region rows [hi_row, hi_row + 2 * rows) (hi rows, then lo rows) of
+    ``prepared_row_len`` k values each, zero past its k extent.  Here the hi
+    rows hold the FP32 value and the lo rows zero (the TF32 split itself is
+    the GPU tests' business).  All groups of a launch read their sources
+    before any output lands, so every group is evaluated first."""
+    values = {}
+    for g in plan["prep_groups"]:
+        # Natural (column-major) shape of the source blocks: a left operand
+        # (transposed into k-contiguous rows) is rows x cols, a right one cols x rows.
+        shape = (g["rows"], g["cols"]) if g["transpose"] else (g["cols"], g["rows"])
+        ins = [_view(bufs[r[0]], r, *shape).copy() for r in g["in"]]
+        for j, codes in zip(g["ops"], g["expr"]):
+            values[j] = _signed_sum([ins[abs(c) - 1] for c in codes],
+                                    [1 if c > 0 else -1 for c in codes])
+    region = _prepared_region(plan, bufs)
+    for j, op in enumerate(plan["prepared"]):
+        rows_k = values[j] if op["transpose"] else values[j].T   # rows x k
+        hi = op["hi_row"]
+        region[:, hi:hi + 2 * op["rows"]] = 0
+        region[:op["cols"], hi:hi + op["rows"]] = rows_k.T
+
+
+def _prepared_region(plan: dict, bufs) -> np.ndarray:
+    ref = plan["prepared_region"]
+    nrows = max(op["hi_row"] + 2 * op["rows"] for op in plan["prepared"])
+    assert ref[0] == WS_BUF and ref[2] == plan["prepared_row_len"]
+    return _view(bufs[WS_BUF], ref, plan["prepared_row_len"], nrows)
+
+
+def _read_prepared(plan: dict, bufs, j: int) -> np.ndarray:
+    """Operand j back from the region (hi + lo), rows x k."""
+    op, region = plan["prepared"][j], _prepared_region(plan, bufs)
+    hi, rows = op["hi_row"], op["rows"]
+    assert not np.any(region[op["cols"]:, hi:hi + 2 * rows]), "prepared padding is not zero"
+    return (region[:op["cols"], hi:hi + rows] + region[:op["cols"], hi + rows:hi + 2 * rows]).T
 
 
 def run_plan(plan: dict, a: np.ndarray, b: np.ndarray, c: np.ndarray,
@@ -46,22 +124,47 @@ def run_plan(plan: dict, a: np.ndarray, b: np.ndarray, c: np.ndarray,
                     x = ins[abs(code) - 1] * F32(1 if code > 0 else -1)
                     acc = x.astype(F32) if acc is None else (acc + x).astype(F32)
                 _view(bufs[out_ref[0]], out_ref, rows, cols)[...] = acc
+    prepared = bool(plan.get("prepared"))
+    if prepared:
+        check_prep_groups(plan)
+        _write_prepared(plan, bufs)
+    decode = plan.get("decode", {})
+    deferred = bool(decode.get("deferred"))
     for leaf in plan["leaves"]:
         lm, ln, lk = leaf["m"], leaf["n"], leaf["k"]
 
         def operand(terms, rows, cols):
-            acc = None
-            for ref, coef in terms:
-                x = _view(bufs[ref[0]], ref, rows, cols).astype(F32) * F32(coef)
-                acc = x if acc is None else (acc + x).astype(F32)
-            return acc
+            return _signed_sum([_view(bufs[ref[0]], ref, rows, cols) for ref, _ in terms],
+                               [coef for _, coef in terms])
 
         left = operand(leaf["left"], lm, lk)
         right = operand(leaf["right"], lk, ln)
         assert np.all(np.isfinite(left)) and np.all(np.isfinite(right)), "read of unwritten workspace"
+        if prepared:
+            # The leaf multiplies its prepared operands, read back from the
+            # region after every earlier leaf's stores: they must equal the
+            # operand sums bit for bit.
+            assert np.array_equal(_read_prepared(plan, bufs, leaf["prep_l"]), left)
+            assert np.array_equal(_read_prepared(plan, bufs, leaf["prep_r"]).T, right)
         prod = (left.astype(F32) @ right.astype(F32)).astype(F32)
         for ref, coef in leaf["out"]:
-            assert ref[0] == 2, "outputs must target C"
-            v = _view(bufs[2], ref, lm, ln)
-            v[...] = (v + F32(coef) * prod).astype(F32)
-    return _view(bufs[2], (2, 0, ldc), m, n).copy()
+            v = _view(bufs[ref[0]], ref, lm, ln)
+            if ref[0] == WS_BUF:
+                assert deferred and ref in decode["buffers"], "workspace output without a decode"
+                v[...] = (F32(coef) * prod).astype(F32)
+            else:
+                assert ref[0] == C_BUF, "outputs must target C or a decode buffer"
+                v[...] = (v + F32(coef) * prod).astype(F32)
+    if deferred:
+        dm, dn = decode["m"], decode["n"]
+        prods = [_view(bufs[WS_BUF], r, dm, dn).copy() for r in decode["buffers"]]
+        for t, tref in enumerate(decode["target_refs"]):
+            assert tref[0] == C_BUF
+            v = _view(bufs[C_BUF], tref, dm, dn)
+            acc = v.copy()
+            for p, terms in enumerate(decode["terms"]):
+                for tt, coef in terms:
+                    if tt == t:
+                        acc = (acc + F32(coef) * prods[p]).astype(F32)
+            v[...] = acc
+    return _view(bufs[C_BUF], (C_BUF, 0, ldc), m, n).copy()

@@ -120,3 +120,103 @@ def test_winograd_plan_has_the_15_addition_structure(built_lib):
     assert [(len(l["left"]), len(l["right"]), len(l["out"])) for l in leaves] == [
         (1, 1, 4), (1, 1, 1), (4, 1, 1), (1, 4, 1), (2, 2, 2), (3, 3, 3), (2, 2, 2)]
     assert len(bag.plan_dump(64, 64, 64, 64, 64, 64, 2, "winograd")["leaves"]) == 49
+
+
+# Prepared (3xTF32) plans: leaves need K >= 1024, so these keep M and N small
+# and K long.  (m, k, n, depth, basis, deferred decode expected)
+PREPARED = [
+    (64, 2048, 64, 1, "minimal", False),    # depth 1: products update C directly
+    (64, 4096, 64, 2, "minimal", True),     # 49 products, 16 targets: deferred decode
+    (64, 4096, 48, 2, "full", True),
+    (64, 4096, 64, 2, "winograd", True),
+    (64, 4096, 64, 2, "classic", False),    # 144 updates / 49 products < 3: direct
+    (77, 4096, 61, 2, "minimal", False),    # peeled M/N strips: leaf shapes differ
+    (32, 8192, 32, 3, "minimal", False),    # 343 products: above the decode's 64
+]
+
+
+@pytest.mark.parametrize("m,k,n,depth,basis,deferred", PREPARED)
+def test_prepared_plan_computes_gemm(built_lib, m, k, n, depth, basis, deferred):
+    """The prepared path's plan -- stages, prepare groups, leaf products on
+    the prepared region and the deferred decode -- executed in numpy."""
+    import bag_b200 as bag
+    rng = np.random.default_rng(m + k + n + depth)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    c = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+    bag.set_math_mode("3xtf32")
+    try:
+        plan = bag.plan_dump(m, n, k, m, k, m, depth, basis)
+    finally:
+        bag.set_math_mode("ffma")
+    assert plan["prepared"] and plan["prep_groups"]
+    assert plan["decode"]["deferred"] is deferred
+    if deferred:
+        assert all(r[0] == 3 and len(l["out"]) == 1 for l in plan["leaves"] for r, _ in l["out"])
+        assert len(plan["decode"]["buffers"]) == len(plan["leaves"])
+        assert len(plan["decode"]["target_refs"]) == 4 ** depth
+    got = run_plan(plan, a, b, c, m, k, m)
+    assert O.rel_frobenius(got, O.fp64_matmul(a, b, c)) < 5e-6 * depth
+
+
+def test_prepare_groups_share_source_blocks(built_lib):
+    """At depth 2 the 98 prepared operands (49 left, 49 right) fold into 14
+    groups: the seven inner-level operands of one outer operand are sums of
+    its four quadrants, so each group reads 4 source blocks once -- 56 block
+    reads instead of the operands' 196 term reads."""
+    import bag_b200 as bag
+    bag.set_math_mode("3xtf32")
+    try:
+        plan = bag.plan_dump(64, 64, 4096, 64, 4096, 64, 2, "minimal")
+    finally:
+        bag.set_math_mode("ffma")
+    ops, groups = plan["prepared"], plan["prep_groups"]
+    assert len(ops) == 98
+    assert sum(len(op["terms"]) for op in ops) == 196
+    assert len(groups) == 14 and all(len(g["ops"]) == 7 for g in groups)
+    assert sum(len(g["in"]) for g in groups) == 56
+
+
+def test_ffma_plans_carry_no_prepared_operands(bag):
+    plan = bag.plan_dump(64, 64, 4096, 64, 4096, 64, 2, "minimal")
+    assert plan["prepared"] == [] and plan["prep_groups"] == []
+    assert plan["prepared_region"] is None and not plan["decode"]["deferred"]
+
+
+def test_plan_sim_catches_a_corrupted_prepared_plan(built_lib):
+    """The checks above have teeth: a flipped sign in one prepare group, a
+    misrouted decode term, or a group output aimed at the wrong operand is
+    caught."""
+    import copy
+
+    import bag_b200 as bag
+    m = n = 64
+    k = 4096
+    rng = np.random.default_rng(5)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    c = np.zeros((m, n), np.float32)
+    bag.set_math_mode("3xtf32")
+    try:
+        plan = bag.plan_dump(m, n, k, m, k, m, 2, "minimal")
+    finally:
+        bag.set_math_mode("ffma")
+    ref = O.fp64_matmul(a, b, c)
+    assert O.rel_frobenius(run_plan(plan, a, b, c, m, k, m), ref) < 1e-5
+
+    bad = copy.deepcopy(plan)
+    code = bad["prep_groups"][3]["expr"][2]
+    code[-1] = -code[-1]
+    with pytest.raises(AssertionError):
+        run_plan(bad, a, b, c, m, k, m)
+
+    bad = copy.deepcopy(plan)
+    g = bad["prep_groups"][0]
+    g["ops"][0], g["ops"][1] = g["ops"][1], g["ops"][0]
+    with pytest.raises(AssertionError):
+        run_plan(bad, a, b, c, m, k, m)
+
+    bad = copy.deepcopy(plan)
+    term = bad["decode"]["terms"][10][0]
+    term[0] = (term[0] + 1) % len(bad["decode"]["target_refs"])
+    assert O.rel_frobenius(run_plan(bad, a, b, c, m, k, m), ref) > 1e-2
