@@ -78,6 +78,7 @@ SIGNATURES = {
     "bag_plan_dump": (_I, [_I, _I, _I, _LL, _LL, _LL, _I, _I, ctypes.c_char_p, _SZ,
                            ctypes.POINTER(_SZ)]),
     "bag_profile_set_events": (_I, [_VP, _VP]),
+    "bag_profile_set_phase_events": (_I, [_VP, _VP]),
     "bag_launch_count": (ctypes.c_ulonglong, []),
     "bag_ffma_probe": (_I, [_VP, _I, _VP, ctypes.POINTER(ctypes.c_double)]),
     "bag_device_error": (_I, [ctypes.POINTER(ctypes.c_uint)]),
@@ -173,6 +174,13 @@ def profile_events(start=None, end=None) -> None:
     """Bracket later leaf launches of this thread with two ``torch.cuda.Event``s."""
     handle = lambda ev: None if ev is None else ev.cuda_event  # noqa: E731
     _check(lib().bag_profile_set_events(handle(start), handle(end)))
+
+
+def profile_phase_events(after_stages=None, after_last=None) -> None:
+    """Record ``after_stages`` once later calls' materialisation launches are
+    queued and ``after_last`` after their last launch (``torch.cuda.Event``s)."""
+    handle = lambda ev: None if ev is None else ev.cuda_event  # noqa: E731
+    _check(lib().bag_profile_set_phase_events(handle(after_stages), handle(after_last)))
 
 
 def set_math_mode(mode: str) -> None:

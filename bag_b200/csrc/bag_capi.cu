@@ -67,6 +67,12 @@ int resolve_depth(int depth, int m, int n, int k) {
 }
 thread_local cudaEvent_t g_prof_start = nullptr;
 thread_local cudaEvent_t g_prof_end = nullptr;
+// Phase events: after the materialisation stages, and after the call's last
+// launch (the decode pass where there is one).
+thread_local cudaEvent_t g_phase_stages = nullptr;
+thread_local cudaEvent_t g_phase_done = nullptr;
+
+void record_phase(cudaEvent_t ev, cudaStream_t stream);
 std::atomic<unsigned long long> g_launches{0};
 
 struct Error : std::runtime_error {
@@ -780,6 +786,7 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream,
       ++g_launches;
     }
   }
+  record_phase(g_phase_stages, stream);
   // Leaf products, grouped into as few launches as the parameter block allows.
   bool vec = true;
   for (const HostLeaf& l : B.leaves) {
@@ -798,6 +805,7 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream,
   g_last_prep_kind = -1;
   if (tensor && !B.prep.empty() && prep_supported()) {
     run_prepared(B, batch, stream);
+    record_phase(g_phase_done, stream);
     return;
   }
   if (g_prof_start) cuda_check(cudaEventRecord(g_prof_start, stream), "cudaEventRecord");
@@ -847,6 +855,11 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream,
     if (lp.nprod) ++g_launches;
   }
   if (g_prof_end) cuda_check(cudaEventRecord(g_prof_end, stream), "cudaEventRecord");
+  record_phase(g_phase_done, stream);
+}
+
+void record_phase(cudaEvent_t ev, cudaStream_t stream) {
+  if (ev) cuda_check(cudaEventRecord(ev, stream), "cudaEventRecord");
 }
 
 void check_device_workspace(const bag_workspace* ws) {
@@ -1354,6 +1367,15 @@ bag_status bag_profile_set_events(void* start_event, void* end_event) {
       fail(BAG_ERR_INVALID, "set both profiling events or neither");
     g_prof_start = static_cast<cudaEvent_t>(start_event);
     g_prof_end = static_cast<cudaEvent_t>(end_event);
+  });
+}
+
+bag_status bag_profile_set_phase_events(void* after_stages, void* after_last) {
+  return guarded([&] {
+    if ((after_stages == nullptr) != (after_last == nullptr))
+      fail(BAG_ERR_INVALID, "set both phase events or neither");
+    g_phase_stages = static_cast<cudaEvent_t>(after_stages);
+    g_phase_done = static_cast<cudaEvent_t>(after_last);
   });
 }
 

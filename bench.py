@@ -385,9 +385,13 @@ def run_bag(args) -> None:
     # Leaf-kernel events, created up front (torch creates events lazily).
     pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
              for _ in range(args.steps)]
-    for s, e in pairs:
-        s.record()
-        e.record()
+    # Phase events per step: before the call, after its materialisation
+    # launches, after its last launch (with the leaf pair: stages | prepare |
+    # leaves | decode).
+    phases = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
+              for _ in range(args.steps)]
+    for ev in [e for p in pairs for e in p] + [e for p in phases for e in p]:
+        ev.record()
     torch.cuda.synchronize()
 
     for _ in range(args.warmup):
@@ -414,10 +418,13 @@ def run_bag(args) -> None:
                 flush.fill_(float(i))
                 step_events[i][0].record()
             bag.profile_events(*pairs[i])
+            bag.profile_phase_events(phases[i][1], phases[i][2])
+            phases[i][0].record()
             step()
             if flush is not None:
                 step_events[i][1].record()
         bag.profile_events(None, None)
+        bag.profile_phase_events(None, None)
         t_end.record()
         torch.cuda.synchronize()
         clocks.window = (host0, time.time())
@@ -434,6 +441,18 @@ def run_bag(args) -> None:
         l2_note = f"inputs larger than L2 ({input_bytes / 2**30:.2f} GiB per GPU); no flush"
     del flush
     leaf_ms = reduce_max(sum(s.elapsed_time(e) for s, e in pairs) / args.steps)
+
+    def phase_mean(f):
+        return reduce_max(sum(f(i) for i in range(args.steps)) / args.steps)
+
+    # Each phase includes the launch gap in front of it.
+    phases_ms = {
+        "stages": phase_mean(lambda i: phases[i][0].elapsed_time(phases[i][1])),
+        "prepare": phase_mean(lambda i: phases[i][1].elapsed_time(pairs[i][0])),
+        "leaves": leaf_ms,
+        "decode": phase_mean(lambda i: pairs[i][1].elapsed_time(phases[i][2])),
+        "call": phase_mean(lambda i: phases[i][0].elapsed_time(phases[i][2])),
+    }
     flops_total = 2.0 * M * N * K * batch
     value = flops_total / (ms * 1e-3) / 1e12
     # Executed leaf FLOPs of this rank's launch: nb x 7^depth products of
@@ -672,6 +691,7 @@ def run_bag(args) -> None:
             "clocks": {k: csum[k] for k in ("sm_mhz", "sm_max_mhz", "reasons",
                                             "samples_in_timed_region")},
             "gpu_launches": int(launches),
+            "phases_ms": phases_ms,
             "executed_tflops": f_exec * world / (ms * 1e-3) / 1e12,
         }
         if cpu is not None:

@@ -155,6 +155,13 @@ bag_status bag_valid_shape(int backend, int s, int* valid);
  * caller can time the product kernel alone; NULL, NULL turns it off.
  * bag_launch_count returns how many kernels this process has launched. */
 bag_status bag_profile_set_events(void* start_event, void* end_event);
+/* Phase events (new): later calls of this host thread also record
+ * `after_stages` once the operand materialisation launches are queued
+ * (before any prepare or leaf launch) and `after_last` after the call's last
+ * launch (the decode pass where there is one).  With the leaf events above
+ * and an event the caller records before the call, a call splits into
+ * stages | prepare | leaves | decode.  NULL, NULL turns it off. */
+bag_status bag_profile_set_phase_events(void* after_stages, void* after_last);
 unsigned long long bag_launch_count(void);
 /* Math mode of later calls on this host thread (like cublasSetMathMode);
  * new, no reference counterpart. */

@@ -287,3 +287,33 @@ def test_prepared_depth3(tensor_mode):
     bag.set_math_mode("3xtf32")
     ffma = float((c_f.double() - exact).norm() / exact.norm())
     assert err <= min(1.25 * ffma, 1e-4), (err, ffma)
+
+
+# Phase events: a prepared depth-2 call splits into stages | prepare | leaves |
+# decode, each bracketed on the call's stream in that order.
+def test_phase_events_split_a_prepared_call(tensor_mode):
+    import torch
+    bag = tensor_mode
+    m = n = 2048
+    k = 4096
+    a, b = _operands(torch, m, k, n, seed=41)
+    c = torch.zeros(m, n, device="cuda")
+    ws = bag.Workspace.for_problem(n, m, k, 2)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    for e in ev:
+        e.record()
+    torch.cuda.synchronize()
+    bag.profile_events(ev[2], ev[3])
+    bag.profile_phase_events(ev[1], ev[4])
+    try:
+        ev[0].record()
+        bag.sgemm(a, b, c, beta=0.0, depth=2, workspace=ws)
+    finally:
+        bag.profile_events(None, None)
+        bag.profile_phase_events(None, None)
+    torch.cuda.synchronize()
+    spans = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
+    assert all(t >= 0 for t in spans), spans
+    assert spans[2] > 0 and spans[3] > 0     # leaves, then the deferred decode
+    with pytest.raises((ValueError, bag.BagError)):
+        bag.profile_phase_events(ev[1], None)
