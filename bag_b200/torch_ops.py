@@ -13,8 +13,12 @@ Importing this module registers
 ``math`` selects the leaf arithmetic for the call ("ffma": the reference's
 sequential-fmaf numerics; "3xtf32": tcgen05 tensor cores on TF32 hi/lo
 splits, used where every leaf has K >= 1024).  Workspaces are created on
-first use for each (device, shape, depth, basis, math) and kept; they are
-never allocated inside a timed call after that.  This is the counterpart of
+first use for each (device, stream, shape, depth, basis, math) and kept, so
+they are never allocated inside a timed call after that; one per stream,
+because a workspace is scratch for one call at a time.  At most
+``workspace_cache_limit()`` of them are kept (4 by default): the least
+recently used is freed first (``cudaFree`` waits for the work still using
+it).  This is the counterpart of
 the reference's Triton entry (``src/bag_triton/bag.py:955``) in PyTorch's
 operator registry; ``bag_b200.bag_matmul`` keeps the reference's own
 signature and errors.
@@ -23,32 +27,59 @@ signature and errors.
 from __future__ import annotations
 
 import threading
+from collections import OrderedDict
 
 import torch
 
 import bag_b200 as _bag
 
-_lock = threading.Lock()
-_workspaces: dict[tuple, "_bag.Workspace"] = {}
+# Guards the cache and spans lookup + launch, so a workspace is never freed
+# while a thread is launching into it.
+_lock = threading.RLock()
+_workspaces: "OrderedDict[tuple, _bag.Workspace]" = OrderedDict()
+_limit = 4
 _MATH = ("ffma", "3xtf32")
 
 
-def _workspace(device: torch.device, m: int, n: int, k: int, depth: int, basis: str,
-               math: str):
-    key = (device.index, m, n, k, depth, basis, math)
-    with _lock:
-        ws = _workspaces.get(key)
-        if ws is None:
-            previous = _bag.get_math_mode()
-            _bag.set_math_mode(math)
-            try:
-                with torch.cuda.device(device):
-                    # Column-major view of the row-major call: C^T (n x m) = B^T A^T.
-                    ws = _bag.Workspace.for_problem(n, m, k, depth, basis)
-            finally:
-                _bag.set_math_mode(previous)
-            _workspaces[key] = ws
+def _create(device: torch.device, m: int, n: int, k: int, depth: int, basis: str, math: str):
+    previous = _bag.get_math_mode()
+    _bag.set_math_mode(math)
+    try:
+        with torch.cuda.device(device):
+            # Column-major view of the row-major call: C^T (n x m) = B^T A^T.
+            return _bag.Workspace.for_problem(n, m, k, depth, basis)
+    finally:
+        _bag.set_math_mode(previous)
+
+
+def _workspace(device: torch.device, stream: int, m: int, n: int, k: int, depth: int,
+               basis: str, math: str):
+    """The cached workspace for this call (caller holds ``_lock``)."""
+    key = (device.index, stream, m, n, k, depth, basis, math)
+    ws = _workspaces.get(key)
+    if ws is not None:
+        _workspaces.move_to_end(key)
+        return ws
+    ws = _create(device, m, n, k, depth, basis, math)
+    _workspaces[key] = ws
+    while len(_workspaces) > _limit:
+        _workspaces.popitem(last=False)[1].close()
     return ws
+
+
+def set_workspace_cache_limit(limit: int) -> None:
+    """Keep at most ``limit`` (>= 1) workspaces; frees the oldest beyond it."""
+    global _limit
+    if int(limit) < 1:
+        raise ValueError("the workspace cache keeps at least one workspace")
+    with _lock:
+        _limit = int(limit)
+        while len(_workspaces) > _limit:
+            _workspaces.popitem(last=False)[1].close()
+
+
+def workspace_cache_limit() -> int:
+    return _limit
 
 
 def clear_workspaces() -> None:
@@ -74,15 +105,17 @@ def _run(c: torch.Tensor, a: torch.Tensor, b: torch.Tensor, beta: float, depth: 
          math: str) -> None:
     m, k = a.shape
     n = b.shape[1]
-    ws = _workspace(a.device, m, n, k, depth, basis, math)
-    previous = _bag.get_math_mode()
-    _bag.set_math_mode(math)
-    try:
-        with torch.cuda.device(a.device):
-            _bag.sgemm(a, b, c, beta=beta, depth=depth, basis=basis, workspace=ws,
-                       stream=torch.cuda.current_stream(a.device))
-    finally:
-        _bag.set_math_mode(previous)
+    stream = torch.cuda.current_stream(a.device)
+    with _lock:
+        ws = _workspace(a.device, stream.cuda_stream, m, n, k, depth, basis, math)
+        previous = _bag.get_math_mode()
+        _bag.set_math_mode(math)
+        try:
+            with torch.cuda.device(a.device):
+                _bag.sgemm(a, b, c, beta=beta, depth=depth, basis=basis, workspace=ws,
+                           stream=stream)
+        finally:
+            _bag.set_math_mode(previous)
 
 
 @torch.library.custom_op("bag_b200::matmul", mutates_args=())

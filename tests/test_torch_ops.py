@@ -66,3 +66,45 @@ def test_traced_by_torch_compile(cuda):
     x = torch.randn(512, 256, device="cuda", generator=g)
     y = torch.randn(256, 384, device="cuda", generator=g)
     assert _rel(compiled(x, y), x.double() @ y.double() + 1.0) <= 1e-5
+
+
+class _FakeWorkspace:
+    def __init__(self, key):
+        self.key, self.closed = key, False
+
+    def close(self):
+        self.closed = True
+
+
+def test_workspace_cache_is_bounded_and_per_stream(monkeypatch):
+    """Least recently used workspaces are freed beyond the limit, and two
+    streams never share one (a workspace is scratch for one call at a time)."""
+    from bag_b200 import torch_ops as T
+    made = []
+
+    def fake_create(device, m, n, k, depth, basis, math):
+        made.append(_FakeWorkspace((device.index, m, n, k)))
+        return made[-1]
+
+    monkeypatch.setattr(T, "_create", fake_create)
+    T.clear_workspaces()
+    old = T.workspace_cache_limit()
+    dev = torch.device("cuda", 0)
+    try:
+        T.set_workspace_cache_limit(2)
+        with T._lock:
+            w1 = T._workspace(dev, 11, 64, 64, 64, 1, "minimal", "ffma")
+            assert T._workspace(dev, 11, 64, 64, 64, 1, "minimal", "ffma") is w1
+            w2 = T._workspace(dev, 22, 64, 64, 64, 1, "minimal", "ffma")   # another stream
+            assert w2 is not w1
+            T._workspace(dev, 11, 64, 64, 64, 1, "minimal", "ffma")        # w1 most recent
+            w3 = T._workspace(dev, 11, 128, 64, 64, 1, "minimal", "ffma")
+        assert w2.closed and not w1.closed and not w3.closed
+        T.set_workspace_cache_limit(1)
+        assert w1.closed and not w3.closed
+        with pytest.raises(ValueError):
+            T.set_workspace_cache_limit(0)
+    finally:
+        T.clear_workspaces()
+        T.set_workspace_cache_limit(old)
+    assert all(w.closed for w in made)
