@@ -34,6 +34,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 
@@ -927,13 +928,14 @@ cudaError_t launch_bn(const PrepLeafPlan& plan, const PrepMaps& maps, int batch,
 }
 
 // Clusters of two leaf_pair_kernel CTAs that fit on the device at once (0 if
-// none do); cached per device.
+// none do); cached per device (value + 1; 0 = not yet known), safe to query
+// from several host threads.
 int pair_clusters() {
-  static int cache[64];
-  static bool known[64];
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (known[dev]) return cache[dev];
+  const int known = cache[dev].load(std::memory_order_acquire);
+  if (known > 0) return known - 1;
   int n = 0;
   if (cudaFuncSetAttribute(leaf_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            pairk::kSmemBytes) == cudaSuccess) {
@@ -951,8 +953,7 @@ int pair_clusters() {
     if (cudaOccupancyMaxActiveClusters(&n, leaf_pair_kernel, &cfg) != cudaSuccess) n = 0;
   }
   cudaGetLastError();   // a refused query leaves no sticky error behind
-  cache[dev] = n;
-  known[dev] = true;
+  cache[dev].store(n + 1, std::memory_order_release);
   return n;
 }
 
