@@ -446,8 +446,17 @@ __global__ void __launch_bounds__(256) materialize_kernel(const __grid_constant_
     const MatJob& J = plan.job[j];
     const long long local = q - plan.chunk_begin[j];
     const int rows4 = (J.rows + 3) / 4;
-    const int c = (int)(local / rows4);
-    const int r = (int)(local % rows4) * 4;
+    // 32-bit division where the job's chunk index fits (a 64-bit divide per
+    // float4 made this pass instruction-bound).
+    int c, r;
+    if (local <= 0x7fffffffLL) {
+      const unsigned l32 = (unsigned)local, d = (unsigned)rows4;
+      c = (int)(l32 / d);
+      r = (int)(l32 - (unsigned)c * d) * 4;
+    } else {
+      c = (int)(local / rows4);
+      r = (int)(local % rows4) * 4;
+    }
     float4 in[kMaxJobInputs];
 #pragma unroll
     for (int t = 0; t < kMaxJobInputs; ++t) in[t] = make_float4(0.f, 0.f, 0.f, 0.f);
