@@ -3,6 +3,7 @@
     python -m bag_b200.profile_case --n 4096 --depth 1          # one small case for ncu
     python -m bag_b200.profile_case --sweep                      # time the current tile config
     python -m bag_b200.profile_case --math 3xtf32 ...            # tensor-core leaf variant
+    python -m bag_b200.profile_case --math 3xtf32 --fused ...    # ... without prepared operands
     python -m bag_b200.profile_case --devices 0,1 --n 16384 --depth 2 --math 3xtf32
                                                                  # time sgemm_multi
 
@@ -21,7 +22,7 @@ import json
 import os
 
 
-def _operands(n: int, depth: int, basis: str):
+def _operands(n: int, depth: int, basis: str, fused: bool = False):
     import torch
 
     import bag_b200 as bag
@@ -30,21 +31,32 @@ def _operands(n: int, depth: int, basis: str):
     b = torch.randn(n, n, device="cuda", generator=g)
     c = torch.zeros(n, n, device="cuda")
     # In 3xTF32 mode a workspace (created in that mode) also holds the prepared
-    # TF32 hi/lo leaf operands, so every depth gets one there.
-    need_ws = depth >= 2 or basis != "minimal" or bag.get_math_mode() == "3xtf32"
-    ws = bag.Workspace.for_problem(n, n, n, depth, basis) if need_ws else None
+    # TF32 hi/lo leaf operands, so every depth gets one there.  `fused` sizes
+    # the workspace as in FFMA mode instead (no prepared region): the
+    # 3xTF32 calls then run the fused-prologue tensor kernel.
+    mode = bag.get_math_mode()
+    need_ws = depth >= 2 or basis != "minimal" or (mode == "3xtf32" and not fused)
+    ws = None
+    if need_ws:
+        if fused:
+            bag.set_math_mode("ffma")
+        try:
+            ws = bag.Workspace.for_problem(n, n, n, depth, basis)
+        finally:
+            bag.set_math_mode(mode)
     return a, b, c, ws
 
 
-def run_case(n: int, depth: int, basis: str, calls: int) -> None:
+def run_case(n: int, depth: int, basis: str, calls: int, fused: bool = False) -> None:
     import torch
 
     import bag_b200 as bag
-    a, b, c, ws = _operands(n, depth, basis)
+    a, b, c, ws = _operands(n, depth, basis, fused)
     for _ in range(calls):
         bag.sgemm(a, b, c, depth=depth, basis=basis, workspace=ws)
     torch.cuda.synchronize()
-    print(f"ok n={n} depth={depth} basis={basis} calls={calls}")
+    print(f"ok n={n} depth={depth} basis={basis} calls={calls} "
+          f"leaf_kernel={bag.last_leaf_kernel()}")
 
 
 def run_sweep(reps: int = 3) -> dict:
@@ -126,6 +138,8 @@ def main() -> None:
     p.add_argument("--sweep", action="store_true")
     p.add_argument("--math", default="ffma", choices=("ffma", "3xtf32"))
     p.add_argument("--devices", default=None, help="comma-separated: time sgemm_multi over them")
+    p.add_argument("--fused", action="store_true",
+                   help="3xtf32 without the prepared region: the fused-prologue tensor kernel")
     args = p.parse_args()
     import bag_b200 as bag
     bag.set_math_mode(args.math)
@@ -135,7 +149,7 @@ def main() -> None:
     elif args.sweep:
         print(json.dumps(run_sweep()), flush=True)
     else:
-        run_case(args.n, args.depth, args.basis, args.calls)
+        run_case(args.n, args.depth, args.basis, args.calls, args.fused)
 
 
 if __name__ == "__main__":
