@@ -591,7 +591,8 @@ cudaError_t launch_leaf(const LeafPlan& plan, int config, bool vec, int batch, c
 // that slice of every product buffer -- and of every target when it
 // accumulates -- into shared memory with cp.async (about 65 KB in flight per
 // CTA, no registers held), then warp t adds its target's products in plan
-// order (lane l: rows 8l .. 8l+7) and writes the slice once.
+// order (lane l: rows 4l .. 4l+3 and 128+4l .. 128+4l+3, so each float4 read
+// of a warp is 512 contiguous bytes) and writes the slice once.
 constexpr int kDecodeRows = 256;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
@@ -621,15 +622,19 @@ __global__ void __launch_bounds__(kMaxDecodeTargets * 32) decode_kernel(
   __syncthreads();
   const int t = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (t >= plan.nt) return;
-  float acc[8];
-  const float* own = tile + (long long)(plan.np + t) * kDecodeRows + lane * 8;
+  constexpr int kHalf = kDecodeRows / 2;
+  float acc[8];   // rows lane*4 + i (i < 4) and kHalf + lane*4 + (i - 4)
+  const float* own = tile + (long long)(plan.np + t) * kDecodeRows + lane * 4;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = plan.accumulate ? own[i] : 0.f;
+  for (int i = 0; i < 4; ++i) {
+    acc[i] = plan.accumulate ? own[i] : 0.f;
+    acc[4 + i] = plan.accumulate ? own[kHalf + i] : 0.f;
+  }
   for (int e = 0; e < plan.count[t]; ++e) {
     const int code = plan.list[t][e];
-    const float* v = tile + (long long)((code > 0 ? code : -code) - 1) * kDecodeRows + lane * 8;
+    const float* v = tile + (long long)((code > 0 ? code : -code) - 1) * kDecodeRows + lane * 4;
     const float4 v0 = *reinterpret_cast<const float4*>(v);
-    const float4 v1 = *reinterpret_cast<const float4*>(v + 4);
+    const float4 v1 = *reinterpret_cast<const float4*>(v + kHalf);
     const float s = code > 0 ? 1.f : -1.f;
     acc[0] = fmaf(s, v0.x, acc[0]); acc[1] = fmaf(s, v0.y, acc[1]);
     acc[2] = fmaf(s, v0.z, acc[2]); acc[3] = fmaf(s, v0.w, acc[3]);
@@ -637,15 +642,19 @@ __global__ void __launch_bounds__(kMaxDecodeTargets * 32) decode_kernel(
     acc[6] = fmaf(s, v1.z, acc[6]); acc[7] = fmaf(s, v1.w, acc[7]);
   }
   const Term& T = plan.out[t];
-  const int r = r0 + lane * 8;
-  float* dst = const_cast<float*>(T.p) + batch * T.bstride + (long long)col * T.ld + r;
-  if (r + 7 < plan.m) {
-    *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
-  } else {
+  float* column = const_cast<float*>(T.p) + batch * T.bstride + (long long)col * T.ld;
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (r + i < plan.m) dst[i] = acc[i];
+  for (int h = 0; h < 2; ++h) {
+    const int r = r0 + h * kHalf + lane * 4;
+    float* dst = column + r;
+    const float* a = acc + 4 * h;
+    if (r + 3 < plan.m) {
+      *reinterpret_cast<float4*>(dst) = make_float4(a[0], a[1], a[2], a[3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (r + i < plan.m) dst[i] = a[i];
+    }
   }
 }
 
