@@ -46,7 +46,7 @@ namespace {
 
 constexpr size_t kNoAllocScratchFloats = size_t(4) << 20;   // 16 MiB per device
 
-__device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
 // Device address of the scratch array on the current device (looked up once
 // per device).  Returns nullptr and sets bag_last_error() on failure.
