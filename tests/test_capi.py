@@ -110,3 +110,20 @@ def test_workspace_sizes(bag):
     plan2 = bag.plan_dump(1024, 1024, 1024, 1024, 1024, 1024, 2, "minimal")
     assert plan1["workspace_elements"] == 0
     assert plan2["workspace_elements"] == 8 * 512 * 512
+
+
+def test_profiling_hooks_take_both_events_or_neither(bag):
+    """The measurement hooks store caller-owned events per host thread; a
+    half-set pair is refused (BAG_ERR_INVALID) and NULL, NULL turns a pair off.
+    Any non-null handle works as a token here: nothing is recorded without a
+    call on a GPU."""
+    lib = bag.lib()
+    token = ctypes.c_void_p(0x1000)
+    assert lib.bag_profile_set_events(token, None) == 1
+    assert b"both" in lib.bag_last_error()
+    assert lib.bag_profile_set_phase_events(None, token) == 1
+    assert b"both" in lib.bag_last_error()
+    assert lib.bag_profile_set_events(None, None) == 0
+    assert lib.bag_profile_set_phase_events(None, None) == 0
+    # Counting launches needs no device either.
+    assert lib.bag_launch_count() >= 0
