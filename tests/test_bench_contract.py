@@ -31,3 +31,36 @@ def test_missing_or_malformed_summary_reads_as_none(tmp_path, monkeypatch):
     (tmp_path / "profiles" / "bad.txt").write_text("traffic_bytes_per_full_launch: n/a\n")
     monkeypatch.setattr(bench, "ROOT", str(tmp_path))
     assert bench.read_traffic("bad.txt") is None
+
+
+def _sample(sm, power_cap=False, thermal=False):
+    state = lambda on: "Active" if on else "Not Active"  # noqa: E731
+    return (f"0, {sm}, 1965, 900.0, 0x0, {state(False)}, {state(thermal)}, "
+            f"{state(False)}, {state(power_cap)}")
+
+
+def test_clock_summary_keeps_the_timed_window():
+    """The bench line's clocks: median SM clock and the throttle reasons of the
+    samples inside the timed region only; outside samples are ignored."""
+    s = bench.ClockSampler(0)
+    s.lines = [(0.5, _sample(600, thermal=True)),          # before the region
+               (1.1, _sample(1950)), (1.2, _sample(1965, power_cap=True)),
+               (1.3, _sample(1900)),
+               (9.0, _sample(300, thermal=True))]          # after it
+    s.window = (1.0, 2.0)
+    out = s.summary()
+    assert out["sm_mhz"] == 1950 and out["sm_max_mhz"] == 1965
+    assert out["reasons"] == ["sw_power_cap"]
+    assert out["samples_in_timed_region"] == 3
+
+
+def test_clock_summary_short_region_uses_nearest_samples_and_skips_bad_lines():
+    s = bench.ClockSampler(0)
+    s.lines = [(1.0, "garbage"), (1.04, _sample(1800, thermal=True)),
+               (1.09, _sample(1900)), (5.0, _sample(100))]
+    s.window = (1.05, 1.06)            # shorter than the 50 ms sampling period
+    out = s.summary()
+    assert out["samples_in_timed_region"] == 0
+    assert out["sm_mhz"] == 1850 and "hw_thermal_slowdown" in out["reasons"]
+    empty = bench.ClockSampler(0)
+    assert empty.summary()["sm_mhz"] is None
