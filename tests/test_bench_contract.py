@@ -64,3 +64,32 @@ def test_clock_summary_short_region_uses_nearest_samples_and_skips_bad_lines():
     assert out["sm_mhz"] == 1850 and "hw_thermal_slowdown" in out["reasons"]
     empty = bench.ClockSampler(0)
     assert empty.summary()["sm_mhz"] is None
+
+
+def test_bench_configs_match_baseline():
+    """Each --config reproduces the shape, seed, distribution and recursion
+    depth that BASELINE.json states for it."""
+    import json
+    import re
+    with open(os.path.join(ROOT, "BASELINE.json")) as f:
+        text = json.load(f)["configs"]
+    C = bench.CONFIGS
+    expect = {   # config -> (index in BASELINE.json configs, M, N, K, batch, seed)
+        "cfg1": (0, 512, 512, 512, 1, 0), "cfg2": (1, 4096, 4096, 4096, 1, 1),
+        "cfg3": (2, 16384, 16384, 16384, 1, 2), "cfg4a": (3, 8192, 4096, 16384, 1, 3),
+        "cfg4b": (3, 10000, 10000, 10000, 1, 3), "cfg5": (4, 2048, 2048, 2048, 64, 4),
+    }
+    for name, (idx, m, n, k, batch, seed) in expect.items():
+        cfg, desc = C[name], text[idx]
+        assert (cfg["m"], cfg["n"], cfg["k"], cfg["batch"], cfg["seed"]) == (m, n, k, batch, seed)
+        assert re.search(rf"seed {seed}\b", desc), (name, desc)
+        for size in {m, n, k}:
+            assert str(size) in desc, (name, size)
+        uniform = "uniform" in desc
+        assert (cfg["dist"][0] == "uniform") == uniform
+        if uniform:
+            lo, hi = cfg["dist"][1:]
+            assert f"[{lo:g},{hi:g})" in desc.replace(".0", "").replace(" ", "")
+    assert "2 levels" in text[2] and C["cfg3"]["depth"] == 2
+    assert "2 recursion levels" in text[1] and C["cfg2"]["depth"] in (1, 2)
+    assert all(C[c]["depth"] == 1 for c in ("cfg1", "cfg4a", "cfg4b", "cfg5"))
