@@ -9,7 +9,14 @@ The reference rejects non-CUDA tensors (``bag.py:998-999``,
 ``torch.Tensor`` subclass whose ``is_cuda`` reports True; the reference files
 are not modified.
 
-Usage: python tests/golden/make_golden.py [--reference /path/to/bag]
+Usage: python tests/golden/make_golden.py --reference <bag checkout> [--only cfg1]
+(or set BAG_REFERENCE_ROOT instead of --reference).
+
+``cfg1_triton_bag_n512.npz`` is BASELINE config 1 on its exact inputs:
+A then B drawn U[-1,1) from ``numpy.random.default_rng(0)`` (``bench.make_inputs``),
+512 x 512 row-major, one BAG level, the reference's default schedule ("auto",
+grouped at this size); it stores the output and the first 64 draws of A and B,
+so a test can check that it regenerates the same inputs.
 
 This script needs the reference checkout and is run only where it exists;
 the fixtures it writes are what travels.
@@ -62,8 +69,13 @@ def _inputs(rng, shape, dist):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default=os.environ.get("BAG_REFERENCE_ROOT", "/root/reference"))
+    parser.add_argument("--reference", default=os.environ.get("BAG_REFERENCE_ROOT"),
+                        help="root of the reference checkout (default: $BAG_REFERENCE_ROOT)")
+    parser.add_argument("--only", choices=["cfg1"], default=None,
+                        help="write only this fixture (the others are left as they are)")
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("give the reference checkout with --reference or BAG_REFERENCE_ROOT")
     os.environ["TRITON_INTERPRET"] = "1"
     sys.path.insert(0, os.path.join(args.reference, "src"))
     import torch
@@ -90,7 +102,32 @@ def main() -> None:
             t = torch.from_numpy(np.asfortranarray(x))
         return tag(t)
 
-    manifest = []
+    # BASELINE config 1 on its exact inputs (bench.make_inputs).
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from bench import CONFIGS, make_inputs
+    a, b = make_inputs(dict(CONFIGS["cfg1"]))
+    ta, tb = to_dev(a, "row"), to_dev(b, "row")
+    out = to_dev(np.zeros(a.shape, np.float32), "row")
+    ws = workspace(ta, tb, out, grouped=True)   # schedule "auto" is grouped up to N=8192
+    t0 = time.time()
+    bag_triton.bag_matmul(ta, tb, out=out, workspace=ws)
+    dt = time.time() - t0
+    got = out.as_subclass(torch.Tensor).contiguous().numpy().copy()
+    np.savez_compressed(os.path.join(HERE, "cfg1_triton_bag_n512.npz"), out=got,
+                        a_head=a.ravel()[:64].copy(), b_head=b.ravel()[:64].copy(), n=512,
+                        layout="row", schedule="auto", seed=0, dist="uniform(-1,1)")
+    cfg1_line = (f"cfg1_triton_bag_n512: BASELINE cfg1 inputs (default_rng(0), U[-1,1), "
+                 f"A then B), n=512 layout=row schedule=auto (grouped) {dt:.2f}s")
+    print(cfg1_line, flush=True)
+    if args.only == "cfg1":
+        path = os.path.join(HERE, "MANIFEST.txt")
+        lines = [ln for ln in open(path).read().splitlines()
+                 if not ln.startswith("cfg1_triton_bag_n512:")]
+        with open(path, "w") as f:
+            f.write("\n".join(lines + [cfg1_line]) + "\n")
+        return
+
+    manifest = [cfg1_line]
     for name, n, layout, schedule, seed, dist in BAG_CASES:
         rng = np.random.default_rng(seed)
         a = _inputs(rng, (n, n), dist)

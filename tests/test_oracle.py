@@ -146,3 +146,19 @@ def test_winograd_oracle_is_a_matmul():
     exact = O.fp64_matmul(a, b)
     for depth in (1, 2, 3):
         assert O.rel_frobenius(O.winograd_product(a, b, depth), exact) < 1e-5
+
+
+def test_oracle_matches_reference_triton_on_cfg1():
+    """BASELINE cfg1 (512, U[-1,1) from default_rng(0), one level): the oracle on the
+    exact bench inputs against the reference's Triton bag_matmul on the same inputs."""
+    from bench import CONFIGS, make_inputs
+    a, b = make_inputs(dict(CONFIGS["cfg1"]))
+    z = np.load(os.path.join(GOLDEN, "cfg1_triton_bag_n512.npz"))
+    assert np.array_equal(z["a_head"], a.ravel()[:64])
+    assert np.array_equal(z["b_head"], b.ravel()[:64])
+    ref64 = O.fp64_matmul(a, b)
+    assert O.rel_frobenius(z["out"], ref64) <= 3e-4                # test_bag.py:60
+    for leaf in ("blas", "fmaf"):
+        mine = O.bag_product(a, b, 1, "minimal", leaf=leaf)
+        assert O.rel_frobenius(mine, z["out"]) <= 2e-6
+        assert O.rel_frobenius(mine, ref64) <= 3e-4
