@@ -62,6 +62,7 @@ SIGNATURES = {
     "bag_workspace_create": (_I, [_I, _I, _I, ctypes.POINTER(_VP)]),
     "bag_workspace_create_ex": (_I, [_I, _I, _I, _I, _I, _I, ctypes.POINTER(_VP)]),
     "bag_workspace_destroy": (_I, [_VP]),
+    "bag_workspace_bytes_for": (_I, [_I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_SZ)]),
     "bag_workspace_bytes": (_SZ, [_VP]),
     "bag_workspace_data": (_VP, [_VP]),
     "bag_matmul": (_I, [_VP, _VP, _VP, _I, _VP, _VP, _I, _I]),
@@ -80,6 +81,7 @@ SIGNATURES = {
     "bag_profile_set_events": (_I, [_VP, _VP]),
     "bag_profile_set_phase_events": (_I, [_VP, _VP]),
     "bag_launch_count": (ctypes.c_ulonglong, []),
+    "bag_device_allocations": (ctypes.c_ulonglong, []),
     "bag_ffma_probe": (_I, [_VP, _I, _VP, ctypes.POINTER(ctypes.c_double)]),
     "bag_device_error": (_I, [ctypes.POINTER(ctypes.c_uint)]),
     "bag_set_math_mode": (_I, [_I]),
@@ -168,6 +170,22 @@ def plan_dump(m: int, n: int, k: int, lda: int, ldb: int, ldc: int, depth: int,
 def launch_count() -> int:
     """Kernels this process has launched through the library."""
     return int(lib().bag_launch_count())
+
+
+def device_allocations() -> int:
+    """Device allocations (cudaMalloc calls) the library has made in this process."""
+    return int(lib().bag_device_allocations())
+
+
+def workspace_bytes_for(m: int, n: int, k: int, depth=1, basis="minimal", batch: int = 1,
+                        math: Optional[str] = None) -> int:
+    """Bytes a workspace for column-major ``C(m x n) += A(m x k) B(k x n)``
+    takes when created in math mode ``math`` (default: this thread's mode)."""
+    mode = MATH[get_math_mode() if math is None else math]
+    out = ctypes.c_size_t(0)
+    _check(lib().bag_workspace_bytes_for(mode, m, n, k, _depth(depth), _basis(basis), batch,
+                                         ctypes.byref(out)))
+    return out.value
 
 
 def profile_events(start=None, end=None) -> None:

@@ -25,6 +25,17 @@ outside the product, with the reference's limits (relative L2 <= 3e-5,
 max scaled error <= 1e-4; ``fp32_baseline.cu:121-192``).  Timing: CUDA events
 around back-to-back calls, repeats adapted to ``--target-ms``, cases in a
 shuffled order per round (``bag.cu:108-124``).
+
+``--profile-calls K`` (with ``--only`` naming one case) is the counterpart of
+the reference's ``benchmarks/cuda/strassen.cu:147-155``: after validation and
+five warm-up calls it runs K calls between ``cudaProfilerStart`` and
+``cudaProfilerStop`` and skips the timed rounds, so a profiler started with
+``--profile-from-start off`` (``ncu``) sees exactly those K calls::
+
+    ncu --profile-from-start off --clock-control none -k regex:leaf_pair -c 1 \
+        python -m bag_b200.benchmark --sizes 4096 --depths 2 --basis minimal \
+            --schedule batched --math 3xtf32 \
+            --only bag_column_minimal_d2_batched_3xtf32 --profile-calls 1
 """
 
 from __future__ import annotations
@@ -56,6 +67,8 @@ def parse(argv=None):
     p.add_argument("--output", default="results")
     p.add_argument("--validate-only", action="store_true")
     p.add_argument("--math", default="ffma", choices=["ffma", "3xtf32"])
+    p.add_argument("--profile-calls", type=int, default=0,
+                   help="run K calls of the --only case inside cudaProfilerStart/Stop, no rounds")
     o = p.parse_args(argv)
     for n in o.sizes:
         if n < 8 or n % 8:
@@ -63,8 +76,10 @@ def parse(argv=None):
     for d in o.depths:
         if d < 1 or d > 8:
             raise SystemExit("depth must be 1..8")
-    if o.rounds < 1 or o.target_ms <= 0 or o.samples < 16:
+    if o.rounds < 1 or o.target_ms <= 0 or o.samples < 16 or o.profile_calls < 0:
         raise SystemExit("invalid measurement options")
+    if o.profile_calls and not o.only:
+        raise SystemExit("profiling requires --only selecting one case")
     return o
 
 
@@ -141,6 +156,26 @@ def validate(torch, c, n: int, samples: int, repeats: int, seeds) -> dict:
             "max_scaled": max_scaled, "pass": ok}
 
 
+def cublas_version():
+    """cuBLAS version as major*10000 + minor*100 + patch (cublasGetProperty), or None."""
+    import ctypes
+    import glob
+    try:
+        import torch
+        root = os.path.dirname(os.path.dirname(torch.__file__))
+        cands = sorted(glob.glob(os.path.join(root, "nvidia", "cublas", "lib", "libcublas.so*")))
+        lib = ctypes.CDLL(cands[0] if cands else "libcublas.so")
+        parts = []
+        for prop in range(3):   # MAJOR_VERSION, MINOR_VERSION, PATCH_LEVEL
+            v = ctypes.c_int(0)
+            if lib.cublasGetProperty(prop, ctypes.byref(v)) != 0:
+                return None
+            parts.append(v.value)
+        return parts[0] * 10000 + parts[1] * 100 + parts[2]
+    except (OSError, AttributeError):
+        return None
+
+
 # ---------------------------------------------------------------------------
 # The run.
 # ---------------------------------------------------------------------------
@@ -167,7 +202,7 @@ def main(argv=None) -> int:
             "seed_offset": o.seed_offset, "rounds": o.rounds, "target_ms": o.target_ms,
             "samples": o.samples, "backend": o.backend, "basis": o.basis,
             "schedule": o.schedule, "cuda_runtime": torch.version.cuda,
-            "cublas_version": None, "sizes": o.sizes, "depths": o.depths,
+            "cublas_version": cublas_version(), "sizes": o.sizes, "depths": o.depths,
             "bag_math": o.math, "library": bag.lib().bag_version().decode()}
     with open(o.output + ".metadata.json", "w") as f:
         json.dump(meta, f)
@@ -215,8 +250,9 @@ def main(argv=None) -> int:
                     cases.append((name, (lambda w=ws, s=sched:
                                          bag.matmul(a, b, c, n, w, backend, s))))
         if o.only:
-            cases = [x for x in cases if x[0] in (o.only, "cublas_full")]
-        if len(cases) < 2:
+            keep_names = (o.only,) if o.profile_calls else (o.only, "cublas_full")
+            cases = [x for x in cases if x[0] in keep_names]
+        if len(cases) < (1 if o.profile_calls else 2):
             raise SystemExit("no legal BAG/Strassen case selected")
         for name, launch in cases:
             for repeats in (1, 3):
@@ -233,6 +269,19 @@ def main(argv=None) -> int:
                     failed = True
         print(f"N={n} FP64 {'FAIL' if failed else 'PASS'} cases={len(cases)}", flush=True)
         if failed or o.validate_only:
+            continue
+        if o.profile_calls:
+            name, launch = cases[0]
+            fill(torch, c, seeds[2])
+            for _ in range(5):
+                launch()
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStart()
+            for _ in range(o.profile_calls):
+                launch()
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStop()
+            print(f"PROFILE COMPLETE N={n} {name} calls={o.profile_calls}", flush=True)
             continue
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 

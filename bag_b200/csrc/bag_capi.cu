@@ -74,6 +74,14 @@ thread_local cudaEvent_t g_phase_done = nullptr;
 
 void record_phase(cudaEvent_t ev, cudaStream_t stream);
 std::atomic<unsigned long long> g_launches{0};
+// Device allocations this library has made (every cudaMalloc goes through
+// device_alloc).
+std::atomic<unsigned long long> g_device_allocs{0};
+
+cudaError_t device_alloc(void** p, size_t bytes) {
+  ++g_device_allocs;
+  return cudaMalloc(p, bytes);
+}
 
 struct Error : std::runtime_error {
   bag_status status;
@@ -567,10 +575,10 @@ size_t plan_workspace_elements(GemmDesc g, bool leaf_operands = false) {
   return B.ws_used;
 }
 
-// Whether this thread's math mode wants prepared leaf operands for `g`: the
-// 3xTF32 mode and every leaf long enough for the tensor path.
-bool leaf_materialisation_wanted(GemmDesc g) {
-  if (g_math_mode != BAG_MATH_3XTF32) return false;
+// Whether math mode `mode` wants prepared leaf operands for `g`: the 3xTF32
+// mode and every leaf long enough for the tensor path.
+bool leaf_materialisation_wanted(GemmDesc g, int mode) {
+  if (mode != BAG_MATH_3XTF32) return false;
   static float fake;
   Builder B;
   g.a = g.b = &fake;
@@ -582,21 +590,14 @@ bool leaf_materialisation_wanted(GemmDesc g) {
   return true;
 }
 
-// Tile configuration: the env var BAG_B200_TILE (a kTile* id) pins one for
-// tuning runs; otherwise the measured-fastest Tall tile, or small tiles when
-// the grid cannot fill the GPU.
+// Tile configuration: the warp-specialised kernel where every product has a
+// compiled signature and the grid fills the GPU, else the measured-fastest
+// Tall tile, or smaller tiles when the grid cannot fill the GPU.
 int signature(const HostLeaf& l, bool vec);
 
 int choose_tile(const std::vector<HostLeaf>& leaves, int sm_count, bool vec) {
-  static const int forced = [] {
-    const char* s = std::getenv("BAG_B200_TILE");
-    if (!s || !*s) return -1;
-    const int v = std::atoi(s);
-    return (v >= 0 && v < kTileCount) ? v : -1;
-  }();
   bool all_fast = vec;
   for (const HostLeaf& l : leaves) all_fast = all_fast && signature(l, vec) != kSigGeneric;
-  if (forced >= 0 && (forced != kTileWS || all_fast)) return forced;
   auto tiles_for = [&](int cfg) {
     const TileShape t = leaf_tile_shape(cfg);
     long long tiles = 0;
@@ -755,6 +756,49 @@ void run_prepared(Builder& B, int batch, cudaStream_t stream) {
   }
 }
 
+// FFMA leaves longer than kFfmaChainSplitK are split along K into chains of
+// at most kFfmaChainK that add into the same C blocks (atomically), so no
+// output is a sequential fmaf chain longer than 4096.  A chain's rounding
+// error grows with its length; the reference's own leaves at the benchmark's
+// square sizes are 2048-4096 long, and a rectangular problem with a long K
+// (e.g. 8192 x 16384 x 4096 at one level: K = 8192 per leaf), which the
+// reference can only run as square calls on sub-blocks (leaf K = 2048, the
+// partial results added into C), then gets that composition's error.  Only
+// leaves whose every output is atomic are split (plain-store and single-writer
+// outputs of bag_primitive keep one chain).
+constexpr int kFfmaChainSplitK = 4096;
+constexpr int kFfmaChainK = 2048;
+
+void split_long_chains(std::vector<HostLeaf>& leaves) {
+  std::vector<HostLeaf> out;
+  out.reserve(leaves.size());
+  for (HostLeaf& l : leaves) {
+    bool atomic = true;
+    for (const Target& t : l.out) atomic = atomic && t.mode == kOutAtomic;
+    if (l.k <= kFfmaChainSplitK || !atomic) {
+      out.push_back(std::move(l));
+      continue;
+    }
+    const int chunks = (l.k + kFfmaChainK - 1) / kFfmaChainK;
+    const int step = (l.k / chunks + 3) / 4 * 4;   // multiples of 4 keep 16-byte offsets
+    for (int k0 = 0; k0 < l.k; k0 += step) {
+      HostLeaf c;
+      c.m = l.m;
+      c.n = l.n;
+      c.k = std::min(step, l.k - k0);
+      c.out = l.out;
+      // Left operands are column-major m x k (column offset), right ones k x n
+      // (row offset).
+      for (const STerm& t : l.left)
+        c.left.push_back({{t.v.p + (long long)k0 * t.v.ld, t.v.ld, t.v.bstride}, t.coef});
+      for (const STerm& t : l.right)
+        c.right.push_back({{t.v.p + k0, t.v.ld, t.v.bstride}, t.coef});
+      out.push_back(std::move(c));
+    }
+  }
+  leaves.swap(out);
+}
+
 // `sources` lists the whole operand matrices (A, B) the tensor-core path may
 // address blocks of through one tensor map each; may be empty.
 void execute_plan(Builder& B, int batch, cudaStream_t stream,
@@ -794,13 +838,14 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream,
     for (const STerm& t : l.right) vec = vec && view_vec_ok(t.v);
     for (const Target& t : l.out) vec = vec && view_vec_ok(t.v);
   }
-  bool all_fast = vec;
-  for (const HostLeaf& l : B.leaves) all_fast = all_fast && signature(l, vec) != kSigGeneric;
   // The tensor path reads operands by TMA, so it needs aligned operands
   // (vec) but no common leading dimension among a product's terms.
   bool tensor = g_math_mode == BAG_MATH_3XTF32 && vec;
   for (const HostLeaf& l : B.leaves)
     tensor = tensor && l.k >= kTcMinK && tc_supported(int(l.left.size()), int(l.right.size()));
+  if (!tensor) split_long_chains(B.leaves);
+  bool all_fast = vec;
+  for (const HostLeaf& l : B.leaves) all_fast = all_fast && signature(l, vec) != kSigGeneric;
   g_last_leaf_path = tensor ? BAG_MATH_3XTF32 : BAG_MATH_FFMA;
   g_last_prep_kind = -1;
   if (tensor && !B.prep.empty() && prep_supported()) {
@@ -891,7 +936,7 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
   }
   // 3xTF32 mode prepares the leaf operands when the workspace was sized for
   // it (created in that mode); otherwise the prologue stays fused.
-  bool leaf_operands = leaf_materialisation_wanted(g);
+  bool leaf_operands = leaf_materialisation_wanted(g, g_math_mode);
   size_t need = plan_workspace_elements(g, leaf_operands);
   if (leaf_operands && (!ws || need * size_t(g.batch) > ws->elements)) {
     leaf_operands = false;
@@ -991,7 +1036,7 @@ std::string dump_plan(int m, int n, int k, long long lda, long long ldb, long lo
              reinterpret_cast<float*>(3 * unit), ldc, 0, 1, depth, basis};
   Builder B;
   // In 3xTF32 mode the plan also lists the prepared (TF32 hi/lo) operands.
-  build_plan(g, reinterpret_cast<float*>(4 * unit), 0, B, leaf_materialisation_wanted(g));
+  build_plan(g, reinterpret_cast<float*>(4 * unit), 0, B, leaf_materialisation_wanted(g, g_math_mode));
   auto ref = [&](const View& v) {
     const uintptr_t p = reinterpret_cast<uintptr_t>(v.p);
     const uintptr_t base = p / unit;
@@ -1127,16 +1172,37 @@ bag_status bag_workspace_create_ex(int m, int n, int k, int depth, int basis, in
                std::max(1, m), 0, std::max(batch, 1), depth, basis};
     // Sized for the calling thread's math mode (3xTF32 adds the prepared
     // leaf operands).
-    const size_t per = plan_workspace_elements(g, leaf_materialisation_wanted(g));
+    const size_t per = plan_workspace_elements(g, leaf_materialisation_wanted(g, g_math_mode));
     const size_t total = per * size_t(std::max(batch, 1));
     auto* ws = new bag_workspace{m, n, k, depth, basis, batch, 0, nullptr, total};
     cudaError_t e = cudaGetDevice(&ws->device);
-    if (e == cudaSuccess && total) e = cudaMalloc(&ws->data, total * sizeof(float));
+    if (e == cudaSuccess && total)
+      e = device_alloc(reinterpret_cast<void**>(&ws->data), total * sizeof(float));
     if (e != cudaSuccess) {
       delete ws;
       cuda_check(e, "workspace allocation");
     }
     *out = ws;
+  });
+}
+
+bag_status bag_workspace_bytes_for(int mode, int m, int n, int k, int depth, int basis, int batch,
+                                   size_t* bytes) {
+  return guarded([&] {
+    if (!bytes) fail(BAG_ERR_INVALID, "null output pointer");
+    *bytes = 0;
+    if (mode != BAG_MATH_FFMA && mode != BAG_MATH_3XTF32) fail(BAG_ERR_INVALID, "unknown math mode");
+    if (m < 0 || n < 0 || k < 0 || batch < 0) fail(BAG_ERR_SHAPE, "negative extent");
+    const int saved = g_math_mode;   // resolve_depth reads this thread's mode
+    g_math_mode = mode;
+    depth = resolve_depth(depth, m, n, k);
+    g_math_mode = saved;
+    if (depth < 0 || depth > 8) fail(BAG_ERR_INVALID, "depth must be 0..8 or BAG_DEPTH_AUTO");
+    if (!known_basis(basis)) fail(BAG_ERR_INVALID, "unknown basis");
+    GemmDesc g{m, n, k, nullptr, std::max(1, m), 0, nullptr, std::max(1, k), 0, nullptr,
+               std::max(1, m), 0, std::max(batch, 1), depth, basis};
+    *bytes = plan_workspace_elements(g, leaf_materialisation_wanted(g, mode)) *
+             size_t(std::max(batch, 1)) * sizeof(float);
   });
 }
 
@@ -1279,7 +1345,7 @@ bag_status sgemm_with_scratch(int layout, int m, int n, int k, const float* a, l
                "; use bag_sgemm_ex with a workspace from bag_workspace_create_ex");
     int dev = 0;
     cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
-    bag_workspace ws{g.m, g.n, g.k, depth, basis, 1, dev, scratch, scratch_elements};
+    bag_workspace ws{g.m, g.n, g.k, g.depth, g.basis, 1, dev, scratch, scratch_elements};
     run_gemm(g, beta, stream, &ws);
   });
 }
@@ -1381,6 +1447,8 @@ bag_status bag_profile_set_phase_events(void* after_stages, void* after_last) {
 
 unsigned long long bag_launch_count(void) { return g_launches.load(); }
 
+unsigned long long bag_device_allocations(void) { return g_device_allocs.load(); }
+
 bag_status bag_set_math_mode(int mode) {
   return guarded([&] {
     if (mode != BAG_MATH_FFMA && mode != BAG_MATH_3XTF32) fail(BAG_ERR_INVALID, "unknown math mode");
@@ -1414,7 +1482,7 @@ bag_status bag_selftest_bounded_wait(unsigned long long limit_ns, int* gave_up) 
     if (!gave_up) fail(BAG_ERR_INVALID, "null output pointer");
     if (limit_ns == 0 || limit_ns > 100000000ull) fail(BAG_ERR_INVALID, "limit must be in (0, 0.1 s]");
     int* flag = nullptr;
-    cuda_check(cudaMalloc(&flag, sizeof(int)), "cudaMalloc");
+    cuda_check(device_alloc(reinterpret_cast<void**>(&flag), sizeof(int)), "cudaMalloc");
     cudaError_t e = run_wait_selftest(limit_ns, flag, nullptr);
     if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
     int host = 0;
@@ -1603,9 +1671,12 @@ bag_status bag_multi_workspace_create(int ngpus, const int* devices, int layout,
           cuda_check(cudaSetDevice(dev), "cudaSetDevice");
         }
       }
-      cuda_check(cudaMalloc(&w->a[g], std::max<size_t>(1, size_t(ms) * k) * 4), "shard allocation");
-      cuda_check(cudaMalloc(&w->b[g], std::max<size_t>(1, size_t(k) * ns) * 4), "shard allocation");
-      cuda_check(cudaMalloc(&w->c[g], std::max<size_t>(1, size_t(ms) * ns) * 4), "shard allocation");
+      cuda_check(device_alloc(reinterpret_cast<void**>(&w->a[g]), std::max<size_t>(1, size_t(ms) * k) * 4),
+                 "shard allocation");
+      cuda_check(device_alloc(reinterpret_cast<void**>(&w->b[g]), std::max<size_t>(1, size_t(k) * ns) * 4),
+                 "shard allocation");
+      cuda_check(device_alloc(reinterpret_cast<void**>(&w->c[g]), std::max<size_t>(1, size_t(ms) * ns) * 4),
+                 "shard allocation");
       cuda_check(cudaStreamCreateWithFlags(&w->streams[g], cudaStreamNonBlocking), "stream");
       cuda_check(cudaEventCreateWithFlags(&w->done[g], cudaEventDisableTiming), "event");
       // The shard problem's workspace, on this device, in this thread's math mode.

@@ -14,22 +14,24 @@
 // loads this library holds until the process exits.
 //
 // Rules of use:
-//  * The first call on each device looks up the array's device address
-//    (cudaGetSymbolAddress, with that device current).  Make that first call
-//    before any stream capture on the device.
+//  * Every call looks up the array's device address on the current device
+//    (cudaGetSymbolAddress, with that device current; cheap once the module is
+//    loaded), so a context that was reset and re-created gets the array's new
+//    address.  The first call on a device may load this library's device code
+//    there; make that first call before any stream capture on the device.
 //  * All calls share the one array and it keeps the previous call's contents.
 //    Nothing in it needs to start at zero: every plan writes each scratch
 //    block completely before any kernel reads it.  Calls that can overlap on
 //    the GPU (different streams, or different host threads) race on the array
 //    and must be serialised by the caller.
 //  * Problems whose plan needs more scratch than the array holds are
-//    rejected with BAG_ERR_WORKSPACE before anything is enqueued.
+//    rejected with BAG_ERR_WORKSPACE before anything is enqueued.  In 3xTF32
+//    mode a plan whose prepared TF32 operands fit in the array uses them;
+//    otherwise its leaves run the tensor kernel with the transforms fused in.
 //  * Nothing here calls cudaMalloc, cudaFree or an allocating library
 //    routine.
 #include <cuda_runtime.h>
 
-#include <map>
-#include <mutex>
 #include <string>
 
 #include "../../include/bag_capi.h"
@@ -48,27 +50,15 @@ constexpr size_t kNoAllocScratchFloats = size_t(4) << 20;   // 16 MiB per device
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
-// Device address of the scratch array on the current device (looked up once
-// per device).  Returns nullptr and sets bag_last_error() on failure.
+// Device address of the scratch array on the current device, looked up on
+// every call.  Returns nullptr and sets bag_last_error() on failure.
 float* scratch_on_current_device() {
-  static std::mutex mu;
-  static std::map<int, float*> addresses;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) {
-    set_last_error(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
-    return nullptr;
-  }
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = addresses.find(dev);
-  if (it != addresses.end()) return it->second;
   float* ptr = nullptr;
-  e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_scratch);
+  const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_scratch);
   if (e != cudaSuccess || ptr == nullptr) {
     set_last_error(std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
     return nullptr;
   }
-  addresses[dev] = ptr;
   return ptr;
 }
 

@@ -18,7 +18,11 @@ they are never allocated inside a timed call after that; one per stream,
 because a workspace is scratch for one call at a time.  At most
 ``workspace_cache_limit()`` of them are kept (4 by default): the least
 recently used is freed first (``cudaFree`` waits for the work still using
-it).  This is the counterpart of
+it).  Creating or freeing a workspace is not allowed while a CUDA graph is
+being captured (``torch.cuda.graph``, ``torch.compile(mode="reduce-overhead")``):
+run each shape once on the capturing stream before capture (a warm-up), so
+the captured calls find their workspace cached; a miss during capture raises
+instead of allocating.  This is the counterpart of
 the reference's Triton entry (``src/bag_triton/bag.py:955``) in PyTorch's
 operator registry; ``bag_b200.bag_matmul`` keeps the reference's own
 signature and errors.
@@ -52,6 +56,14 @@ def _create(device: torch.device, m: int, n: int, k: int, depth: int, basis: str
         _bag.set_math_mode(previous)
 
 
+def _no_capture(what: str) -> None:
+    if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+        raise RuntimeError(
+            f"bag_b200: {what} during CUDA graph capture would call cudaMalloc/cudaFree; run "
+            "this shape once on the same stream before capturing (a warm-up) so its "
+            "workspace is cached, and keep the cache limit above the shapes in use")
+
+
 def _workspace(device: torch.device, stream: int, m: int, n: int, k: int, depth: int,
                basis: str, math: str):
     """The cached workspace for this call (caller holds ``_lock``)."""
@@ -60,6 +72,7 @@ def _workspace(device: torch.device, stream: int, m: int, n: int, k: int, depth:
     if ws is not None:
         _workspaces.move_to_end(key)
         return ws
+    _no_capture(f"creating a workspace for {m}x{n}x{k} depth {depth} ({basis}, {math})")
     ws = _create(device, m, n, k, depth, basis, math)
     _workspaces[key] = ws
     while len(_workspaces) > _limit:
@@ -72,6 +85,7 @@ def set_workspace_cache_limit(limit: int) -> None:
     global _limit
     if int(limit) < 1:
         raise ValueError("the workspace cache keeps at least one workspace")
+    _no_capture("changing the workspace cache")
     with _lock:
         _limit = int(limit)
         while len(_workspaces) > _limit:
@@ -84,6 +98,7 @@ def workspace_cache_limit() -> int:
 
 def clear_workspaces() -> None:
     """Free the cached workspaces."""
+    _no_capture("freeing workspaces")
     with _lock:
         for ws in _workspaces.values():
             ws.close()

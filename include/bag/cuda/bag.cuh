@@ -73,6 +73,16 @@ struct Workspace {
 };
 
 // Enqueue C <- AB + C.  A/B/C are distinct column-major N x N FP32 matrices.
+//
+// Leaf arithmetic: the reference's sequential-fmaf FP32 SIMT numerics by
+// default.  A thread that calls bag_set_math_mode(BAG_MATH_3XTF32) before it
+// creates the Workspace gets the tcgen05 3xTF32 leaves on prepared TF32
+// operands, the fast path (the workspace then also holds those operands:
+// bag_workspace_bytes_for(BAG_MATH_3XTF32, ...) gives its size up front).  A
+// Workspace created in FFMA mode and used from a 3XTF32 thread runs the
+// tensor leaves with the transforms fused into their prologue, a slower path.
+// bag_last_leaf_kernel() reports which leaf kernel the last call on the
+// thread ran (BAG_LEAF_KERNEL_FFMA / _TF32_FUSED / _TF32_SINGLE / _TF32_PAIR).
 inline void matmul(const float* a, const float* b, float* c, int n, cudaStream_t caller,
                    Workspace& ws, Backend backend = Backend::ColumnTile8,
                    Schedule schedule = Schedule::Batched) {

@@ -8,6 +8,7 @@
  *
  * Reference interfaces replaced (liuyao0322/bag, path:line):
  *   bag_workspace_create/_destroy/_bytes  bag_cuda::Workspace, include/bag/cuda/bag.cuh:34-55
+ *   bag_workspace_bytes_for               bag_cuda::Workspace::bytes, bag.cuh:52 (sizing before creation)
  *   bag_local_elements                    bag_cuda::local_elements, bag.cuh:23-30
  *   bag_matmul                            bag_cuda::matmul, bag.cuh:247-260
  *   bag_valid_shape                       strassen_cuda::valid_shape, include/bag/cuda/strassen.cuh:57-66
@@ -86,6 +87,14 @@ bag_status bag_workspace_create(int n, int depth, int basis, bag_workspace** out
 /* Workspace for C(m x n) += A(m x k) B(k x n), `batch` problems at once. */
 bag_status bag_workspace_create_ex(int m, int n, int k, int depth, int basis, int batch,
                                    bag_workspace** out);
+/* Bytes bag_workspace_create_ex would allocate for this problem when called
+ * on a thread in math mode `mode` (BAG_MATH_*): in 3XTF32 mode, when every
+ * leaf has K >= 1024, the workspace also holds the prepared TF32 hi/lo leaf
+ * operands (without them, 3XTF32 calls run the slower fused-transform tensor
+ * kernel).  No GPU needed.  New; the reference sizes its workspace with
+ * local_elements (bag.cuh:23-30). */
+bag_status bag_workspace_bytes_for(int mode, int m, int n, int k, int depth, int basis, int batch,
+                                   size_t* bytes);
 bag_status bag_workspace_destroy(bag_workspace* ws);
 size_t bag_workspace_bytes(const bag_workspace* ws);
 /* Device base of the workspace's rounded-operand blocks (NULL when the plan
@@ -113,11 +122,15 @@ bag_status bag_sgemm_ex(int layout, int m, int n, int k, const float* a, long lo
  * Instead of a workspace it uses one built-in device scratch array of
  * 4,194,304 floats (16 MiB) that each GPU loading the library holds until the
  * process exits; problems needing more scratch (e.g. depth 2 beyond N = 1448
- * square) fail with BAG_ERR_WORKSPACE before anything is enqueued.  The first
- * call on a device looks up the array's address and should come before any
- * stream capture on that device.  All calls share the array, so calls that can
- * overlap on the GPU race and must be serialised by the caller.  Allocates
- * nothing (no cudaMalloc/cudaFree). */
+ * square) fail with BAG_ERR_WORKSPACE before anything is enqueued.  Every call
+ * looks up the array's address on the current device (so a device reset does
+ * not leave a stale address behind); the first call on a device may load the
+ * library's device code there and should come before any stream capture on
+ * that device.  In 3XTF32 mode the prepared TF32 operands are used when they
+ * fit in the array, else the leaves run with the transforms fused in
+ * (bag_last_leaf_kernel tells which).  All calls share the array, so calls
+ * that can overlap on the GPU race and must be serialised by the caller.
+ * Allocates nothing (no cudaMalloc/cudaFree). */
 bag_status bag_sgemm_noalloc(int layout, int m, int n, int k, const float* a, long long lda,
                              const float* b, long long ldb, float* c, long long ldc, float beta,
                              int depth, int basis, bag_stream_t stream);
@@ -163,6 +176,10 @@ bag_status bag_profile_set_events(void* start_event, void* end_event);
  * stages | prepare | leaves | decode.  NULL, NULL turns it off. */
 bag_status bag_profile_set_phase_events(void* after_stages, void* after_last);
 unsigned long long bag_launch_count(void);
+/* Device allocations (cudaMalloc calls) this library has made in this process:
+ * workspaces, multi-GPU shard buffers, the self-test's flag.  New; diagnostic
+ * (a caller can check that a call allocated nothing). */
+unsigned long long bag_device_allocations(void);
 /* Math mode of later calls on this host thread (like cublasSetMathMode);
  * new, no reference counterpart. */
 bag_status bag_set_math_mode(int mode);

@@ -5,8 +5,8 @@ The recipe compiles ``oracle/ref_harness.cu`` (a thin C-ABI wrapper) with
 ``-I <reference>/include``, so every kernel in the library is the reference's
 own code, unmodified, built for sm_100a.  Output goes only to ``oracle/_ref/``
 (git-ignored; it travels to the GPU box as a built file).  Needs the
-reference checkout, so it runs only where that exists; elsewhere the prebuilt
-library is used as is.
+reference checkout (its root given as an argument or by BAG_REFERENCE_ROOT), so
+it runs only where that exists; elsewhere the prebuilt library is used as is.
 """
 
 from __future__ import annotations
@@ -21,10 +21,10 @@ LIB = os.path.join(OUT_DIR, "libbagref.so")
 
 
 def build(reference: str | None = None, force: bool = False) -> str | None:
-    reference = reference or os.environ.get("BAG_REFERENCE_ROOT", "/root/reference")
-    include = os.path.join(reference, "include")
+    reference = reference or os.environ.get("BAG_REFERENCE_ROOT")
     src = os.path.join(HERE, "ref_harness.cu")
-    if not os.path.isdir(include):
+    include = os.path.join(reference, "include") if reference else None
+    if not include or not os.path.isdir(include):
         return LIB if os.path.exists(LIB) else None
     if not force and os.path.exists(LIB) and os.path.getmtime(LIB) >= os.path.getmtime(src):
         return LIB

@@ -60,6 +60,7 @@ def test_driver_writes_reference_format(cuda, tmp_path, math_mode, size, depths)
     assert rc == 0
     meta = json.load(open(out + ".metadata.json"))
     assert meta["sizes"] == [size] and meta["bag_math"] == math_mode
+    assert isinstance(meta["cublas_version"], int) and meta["cublas_version"] >= 110000
     rounds = _rows(out + ".rounds.csv")
     assert rounds[0] == ["parent_n", "case", "mode", "round", "repeats", "batch_ms", "latency_ms",
                          "equivalent_tflops"]
@@ -72,3 +73,23 @@ def test_driver_writes_reference_format(cuda, tmp_path, math_mode, size, depths)
     assert {r[1] for r in rounds[1:]} == cases
     ws = _rows(out + ".workspace.csv")
     assert ws[0] == ["parent_n", "depth", "basis", "bytes"] and len(ws) > 1
+
+
+@pytest.mark.gpu
+def test_profile_calls_runs_one_case_without_rounds(cuda, tmp_path, capsys):
+    """--profile-calls K (strassen.cu:147-155): validation, then K calls of the
+    one --only case inside cudaProfilerStart/Stop, and no timed rounds."""
+    out = str(tmp_path / "prof")
+    rc = D.main(["--sizes", "512", "--depths", "2", "--basis", "minimal", "--schedule", "batched",
+                 "--only", "bag_column_minimal_d2_batched", "--profile-calls", "2",
+                 "--output", out])
+    assert rc == 0
+    assert "PROFILE COMPLETE N=512 bag_column_minimal_d2_batched calls=2" in capsys.readouterr().out
+    assert len(_rows(out + ".rounds.csv")) == 1            # header only
+    checks = _rows(out + ".correctness.csv")
+    assert {r[1] for r in checks[1:]} == {"bag_column_minimal_d2_batched"}
+
+
+def test_profile_calls_needs_one_case():
+    with pytest.raises(SystemExit):
+        D.parse(["--profile-calls", "1"])

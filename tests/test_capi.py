@@ -127,3 +127,38 @@ def test_profiling_hooks_take_both_events_or_neither(bag):
     assert lib.bag_profile_set_phase_events(None, None) == 0
     # Counting launches needs no device either.
     assert lib.bag_launch_count() >= 0
+
+
+def test_workspace_bytes_for_follows_the_math_mode():
+    """bag_workspace_bytes_for sizes a workspace as bag_workspace_create_ex would
+    on a thread in that mode: in 3XTF32 the prepared operands (and the deferred
+    decode's product buffers) come on top of the FFMA plan's rounded operands."""
+    import bag_b200 as bag
+    n, depth = 16384, 2
+    ffma = bag.workspace_bytes_for(n, n, n, depth, math="ffma")
+    tf32 = bag.workspace_bytes_for(n, n, n, depth, math="3xtf32")
+    assert ffma == 8 * (n // 2) ** 2 * 4                         # 8 outer operands of 8192^2
+    assert tf32 > ffma + 98 * 2 * 4096 * 4096 * 4                # + 98 operands, hi and lo planes
+    previous = bag.get_math_mode()
+    try:
+        for mode, want in (("ffma", ffma), ("3xtf32", tf32)):
+            bag.set_math_mode(mode)
+            assert bag.plan_dump(n, n, n, n, n, n, depth)["workspace_elements"] * 4 == want
+            assert bag.workspace_bytes_for(n, n, n, depth) == want   # this thread's mode
+    finally:
+        bag.set_math_mode(previous)
+    # Leaves shorter than 1024 stay on FFMA: no prepared region.
+    assert bag.workspace_bytes_for(1024, 1024, 1024, 1, math="3xtf32") == \
+        bag.workspace_bytes_for(1024, 1024, 1024, 1, math="ffma")
+    assert bag.workspace_bytes_for(512, 512, 512, 3, batch=4, math="ffma") == \
+        4 * bag.workspace_bytes_for(512, 512, 512, 3, math="ffma")
+    with pytest.raises(ValueError):
+        bag.workspace_bytes_for(-1, 8, 8, 1)
+
+
+def test_device_allocation_counter_without_a_gpu():
+    import bag_b200 as bag
+    before = bag.device_allocations()
+    bag.workspace_bytes_for(4096, 4096, 4096, 2, math="3xtf32")
+    bag.plan_dump(256, 256, 256, 256, 256, 256, 2)
+    assert bag.device_allocations() == before   # sizing and planning allocate nothing

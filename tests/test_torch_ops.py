@@ -108,3 +108,63 @@ def test_workspace_cache_is_bounded_and_per_stream(monkeypatch):
         T.clear_workspaces()
         T.set_workspace_cache_limit(old)
     assert all(w.closed for w in made)
+
+
+def test_cache_miss_during_graph_capture_raises(monkeypatch):
+    """A workspace miss (or a cache change) while a CUDA graph is being captured
+    raises instead of calling cudaMalloc/cudaFree inside the capture."""
+    from bag_b200 import torch_ops as T
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
+    monkeypatch.setattr(T, "_create", lambda *a: _FakeWorkspace(a))
+    monkeypatch.setattr(T, "_workspaces", T.OrderedDict())
+    dev = torch.device("cuda", 0)
+    with pytest.raises(RuntimeError, match="warm-up"):
+        T._workspace(dev, 1, 64, 64, 64, 1, "minimal", "ffma")
+    with pytest.raises(RuntimeError, match="capture"):
+        T.clear_workspaces()
+    with pytest.raises(RuntimeError, match="capture"):
+        T.set_workspace_cache_limit(2)
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: False)
+    ws = T._workspace(dev, 1, 64, 64, 64, 1, "minimal", "ffma")   # warm-up: created
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
+    assert T._workspace(dev, 1, 64, 64, 64, 1, "minimal", "ffma") is ws   # hit: fine
+
+
+@pytest.mark.gpu
+def test_3xtf32_op_sizes_its_workspace_for_the_prepared_path(cuda):
+    """torch.ops.bag_b200.matmul(math="3xtf32") creates its workspace in that
+    mode, so the call runs the prepared-operand CTA-pair kernel."""
+    import bag_b200 as bag
+    from bag_b200 import torch_ops as T
+    n, depth = 4096, 2
+    g = torch.Generator(device="cuda").manual_seed(41)
+    a = torch.randn(n, n, device="cuda", generator=g)
+    b = torch.randn(n, n, device="cuda", generator=g)
+    c = torch.ops.bag_b200.matmul(a, b, depth, "minimal", "3xtf32")
+    torch.cuda.synchronize()
+    assert bag.last_leaf_kernel() == "tf32_pair"
+    key = (a.device.index, torch.cuda.current_stream().cuda_stream, n, n, n, depth, "minimal",
+           "3xtf32")
+    assert T._workspaces[key].bytes() == bag.workspace_bytes_for(n, n, n, depth, math="3xtf32")
+    assert _rel(c, a.double() @ b.double()) <= 1e-5
+    assert bag.device_error() == 0
+
+
+@pytest.mark.gpu
+def test_op_replays_in_a_cuda_graph_after_warm_up(cuda):
+    g = torch.Generator(device="cuda").manual_seed(43)
+    a = torch.randn(1024, 768, device="cuda", generator=g)
+    b = torch.randn(768, 640, device="cuda", generator=g)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        torch.ops.bag_b200.matmul(a, b, 2, "minimal", "ffma")   # warm-up: workspace cached
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        out = torch.ops.bag_b200.matmul(a, b, 2, "minimal", "ffma")
+    a.copy_(torch.randn(1024, 768, device="cuda", generator=g))
+    graph.replay()
+    torch.cuda.synchronize()
+    assert _rel(out, a.double() @ b.double()) <= 1e-5

@@ -50,11 +50,14 @@ def test_noalloc_matches_workspace_entry_point(bag, cuda, n, depth, basis):
     torch.cuda.synchronize()
     for call in range(2):   # the second call sees the first call's scratch contents
         c = torch.full((n, n), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        allocs_before = bag.device_allocations()
         free_before = torch.cuda.mem_get_info()[0]
         status = _noalloc(bag, a, b, c, depth, basis)
         torch.cuda.synchronize()
         assert status == 0, bag.lib().bag_last_error()
-        if call == 1:   # after the first call set the device up, nothing is allocated
+        assert bag.device_allocations() == allocs_before   # the library allocated nothing
+        if call == 1:   # after the first call set the device up, device memory is unchanged
             assert torch.cuda.mem_get_info()[0] == free_before
         assert bool(torch.isfinite(c).all())
         assert _rel(c, c_ref) <= 2e-6, (call, _rel(c, c_ref))
@@ -86,3 +89,39 @@ def test_noalloc_rejects_problems_beyond_its_scratch(bag, cuda):
     torch.cuda.synchronize()
     assert bool((c == 3.0).all())   # nothing was enqueued
     assert np.isclose(float(c[0, 0]), 3.0)
+
+
+# 3xTF32 mode: a plan whose prepared TF32 operands fit in the built-in scratch
+# runs on them (the CTA-pair leaf kernel); one whose operands do not fit runs
+# the tensor kernel with the transforms fused in.  Both against the workspace
+# entry point in the same mode, and within 1.25x the FFMA path's error (the
+# reference's numerics) as the other 3xTF32 tests bound it.
+@pytest.mark.parametrize("m,k,n,depth,kernel", [(512, 1024, 512, 0, "tf32_pair"),
+                                                (512, 2048, 512, 1, "tf32_fused")])
+def test_noalloc_in_3xtf32_mode(bag, cuda, m, k, n, depth, kernel):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(m + k + depth)
+    a = torch.randn(m, k, device="cuda", generator=g)
+    b = torch.randn(k, n, device="cuda", generator=g)
+    exact = a.double() @ b.double()
+    c_ffma = torch.empty(m, n, device="cuda")
+    bag.sgemm(a, b, c_ffma, beta=0.0, depth=depth, workspace=bag.Workspace.for_problem(n, m, k, depth))
+    bag.set_math_mode("3xtf32")
+    try:
+        ws = bag.Workspace.for_problem(n, m, k, depth)
+        c_ref = torch.empty(m, n, device="cuda")
+        bag.sgemm(a, b, c_ref, beta=0.0, depth=depth, workspace=ws)
+        for call in range(2):
+            c = torch.full((m, n), float("nan"), device="cuda")
+            torch.cuda.synchronize()
+            allocs = bag.device_allocations()
+            assert _noalloc(bag, a, b, c, depth, "minimal") == 0, bag.lib().bag_last_error()
+            torch.cuda.synchronize()
+            assert bag.device_allocations() == allocs
+            assert bag.last_leaf_kernel() == kernel, (call, bag.last_leaf_kernel())
+            assert bool(torch.isfinite(c).all())
+            assert _rel(c, exact) <= 1.25 * _rel(c_ffma, exact), call
+            assert _rel(c, c_ref) <= 2e-6, call
+    finally:
+        bag.set_math_mode("ffma")
+    assert bag.device_error() == 0
