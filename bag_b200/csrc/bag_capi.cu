@@ -254,8 +254,57 @@ struct Builder {
     return {p, ld, ws_bstride};
   }
 
-  // Round a signed sum of blocks into the workspace (one job output).
-  View materialize(const Expr& e, int rows, int cols) {
+  // Rounded operands of the deepest level on the prepared path stay
+  // virtual: no workspace block is written for them; the prepare pass
+  // evaluates them (the mids of a tree group) in the same order instead.  A
+  // virtual block is a range of fake addresses far above any device pointer
+  // with its definition, so a view inside it resolves to the same offset in
+  // each of the definition's terms.
+  bool virtual_last = false;
+  struct VBuf {
+    const float* begin;
+    const float* end;
+    long long ld;
+    int rows, cols;
+    Expr def;
+  };
+  std::vector<VBuf> vbufs;
+  uintptr_t vnext = uintptr_t(1) << 50;
+
+  const VBuf* vbuf_of(const View& v) const {
+    for (const VBuf& b : vbufs)
+      if (v.p >= b.begin && v.p < b.end) return &b;
+    return nullptr;
+  }
+
+  // A view as a signed sum of real blocks: a virtual view is its block's
+  // definition at the view's offset, any other view itself.
+  Expr resolve(const View& v) const {
+    const VBuf* b = vbuf_of(v);
+    if (!b) return {{v, 1.f}};
+    const long long off = v.p - b->begin, col = off / b->ld, row = off % b->ld;
+    Expr e;
+    for (const STerm& t : b->def)
+      e.push_back({{t.v.p + row + col * t.v.ld, t.v.ld, t.v.bstride}, t.coef});
+    return e;
+  }
+
+  // Round a signed sum of blocks into the workspace (one job output), or,
+  // with `may_virtualize` on the prepared path and only real blocks in the
+  // sum, define a virtual block.
+  View materialize(const Expr& e, int rows, int cols, bool may_virtualize = false) {
+    if (virtual_last && may_virtualize) {
+      bool real = true;
+      for (const STerm& t : e) real = real && vbuf_of(t.v) == nullptr;
+      if (real) {
+        const long long ld = std::max<long long>(4, (rows + 3) / 4 * 4);
+        const float* p = reinterpret_cast<const float*>(vnext);
+        const size_t count = size_t(ld) * std::max(cols, 1);
+        vnext += (count * sizeof(float) + 255) / 256 * 256;
+        vbufs.push_back({p, p + count, ld, rows, cols, e});
+        return {p, ld, ws_bstride};
+      }
+    }
     int stage = 1;
     for (const STerm& t : e) stage = std::max(stage, stage_of(t.v) + 1);
     if ((int)stages.size() < stage) stages.resize(stage);
@@ -310,9 +359,12 @@ struct Builder {
   // once, as TF32 hi and lo rows of the prepared region (rows of
   // prep_row_len k values), by one HBM-speed pass; the leaf products then
   // only load and multiply.  With the tensor core the fused transform and
-  // split, not the tensor core, bound a product.
+  // split, not the tensor core, bound a product.  An operand is a signed sum
+  // of mids, each mid a signed sum of real blocks (a virtual block's
+  // definition, or one block).
+  using Mid = Expr;
   struct PrepOp {
-    Expr terms;
+    std::vector<std::pair<Mid, float>> terms;   // (mid, +-1) in the prologue's order
     int rows, cols;
     bool transpose;   // left operands: column-major rows x cols -> k-contiguous rows
     int hi_row;       // lo rows follow at hi_row + rows
@@ -321,17 +373,27 @@ struct Builder {
   int prep_rows = 0, prep_row_len = 0;
   View prep_region{nullptr, 0, 0};
 
+  static bool same_expr(const Expr& a, const Expr& b) {
+    if (a.size() != b.size()) return false;
+    for (size_t i = 0; i < a.size(); ++i)
+      if (!(a[i].v == b[i].v) || a[i].coef != b[i].coef) return false;
+    return true;
+  }
+
   int prep_index(const Expr& e, int rows, int cols, bool transpose) {
+    std::vector<std::pair<Mid, float>> terms;
+    for (const STerm& t : e) terms.push_back({resolve(t.v), t.coef});
     for (size_t i = 0; i < prep.size(); ++i) {
       const PrepOp& o = prep[i];
-      if (o.rows != rows || o.cols != cols || o.transpose != transpose || o.terms.size() != e.size())
+      if (o.rows != rows || o.cols != cols || o.transpose != transpose ||
+          o.terms.size() != terms.size())
         continue;
       bool same = true;
-      for (size_t t = 0; t < e.size() && same; ++t)
-        same = o.terms[t].v == e[t].v && o.terms[t].coef == e[t].coef;
+      for (size_t t = 0; t < terms.size() && same; ++t)
+        same = o.terms[t].second == terms[t].second && same_expr(o.terms[t].first, terms[t].first);
       if (same) return int(i);
     }
-    prep.push_back({e, rows, cols, transpose, prep_rows});
+    prep.push_back({terms, rows, cols, transpose, prep_rows});
     prep_rows += 2 * rows;
     return int(prep.size()) - 1;
   }
@@ -345,56 +407,104 @@ struct Builder {
       l.prep_r = prep_index(l.right, l.n, l.k, false);
     }
     prep_region = alloc(prep_row_len, std::max(prep_rows, 1), int(stages.size()) + 1);
-    group_prepared();
+    build_trees();
   }
 
-  // Prepare groups: prepared operands of one shape that are sums of the same
-  // few source blocks share a group, so prep_group_kernel reads each source
-  // block once per tile for all of them.  First fit, in prep order; each
-  // output keeps its operand's term order (expr codes: +-(input index + 1)).
-  struct PrepGroupHost {
+  // Tree groups (prep_tree_kernel): operands of one shape whose mids fit a
+  // segment (<= 4 mids, <= 8 outputs) and whose blocks fit a group (<= 16
+  // inputs, <= 8 segments) are prepared together, each block read once per
+  // tile.  First fit in prep order.
+  struct TreeSegHost {
+    std::vector<Mid> mids;
+    std::vector<int> ops;                  // indices into prep
+    std::vector<std::vector<int>> expr;    // per op: +-(mid index + 1)
+  };
+  struct TreeGroupHost {
     int rows, cols;
     bool transpose;
     std::vector<View> in;
-    std::vector<int> ops;                  // indices into prep
-    std::vector<std::vector<int>> expr;    // per output, its terms as input codes
+    std::vector<TreeSegHost> segs;
+    int input_code(const STerm& t) const {
+      const int u = int(std::find(in.begin(), in.end(), t.v) - in.begin());
+      return t.coef > 0 ? u + 1 : -(u + 1);
+    }
   };
-  std::vector<PrepGroupHost> prep_groups;
+  std::vector<TreeGroupHost> trees;
 
-  void group_prepared() {
-    prep_groups.clear();
+  static int find_mid(const std::vector<Mid>& mids, const Mid& m) {
+    for (size_t i = 0; i < mids.size(); ++i)
+      if (same_expr(mids[i], m)) return int(i);
+    return -1;
+  }
+
+  void build_trees() {
+    trees.clear();
     for (size_t j = 0; j < prep.size(); ++j) {
       const PrepOp& o = prep[j];
       if (o.terms.empty() || o.terms.size() > size_t(kMaxOperandTerms))
         fail(BAG_ERR_INTERNAL, "prepared operand has an unsupported term count");
-      PrepGroupHost* home = nullptr;
-      for (PrepGroupHost& g : prep_groups) {
-        if (g.rows != o.rows || g.cols != o.cols || g.transpose != o.transpose ||
-            g.ops.size() >= size_t(kMaxPrepGroupOut))
-          continue;
-        size_t fresh = 0;
-        for (const STerm& t : o.terms)
-          if (std::find(g.in.begin(), g.in.end(), t.v) == g.in.end()) ++fresh;
-        if (g.in.size() + fresh <= size_t(kMaxPrepGroupIn)) {
-          home = &g;
-          break;
+      std::vector<Mid> om;
+      std::vector<View> oin;
+      for (const auto& t : o.terms) {
+        if (t.second != 1.f && t.second != -1.f)
+          fail(BAG_ERR_INTERNAL, "prepared operand term coefficient is not +-1");
+        if (t.first.empty() || t.first.size() > size_t(kMaxOperandTerms))
+          fail(BAG_ERR_INTERNAL, "prepared operand mid has an unsupported term count");
+        if (find_mid(om, t.first) < 0) om.push_back(t.first);
+        for (const STerm& x : t.first) {
+          if (x.coef != 1.f && x.coef != -1.f)
+            fail(BAG_ERR_INTERNAL, "prepared operand block coefficient is not +-1");
+          if (std::find(oin.begin(), oin.end(), x.v) == oin.end()) oin.push_back(x.v);
         }
       }
+      if (om.size() > size_t(kTreeMid) || oin.size() > size_t(kTreeIn))
+        fail(BAG_ERR_INTERNAL, "prepared operand too wide for a tree group");
+      auto fresh_inputs = [&](const TreeGroupHost& g) {
+        size_t fresh = 0;
+        for (const View& v : oin)
+          if (std::find(g.in.begin(), g.in.end(), v) == g.in.end()) ++fresh;
+        return g.in.size() + fresh;
+      };
+      TreeGroupHost* home = nullptr;
+      TreeSegHost* seg = nullptr;
+      for (TreeGroupHost& g : trees) {
+        if (g.rows != o.rows || g.cols != o.cols || g.transpose != o.transpose ||
+            fresh_inputs(g) > size_t(kTreeIn))
+          continue;
+        for (TreeSegHost& sg : g.segs) {
+          if (sg.ops.size() >= size_t(kTreeOut)) continue;
+          size_t fresh = 0;
+          for (const Mid& m : om) fresh += find_mid(sg.mids, m) < 0 ? 1 : 0;
+          if (sg.mids.size() + fresh <= size_t(kTreeMid)) {
+            home = &g;
+            seg = &sg;
+            break;
+          }
+        }
+        if (seg) break;
+        if (!home && g.segs.size() < size_t(kTreeSeg)) home = &g;
+      }
       if (!home) {
-        prep_groups.push_back({o.rows, o.cols, o.transpose, {}, {}, {}});
-        home = &prep_groups.back();
+        trees.push_back({o.rows, o.cols, o.transpose, {}, {}});
+        home = &trees.back();
       }
+      if (!seg) {
+        home->segs.push_back({});
+        seg = &home->segs.back();
+      }
+      for (const View& v : oin)
+        if (std::find(home->in.begin(), home->in.end(), v) == home->in.end()) home->in.push_back(v);
       std::vector<int> codes;
-      for (const STerm& t : o.terms) {
-        auto it = std::find(home->in.begin(), home->in.end(), t.v);
-        if (it == home->in.end()) it = home->in.insert(home->in.end(), t.v);
-        if (t.coef != 1.f && t.coef != -1.f)
-          fail(BAG_ERR_INTERNAL, "prepared operand term coefficient is not +-1");
-        const int u = int(it - home->in.begin());
-        codes.push_back(t.coef > 0 ? u + 1 : -(u + 1));
+      for (const auto& t : o.terms) {
+        int mi = find_mid(seg->mids, t.first);
+        if (mi < 0) {
+          seg->mids.push_back(t.first);
+          mi = int(seg->mids.size()) - 1;
+        }
+        codes.push_back(t.second > 0 ? mi + 1 : -(mi + 1));
       }
-      home->ops.push_back(int(j));
-      home->expr.push_back(codes);
+      seg->ops.push_back(int(j));
+      seg->expr.push_back(codes);
     }
   }
 
@@ -448,13 +558,13 @@ struct Builder {
 
   // Reduce an operand to a single unit-coefficient block.  A lone negated
   // block keeps its data; the sign moves to the outputs (exact).
-  View single(const Expr& e, int rows, int cols, float* sign) {
+  View single(const Expr& e, int rows, int cols, float* sign, bool may_virtualize = false) {
     if (e.size() == 1) {
       *sign = e[0].coef;
       return e[0].v;
     }
     *sign = 1.f;
-    return materialize(e, rows, cols);
+    return materialize(e, rows, cols, may_virtualize);
   }
 
   static void quads(const View& v, int rows, int cols, View q[4]) {
@@ -467,11 +577,11 @@ struct Builder {
 
   // Full-basis transform of one operand's quadrants (bag.cuh:66-68):
   // T11 = X11 (a view), T12 = X12 - X21 + X22, T21 = X22 - X21, T22 = X12 + X22.
-  void full_transform(const View q[4], int rows, int cols, View t[4]) {
+  void full_transform(const View q[4], int rows, int cols, View t[4], bool may_virtualize) {
     t[0] = q[0];
-    t[1] = materialize({{q[1], 1.f}, {q[2], -1.f}, {q[3], 1.f}}, rows, cols);
-    t[2] = materialize({{q[3], 1.f}, {q[2], -1.f}}, rows, cols);
-    t[3] = materialize({{q[1], 1.f}, {q[3], 1.f}}, rows, cols);
+    t[1] = materialize({{q[1], 1.f}, {q[2], -1.f}, {q[3], 1.f}}, rows, cols, may_virtualize);
+    t[2] = materialize({{q[3], 1.f}, {q[2], -1.f}}, rows, cols, may_virtualize);
+    t[3] = materialize({{q[1], 1.f}, {q[3], 1.f}}, rows, cols, may_virtualize);
   }
 
   void expand(const Expr& L, const Expr& R, const std::vector<Target>& T, int m, int k, int n,
@@ -480,9 +590,13 @@ struct Builder {
       leaves.push_back({m, n, k, L, R, T});
       return;
     }
+    // At the last level the operands' quadrants become leaf operand terms, so
+    // on the prepared path what this level rounds can stay virtual (the Full
+    // basis transforms the quadrants first: there only the transform does).
+    const bool last = depth == 1;
     float ls = 1.f, rs = 1.f;
-    const View lv = single(L, m, k, &ls);
-    const View rv = single(R, k, n, &rs);
+    const View lv = single(L, m, k, &ls, last && basis != kFull);
+    const View rv = single(R, k, n, &rs, last && basis != kFull);
     View lq[4], rq[4];
     quads(lv, m, k, lq);
     quads(rv, k, n, rq);
@@ -493,8 +607,8 @@ struct Builder {
                                                      : kMinimal7;
     if (basis == kFull) {
       View lt[4], rt[4];
-      full_transform(lq, h, kk, lt);
-      full_transform(rq, kk, w, rt);
+      full_transform(lq, h, kk, lt, last);
+      full_transform(rq, kk, w, rt, last);
       std::copy(lt, lt + 4, lq);
       std::copy(rt, rt + 4, rq);
     }
@@ -537,6 +651,7 @@ void build_plan(const GemmDesc& g, float* ws, long long ws_bstride, Builder& B,
   B.basis = g.basis;
   B.ws = ws;
   B.ws_bstride = ws_bstride;
+  B.virtual_last = leaf_operands;
   const View A{g.a, g.lda, g.sa}, Bv{g.b, g.ldb, g.sb}, C{g.c, g.ldc, g.sc};
   if (g.m == 0 || g.n == 0) return;
   int depth = g.depth;
@@ -656,35 +771,44 @@ int prep_leaf_kind() {
 }
 
 void run_prepared(Builder& B, int batch, cudaStream_t stream) {
-  const int tile = prep_row_align();
-  const std::vector<Builder::PrepGroupHost>& groups = B.prep_groups;
-  for (size_t g0 = 0; g0 < groups.size(); g0 += kMaxPrepGroups) {
-    PrepGroupPlan pp;
+  const int tile = 32;   // prep_tree_kernel's tile: 32 rows x 32 k
+  const std::vector<Builder::TreeGroupHost>& groups = B.trees;
+  for (size_t g0 = 0; g0 < groups.size(); g0 += kMaxTreeGroups) {
+    PrepTreePlan pp;
     std::memset(&pp, 0, sizeof(pp));
     pp.row_len = B.prep_row_len;
     pp.region = const_cast<float*>(B.prep_region.p);
     pp.region_bstride = B.ws_bstride;
     long long tiles = 0;
-    for (size_t gi = g0; gi < std::min(groups.size(), g0 + kMaxPrepGroups); ++gi) {
-      const Builder::PrepGroupHost& hg = groups[gi];
-      PrepGroup& G = pp.group[pp.ngroups++];
+    for (size_t gi = g0; gi < std::min(groups.size(), g0 + kMaxTreeGroups); ++gi) {
+      const Builder::TreeGroupHost& hg = groups[gi];
+      TreeGroup& G = pp.group[pp.ngroups++];
       G.rows = hg.rows;
       G.cols = hg.cols;
       G.transpose = hg.transpose ? 1 : 0;
       G.nin = int(hg.in.size());
       for (int u = 0; u < G.nin; ++u) G.in[u] = make_term(hg.in[u], 1.f, 0);
-      G.nout = int(hg.ops.size());
-      for (int q = 0; q < G.nout; ++q) {
-        G.out_hi[q] = B.prep[hg.ops[q]].hi_row;
-        for (size_t t = 0; t < hg.expr[q].size(); ++t)
-          G.expr[q][t] = static_cast<signed char>(hg.expr[q][t]);
+      G.nseg = int(hg.segs.size());
+      for (int sg = 0; sg < G.nseg; ++sg) {
+        const Builder::TreeSegHost& hs = hg.segs[sg];
+        TreeSeg& S = G.seg[sg];
+        S.nmid = int(hs.mids.size());
+        for (int i = 0; i < S.nmid; ++i)
+          for (size_t q = 0; q < hs.mids[i].size(); ++q)
+            S.mid[i][q] = static_cast<signed char>(hg.input_code(hs.mids[i][q]));
+        S.nout = int(hs.ops.size());
+        for (int o = 0; o < S.nout; ++o) {
+          S.out_hi[o] = B.prep[hs.ops[o]].hi_row;
+          for (size_t q = 0; q < hs.expr[o].size(); ++q)
+            S.expr[o][q] = static_cast<signed char>(hs.expr[o][q]);
+        }
       }
       G.tile_begin = tiles;
       tiles += (long long)((hg.rows + tile - 1) / tile) * (B.prep_row_len / tile);
     }
     pp.ntiles = tiles;
     if (tiles > INT32_MAX) fail(BAG_ERR_SHAPE, "problem too large");
-    cuda_check(launch_prep_groups(pp, batch, stream), "prepare launch");
+    cuda_check(launch_prep_tree(pp, batch, stream), "prepare launch");
     ++g_launches;
   }
   if (g_prof_start) cuda_check(cudaEventRecord(g_prof_start, stream), "cudaEventRecord");
@@ -838,21 +962,26 @@ void execute_plan(Builder& B, int batch, cudaStream_t stream,
     for (const STerm& t : l.right) vec = vec && view_vec_ok(t.v);
     for (const Target& t : l.out) vec = vec && view_vec_ok(t.v);
   }
-  // The tensor path reads operands by TMA, so it needs aligned operands
+  // The tensor paths read operands by TMA, so they need aligned operands
   // (vec) but no common leading dimension among a product's terms.
   bool tensor = g_math_mode == BAG_MATH_3XTF32 && vec;
-  for (const HostLeaf& l : B.leaves)
-    tensor = tensor && l.k >= kTcMinK && tc_supported(int(l.left.size()), int(l.right.size()));
-  if (!tensor) split_long_chains(B.leaves);
-  bool all_fast = vec;
-  for (const HostLeaf& l : B.leaves) all_fast = all_fast && signature(l, vec) != kSigGeneric;
-  g_last_leaf_path = tensor ? BAG_MATH_3XTF32 : BAG_MATH_FFMA;
+  for (const HostLeaf& l : B.leaves) tensor = tensor && l.k >= kTcMinK;
   g_last_prep_kind = -1;
-  if (tensor && !B.prep.empty() && prep_supported()) {
+  if (!B.prep.empty()) {
+    // A prepared plan's deepest operands may be virtual: it runs only here.
+    if (!(tensor && prep_supported()))
+      fail(BAG_ERR_INTERNAL, "a prepared-operand plan cannot take the prepared path");
+    g_last_leaf_path = BAG_MATH_3XTF32;
     run_prepared(B, batch, stream);
     record_phase(g_phase_done, stream);
     return;
   }
+  for (const HostLeaf& l : B.leaves)
+    tensor = tensor && tc_supported(int(l.left.size()), int(l.right.size()));
+  if (!tensor) split_long_chains(B.leaves);
+  bool all_fast = vec;
+  for (const HostLeaf& l : B.leaves) all_fast = all_fast && signature(l, vec) != kSigGeneric;
+  g_last_leaf_path = tensor ? BAG_MATH_3XTF32 : BAG_MATH_FFMA;
   if (g_prof_start) cuda_check(cudaEventRecord(g_prof_start, stream), "cudaEventRecord");
   const int cfg = tensor ? -1 : choose_tile(B.leaves, sms, vec);
   const TileShape ts = tensor ? tc_tile_shape() : leaf_tile_shape(cfg);
@@ -935,8 +1064,12 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
     return;
   }
   // 3xTF32 mode prepares the leaf operands when the workspace was sized for
-  // it (created in that mode); otherwise the prologue stays fused.
-  bool leaf_operands = leaf_materialisation_wanted(g, g_math_mode);
+  // it (created in that mode) and the prepared path can run (TMA available,
+  // 16-byte-aligned matrices); otherwise the prologue stays fused.
+  const bool aligned = aligned16(g.a) && aligned16(g.b) && aligned16(g.c) && g.lda % 4 == 0 &&
+                       g.ldb % 4 == 0 && g.ldc % 4 == 0 && g.sa % 4 == 0 && g.sb % 4 == 0 &&
+                       g.sc % 4 == 0;
+  bool leaf_operands = aligned && leaf_materialisation_wanted(g, g_math_mode) && prep_supported();
   size_t need = plan_workspace_elements(g, leaf_operands);
   if (leaf_operands && (!ws || need * size_t(g.batch) > ws->elements)) {
     leaf_operands = false;
@@ -1038,6 +1171,11 @@ std::string dump_plan(int m, int n, int k, long long lda, long long ldb, long lo
   // In 3xTF32 mode the plan also lists the prepared (TF32 hi/lo) operands.
   build_plan(g, reinterpret_cast<float*>(4 * unit), 0, B, leaf_materialisation_wanted(g, g_math_mode));
   auto ref = [&](const View& v) {
+    if (B.vbuf_of(v)) {   // a virtual block (prepared path): buffer id 4
+      const long long off = (long long)((reinterpret_cast<uintptr_t>(v.p) - (uintptr_t(1) << 50)) /
+                                        sizeof(float));
+      return "[4," + std::to_string(off) + "," + std::to_string(v.ld) + "]";
+    }
     const uintptr_t p = reinterpret_cast<uintptr_t>(v.p);
     const uintptr_t base = p / unit;
     const long long off = (long long)((p - base * unit) / sizeof(float));
@@ -1104,22 +1242,48 @@ std::string dump_plan(int m, int n, int k, long long lda, long long ldb, long lo
            std::to_string(int(d.terms[p][e].second)) + "]";
     s += "]";
   }
+  // Tree groups: inputs (blocks), then per segment its mids (codes over the
+  // inputs), its operands (indices into "prepared") and their codes over the
+  // segment's mids.
   s += "]},\"prep_groups\":[";
-  for (size_t gi = 0; gi < B.prep_groups.size(); ++gi) {
-    const Builder::PrepGroupHost& g = B.prep_groups[gi];
+  auto codes = [](const std::vector<int>& c) {
+    std::string r = "[";
+    for (size_t t = 0; t < c.size(); ++t) r += (t ? "," : "") + std::to_string(c[t]);
+    return r + "]";
+  };
+  for (size_t gi = 0; gi < B.trees.size(); ++gi) {
+    const Builder::TreeGroupHost& g = B.trees[gi];
     s += gi ? "," : "";
     s += "{\"rows\":" + std::to_string(g.rows) + ",\"cols\":" + std::to_string(g.cols) +
          ",\"transpose\":" + std::string(g.transpose ? "true" : "false") + ",\"in\":[";
     for (size_t u = 0; u < g.in.size(); ++u) s += (u ? "," : "") + ref(g.in[u]);
-    s += "],\"ops\":[";
-    for (size_t q = 0; q < g.ops.size(); ++q) s += (q ? "," : "") + std::to_string(g.ops[q]);
-    s += "],\"expr\":[";
-    for (size_t q = 0; q < g.expr.size(); ++q) {
-      s += q ? ",[" : "[";
-      for (size_t t = 0; t < g.expr[q].size(); ++t)
-        s += (t ? "," : "") + std::to_string(g.expr[q][t]);
-      s += "]";
+    s += "],\"segs\":[";
+    for (size_t sg = 0; sg < g.segs.size(); ++sg) {
+      const Builder::TreeSegHost& hs = g.segs[sg];
+      s += sg ? ",{\"mids\":[" : "{\"mids\":[";
+      for (size_t i = 0; i < hs.mids.size(); ++i) {
+        std::vector<int> c;
+        for (const STerm& t : hs.mids[i]) c.push_back(g.input_code(t));
+        s += (i ? "," : "") + codes(c);
+      }
+      s += "],\"ops\":" + codes(hs.ops) + ",\"expr\":[";
+      for (size_t o = 0; o < hs.expr.size(); ++o) s += (o ? "," : "") + codes(hs.expr[o]);
+      s += "]}";
     }
+    s += "]}";
+  }
+  s += "]";
+  // Virtual blocks (prepared path): what a materialisation job would have
+  // written, for checkers that evaluate the leaf operands the long way.
+  s += ",\"virtual\":[";
+  for (size_t i = 0; i < B.vbufs.size(); ++i) {
+    const Builder::VBuf& vb = B.vbufs[i];
+    s += (i ? ",{\"out\":" : "{\"out\":") + ref({vb.begin, vb.ld, 0}) +
+         ",\"rows\":" + std::to_string(vb.rows) + ",\"cols\":" + std::to_string(vb.cols) +
+         ",\"terms\":[";
+    for (size_t t = 0; t < vb.def.size(); ++t)
+      s += std::string(t ? "," : "") + "[" + ref(vb.def[t].v) + "," +
+           std::to_string(int(vb.def[t].coef)) + "]";
     s += "]}";
   }
   s += "]";
@@ -1131,9 +1295,14 @@ std::string dump_plan(int m, int n, int k, long long lda, long long ldb, long lo
     s += "{\"rows\":" + std::to_string(o.rows) + ",\"cols\":" + std::to_string(o.cols) +
          ",\"transpose\":" + std::string(o.transpose ? "true" : "false") +
          ",\"hi_row\":" + std::to_string(o.hi_row) + ",\"terms\":[";
-    for (size_t t = 0; t < o.terms.size(); ++t)
-      s += std::string(t ? "," : "") + "[" + ref(o.terms[t].v) + "," +
-           std::to_string(int(o.terms[t].coef)) + "]";
+    // [[[block, coef], ...] (a mid), coef] per term
+    for (size_t t = 0; t < o.terms.size(); ++t) {
+      s += std::string(t ? "," : "") + "[[";
+      for (size_t q = 0; q < o.terms[t].first.size(); ++q)
+        s += std::string(q ? "," : "") + "[" + ref(o.terms[t].first[q].v) + "," +
+             std::to_string(int(o.terms[t].first[q].coef)) + "]";
+      s += "]," + std::to_string(int(o.terms[t].second)) + "]";
+    }
     s += "]}";
   }
   s += "]}";

@@ -58,7 +58,7 @@ cudaError_t launch_leaf_tc(const LeafPlan& plan, const TcSource* sources, int ns
                            cudaStream_t stream);
 cudaError_t read_and_clear_tc_device_error(unsigned* value);
 
-// Prepared-operand 3xTF32 path (bag_tc3_kernel.cu): prep_kernel writes each
+// Prepared-operand 3xTF32 path (bag_tc3_kernel.cu): prep_tree_kernel writes each
 // leaf operand's TF32 hi/lo rows into a workspace region (rows of row_len k,
 // row_len a multiple of prep_row_align()); the leaf kernels run the products
 // on them: leaf_prep_kernel with 128 x 256 tiles on one SM each
@@ -69,7 +69,7 @@ bool prep_supported();
 bool prep_pair_supported();
 int prep_row_align();
 TileShape prep_tile_shape(int kind);
-cudaError_t launch_prep_groups(const PrepGroupPlan& plan, int batch, cudaStream_t stream);
+cudaError_t launch_prep_tree(const PrepTreePlan& plan, int batch, cudaStream_t stream);
 cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* region,
                              long long row_len, long long rows, long long region_bstride,
                              int batch, cudaStream_t stream);

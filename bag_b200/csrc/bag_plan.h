@@ -86,38 +86,55 @@ struct MatPlan {
   MatJob job[kMaxJobs];
 };
 
-// Prepared operands (3xTF32 path): every distinct leaf operand -- the signed
-// sum of its blocks, in the fused prologue's order -- is written as TF32 hi
-// and lo rows of `cols` k values (k contiguous, zero-padded to the region's
-// row length) at rows [out_hi, out_hi + rows) and [out_hi + rows, out_hi +
-// 2 rows) of the prepared region; a left operand (column-major rows x cols,
-// rows contiguous) is transposed on the way, a right operand (k contiguous)
-// keeps its orientation.  Operands that are signed sums of the same few
-// source blocks -- the 7 leaf operands of one outer product at depth 2, the 7
-// made of A's (or B's) quadrants at depth 1 -- form a group and are prepared
-// together, each source block read once per tile.  expr[o]: output o's terms,
-// signed (input index + 1), in the prologue's order (the first with its sign,
-// then fmaf); 0 ends.
-constexpr int kMaxPrepGroupIn = 4;
-constexpr int kMaxPrepGroupOut = 8;
-constexpr int kMaxPrepGroups = 24;
+// Prepared operands (3xTF32 path): every distinct leaf operand is written as
+// TF32 hi and lo rows of `cols` k values (k contiguous, zero-padded to the
+// region's row length) at rows [out_hi, out_hi + rows) and [out_hi + rows,
+// out_hi + 2 rows) of the prepared region; a left operand (column-major
+// rows x cols, rows contiguous) is transposed on the way, a right operand (k
+// contiguous) keeps its orientation.
+//
+// A leaf operand is a signed sum of "mids", each mid a signed sum of source
+// blocks: at the deepest recursion level the operand the reference rounds
+// before its last split (prepare_child, bag.cuh:124-135; the Full-basis
+// transform, bag.cuh:66-68) is a mid, evaluated in FP32 in the reference's
+// order exactly as a materialisation pass would round it, and the leaf
+// operand sums such mids in the fused prologue's order (the first term with
+// its sign, then fmaf with +-1).  The values are therefore those of
+// materialising the mids first, without their HBM round trip.  A tree group
+// holds up to 16 source blocks of one shape, read once per tile, and up to 8
+// segments; a segment holds up to 4 mids (codes over the group's inputs) and
+// up to 8 outputs (codes over the segment's mids).  At depth 2 with the
+// Minimal basis one group per side covers all 49 leaf operands: the 16
+// sub-blocks of A's (B's) quadrants, one segment per outer product.  Codes
+// are signed (index + 1); 0 ends a list.
+constexpr int kTreeIn = 16;
+constexpr int kTreeSeg = 8;
+constexpr int kTreeMid = 4;
+constexpr int kTreeOut = 8;
+constexpr int kMaxTreeGroups = 20;
 
-struct PrepGroup {
-  int rows, cols;
-  int transpose, nin, nout;
-  Term in[kMaxPrepGroupIn];                                // coef unused
-  int out_hi[kMaxPrepGroupOut];                            // lo rows at out_hi + rows
-  signed char expr[kMaxPrepGroupOut][kMaxOperandTerms];
-  long long tile_begin;                                    // first work item of the group
+struct TreeSeg {
+  int nmid, nout;
+  signed char mid[kTreeMid][kMaxOperandTerms];    // per mid: its inputs
+  signed char expr[kTreeOut][kMaxOperandTerms];   // per output: its mids
+  int out_hi[kTreeOut];                           // lo rows at out_hi + rows
 };
 
-struct PrepGroupPlan {
+struct TreeGroup {
+  int rows, cols;
+  int transpose, nin, nseg;
+  Term in[kTreeIn];                               // coef unused
+  TreeSeg seg[kTreeSeg];
+  long long tile_begin;                           // first work item of the group
+};
+
+struct PrepTreePlan {
   int ngroups;
-  int row_len;                 // floats per region row (k, padded to the stage length)
+  int row_len;                 // floats per region row (k, padded to the tile length)
   float* region;
   long long region_bstride;    // floats between batch entries' regions
   long long ntiles;
-  PrepGroup group[kMaxPrepGroups];
+  TreeGroup group[kMaxTreeGroups];
 };
 
 // Leaf products on prepared operands: A rows a_hi.., B rows b_hi.. of the
@@ -157,6 +174,6 @@ struct DecodePlan {
 static_assert(sizeof(LeafPlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(DecodePlan) < 32000, "kernel parameter limit");
 static_assert(sizeof(MatPlan) < 32000, "kernel parameter limit");
-static_assert(sizeof(PrepGroupPlan) < 32000, "kernel parameter limit");
+static_assert(sizeof(PrepTreePlan) < 32000, "kernel parameter limit");
 
 }  // namespace bag_b200

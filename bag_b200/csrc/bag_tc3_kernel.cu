@@ -1,13 +1,13 @@
 // Prepared-operand 3xTF32 path of the BAG FP32 matmul (sm_100a).
 //
-// prep_group_kernel: one HBM-speed pass writes every distinct leaf operand of
-//   the plan -- the signed sum of its blocks, in the fused prologue's order
-//   (x + delta*y, bag.cuh:69-73) -- as TF32 hi = rn_tf32(x) and
+// prep_tree_kernel: one HBM-speed pass writes every distinct leaf operand of
+//   the plan -- a signed sum of mids, each mid a signed sum of source blocks,
+//   both in the reference's evaluation order (x + delta*y, bag.cuh:69-73;
+//   prepare_child, bag.cuh:124-135) -- as TF32 hi = rn_tf32(x) and
 //   lo = rn_tf32(x - hi) rows of a workspace region, k contiguous (left
-//   operands are transposed on the way through a shared-memory tile) and
-//   zero-padded to the region's row length (a multiple of the 64-k tile);
-//   operands made of the same source blocks are written together, each block
-//   read once per tile.
+//   operands are transposed on the way through shared memory) and
+//   zero-padded to the region's row length; all operands of a tree group are
+//   written together, each source block read once per tile.
 //
 // leaf_prep_kernel<BN>: persistent (one CTA per SM); each CTA computes 128 x BN
 //   output tiles of the leaf products in turn, straight from the region:
@@ -50,7 +50,6 @@ namespace {
 constexpr int kStageK = 32;
 constexpr unsigned kSuspendNs = 1000000;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
-constexpr int kPrepTile = 64;   // prepare tile: 64 rows x 64 k, 256 threads
 
 template <int BN>
 struct Cfg {
@@ -237,9 +236,7 @@ struct Ring {
 
 }  // namespace
 
-// ---- prepare pass ---------------------------------------------------------
-// One CTA (256 threads) writes a 64-row x 64-k tile of one prepared operand;
-// thread t covers rows t/16 + 16i (i < 4) and k values 4(t%16) .. +3.
+// ---- prepare pass (tree groups) ---------------------------------------------
 __device__ __forceinline__ float4 load4(const float* p) {
   return *reinterpret_cast<const float4*>(p);
 }
@@ -252,116 +249,143 @@ __device__ __forceinline__ float4 lo4(float4 v, float4 h) {
                      tf32_rn(v.w - h.w));
 }
 
-// ---- prepare groups ---------------------------------------------------------
-// One CTA (256 threads) writes a 64-row x 64-k tile of every operand of a
-// group: each thread loads its 4 rows x 4 k of every input block once, then
-// evaluates each output's signed sum in the prologue's order, splits it into
-// TF32 hi/lo and stores both (left operands through a shared-memory
-// transpose, one output at a time).
-__device__ __forceinline__ float4 group_eval(const signed char (&e)[kMaxOperandTerms],
-                                             const float4 (&x)[kMaxPrepGroupIn]) {
-  auto pick = [&](int code) {
-    const int u = (code > 0 ? code : -code) - 1;
-    float4 r = x[0];
-#pragma unroll
-    for (int i = 1; i < kMaxPrepGroupIn; ++i)
-      if (u == i) r = x[i];
-    return r;
-  };
-  float4 v = pick(e[0]);
-  if (e[0] < 0) v = make_float4(-v.x, -v.y, -v.z, -v.w);
-#pragma unroll
-  for (int t = 1; t < kMaxOperandTerms; ++t) {
-    if (e[t] == 0) break;
-    const float4 y = pick(e[t]);
-    const float c = e[t] > 0 ? 1.f : -1.f;
-    v = make_float4(fmaf(c, y.x, v.x), fmaf(c, y.y, v.y), fmaf(c, y.z, v.z), fmaf(c, y.w, v.w));
-  }
-  return v;
+// Signed sum in FP32: the first term with its sign (exact), then fmaf with
+// +-1 per further term -- the rounding of the materialisation pass and of the
+// fused prologue.
+__device__ __forceinline__ float4 signed_add(float4 acc, float4 v, int code, bool first) {
+  const float c = code > 0 ? 1.f : -1.f;
+  if (first) return make_float4(c * v.x, c * v.y, c * v.z, c * v.w);
+  return make_float4(fmaf(c, v.x, acc.x), fmaf(c, v.y, acc.y), fmaf(c, v.z, acc.z),
+                     fmaf(c, v.w, acc.w));
 }
 
-// 4 consecutive elements starting at element a + b * ld of input u, those at
-// a + q >= lim read as zero (a + 3 < lim: one 16-byte load).
-__device__ __forceinline__ float4 group_load(const PrepGroup& G, int u, long long batch,
-                                             long long a, long long b, long long lim) {
-  const Term& T = G.in[u];
-  const float* p = T.p + batch * T.bstride + a + b * T.ld;
-  if (a + 3 < lim) return load4(p);
-  float e[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-    if (a + q < lim) e[q] = p[q];
-  return make_float4(e[0], e[1], e[2], e[3]);
-}
+// One CTA (256 threads) writes a 32-row x 32-k tile of every operand of a
+// tree group.  Thread t owns row 4 (t / 32) + (t % 32) / 8 of the tile and its
+// k values 4 (t % 8) .. +3, so a warp's store covers 4 rows x 128 contiguous
+// bytes.  Every input's tile is staged in shared memory as [k][row] (a 33-float
+// pitch: conflict-free both for a left operand's loads along the rows and for
+// the threads' reads along k); a right operand (k contiguous in its source)
+// is loaded along k.  Then, segment by segment, the thread evaluates the
+// segment's mids from the inputs (kept in shared memory, indexed by the
+// plan's codes), each output from the mids, splits it into TF32 hi/lo and
+// stores both.  Inputs past the block (rows or k) read as zero, so the
+// region's padding past an operand's k extent is written as zero.
+constexpr int kTreeTile = 32;
+constexpr int kTreePitch = kTreeTile + 1;
+constexpr int kTreeThreads = 256;
+constexpr int kTreeSmemBytes = kTreeIn * kTreeTile * kTreePitch * 4;
 
-__global__ void __launch_bounds__(256) prep_group_kernel(const __grid_constant__ PrepGroupPlan plan) {
-  __shared__ float tile[2][kPrepTile][kPrepTile + 1];   // [hi/lo][k][row] (transposed path)
+__global__ void __launch_bounds__(kTreeThreads, 2)
+    prep_tree_kernel(const __grid_constant__ PrepTreePlan plan) {
+  extern __shared__ float staged[];                   // [input][k][row], pitch kTreePitch
+  __shared__ float4 mids[kTreeMid][kTreeThreads];      // this thread's mids
   const long long item = blockIdx.x;
   int gi = 0;
   while (gi + 1 < plan.ngroups && plan.group[gi + 1].tile_begin <= item) ++gi;
-  const PrepGroup& G = plan.group[gi];
+  const TreeGroup& G = plan.group[gi];
   const long long local = item - G.tile_begin;
-  const int ktiles = plan.row_len / kPrepTile;
-  const int r0 = int(local / ktiles) * kPrepTile, k0 = int(local % ktiles) * kPrepTile;
+  const int ktiles = plan.row_len / kTreeTile;
+  const int r0 = int(local / ktiles) * kTreeTile, k0 = int(local % ktiles) * kTreeTile;
   const long long batch = blockIdx.y;
-  const int t4 = (threadIdx.x % 16) * 4, t16 = threadIdx.x / 16;
-  float* region = plan.region + batch * plan.region_bstride;
-  const long long ld = plan.row_len;
+  const int t = threadIdx.x;
+  const int row = 4 * (t / 32) + (t % 32) / 8, kc = 4 * (t % 8);
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  // Load every input's piece first (up to 16 loads in flight), then stage.
+  float4 v[kTreeIn];
   if (G.transpose) {
-    // Left operands: element (r, k) at p + r + k*ld; each thread holds rows
-    // r0 + t4 .. +3 of k columns k0 + t16 + 16i.
-    float4 x[4][kMaxPrepGroupIn];
+    // Left operand: element (r, k) at p + r + k * ld; rows 4 (t % 8) .. +3 of k
+    // column t / 8 of the tile.
+    const int rr = 4 * (t % 8), kk = t / 8;
+    const int r = r0 + rr, k = k0 + kk;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k = k0 + t16 + 16 * i, r = r0 + t4;
-#pragma unroll
-      for (int u = 0; u < kMaxPrepGroupIn; ++u)
-        x[i][u] = u < G.nin && k < G.cols && r < G.rows ? group_load(G, u, batch, r, k, G.rows)
-                                                         : zero;
+    for (int u = 0; u < kTreeIn; ++u) {
+      v[u] = zero;
+      if (u < G.nin && k < G.cols) {
+        const Term& T = G.in[u];
+        const float* p = T.p + batch * T.bstride + r + (long long)k * T.ld;
+        if (r + 3 < G.rows) {
+          v[u] = load4(p);
+        } else {
+          if (r + 0 < G.rows) v[u].x = p[0];
+          if (r + 1 < G.rows) v[u].y = p[1];
+          if (r + 2 < G.rows) v[u].z = p[2];
+        }
+      }
     }
-    for (int o = 0; o < G.nout; ++o) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int kk = t16 + 16 * i;
-        const float4 v = group_eval(G.expr[o], x[i]);
-        const float4 h = hi4(v), l = lo4(v, h);
-        tile[0][kk][t4 + 0] = h.x; tile[0][kk][t4 + 1] = h.y;
-        tile[0][kk][t4 + 2] = h.z; tile[0][kk][t4 + 3] = h.w;
-        tile[1][kk][t4 + 0] = l.x; tile[1][kk][t4 + 1] = l.y;
-        tile[1][kk][t4 + 2] = l.z; tile[1][kk][t4 + 3] = l.w;
+    for (int u = 0; u < kTreeIn; ++u) {
+      if (u < G.nin) {
+        float* s = staged + (u * kTreeTile + kk) * kTreePitch + rr;
+        s[0] = v[u].x;
+        s[1] = v[u].y;
+        s[2] = v[u].z;
+        s[3] = v[u].w;
       }
-      __syncthreads();
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int rr = t16 + 16 * i, r = r0 + rr;
-        if (r >= G.rows) continue;
-        const float4 h = make_float4(tile[0][t4][rr], tile[0][t4 + 1][rr], tile[0][t4 + 2][rr],
-                                     tile[0][t4 + 3][rr]);
-        const float4 l = make_float4(tile[1][t4][rr], tile[1][t4 + 1][rr], tile[1][t4 + 2][rr],
-                                     tile[1][t4 + 3][rr]);
-        *reinterpret_cast<float4*>(region + (long long)(G.out_hi[o] + r) * ld + k0 + t4) = h;
-        *reinterpret_cast<float4*>(region + (long long)(G.out_hi[o] + G.rows + r) * ld + k0 + t4) = l;
-      }
-      __syncthreads();   // the next output reuses the tile
     }
   } else {
-    // Right operands: element (k, n) at p + k + n*ld; read and write along k.
+    // Right operand: element (k, r) at p + k + r * ld; k values kc .. +3 of row
+    // `row` of the tile.
+    const int r = r0 + row, k = k0 + kc;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = r0 + t16 + 16 * i, k = k0 + t4;
-      if (r >= G.rows) continue;
-      float4 x[kMaxPrepGroupIn];
-#pragma unroll
-      for (int u = 0; u < kMaxPrepGroupIn; ++u)
-        x[u] = u < G.nin && k < G.cols ? group_load(G, u, batch, k, r, G.cols) : zero;
-      for (int o = 0; o < G.nout; ++o) {
-        const float4 v = group_eval(G.expr[o], x);
-        const float4 h = hi4(v);
-        *reinterpret_cast<float4*>(region + (long long)(G.out_hi[o] + r) * ld + k) = h;
-        *reinterpret_cast<float4*>(region + (long long)(G.out_hi[o] + G.rows + r) * ld + k) =
-            lo4(v, h);
+    for (int u = 0; u < kTreeIn; ++u) {
+      v[u] = zero;
+      if (u < G.nin && r < G.rows) {
+        const Term& T = G.in[u];
+        const float* p = T.p + batch * T.bstride + k + (long long)r * T.ld;
+        if (k + 3 < G.cols) {
+          v[u] = load4(p);
+        } else {
+          if (k + 0 < G.cols) v[u].x = p[0];
+          if (k + 1 < G.cols) v[u].y = p[1];
+          if (k + 2 < G.cols) v[u].z = p[2];
+        }
       }
+    }
+#pragma unroll
+    for (int u = 0; u < kTreeIn; ++u) {
+      if (u < G.nin) {
+        float* s = staged + (u * kTreeTile + kc) * kTreePitch + row;
+        s[0] = v[u].x;
+        s[kTreePitch] = v[u].y;
+        s[2 * kTreePitch] = v[u].z;
+        s[3 * kTreePitch] = v[u].w;
+      }
+    }
+  }
+  __syncthreads();
+  const int r = r0 + row;
+  if (r >= G.rows) return;
+  auto input = [&](int u) {
+    const float* s = staged + (u * kTreeTile + kc) * kTreePitch + row;
+    return make_float4(s[0], s[kTreePitch], s[2 * kTreePitch], s[3 * kTreePitch]);
+  };
+  float* region = plan.region + batch * plan.region_bstride;
+  const long long ld = plan.row_len;
+  for (int sg = 0; sg < G.nseg; ++sg) {
+    const TreeSeg& S = G.seg[sg];
+    for (int i = 0; i < S.nmid; ++i) {
+      float4 m = zero;
+#pragma unroll
+      for (int q = 0; q < kMaxOperandTerms; ++q) {
+        const int code = S.mid[i][q];
+        if (code == 0) break;
+        m = signed_add(m, input((code > 0 ? code : -code) - 1), code, q == 0);
+      }
+      mids[i][t] = m;
+    }
+    for (int o = 0; o < S.nout; ++o) {
+      float4 x = zero;
+#pragma unroll
+      for (int q = 0; q < kMaxOperandTerms; ++q) {
+        const int code = S.expr[o][q];
+        if (code == 0) break;
+        x = signed_add(x, mids[(code > 0 ? code : -code) - 1][t], code, q == 0);
+      }
+      const float4 h = hi4(x);
+      float* dst = region + (long long)(S.out_hi[o] + r) * ld + k0 + kc;
+      *reinterpret_cast<float4*>(dst) = h;
+      *reinterpret_cast<float4*>(dst + (long long)G.rows * ld) = lo4(x, h);
     }
   }
 }
@@ -984,11 +1008,15 @@ bool prep_supported() { return encode_fn() != nullptr; }
 
 bool prep_pair_supported() { return prep_supported() && pair_clusters() > 0; }
 
-int prep_row_align() { return kPrepTile; }   // a multiple of the 32-k stage
+int prep_row_align() { return 64; }   // a multiple of the 32-k stage and the 32-k prepare tile
 
-cudaError_t launch_prep_groups(const PrepGroupPlan& plan, int batch, cudaStream_t stream) {
+cudaError_t launch_prep_tree(const PrepTreePlan& plan, int batch, cudaStream_t stream) {
   if (plan.ngroups == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
-  prep_group_kernel<<<dim3(unsigned(plan.ntiles), batch), 256, 0, stream>>>(plan);
+  cudaError_t e = cudaFuncSetAttribute(prep_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kTreeSmemBytes);
+  if (e != cudaSuccess) return e;
+  prep_tree_kernel<<<dim3(unsigned(plan.ntiles), batch), kTreeThreads, kTreeSmemBytes, stream>>>(
+      plan);
   return cudaGetLastError();
 }
 

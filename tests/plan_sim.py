@@ -3,10 +3,15 @@
 This checks the C++ plan builder on CPU: every materialisation job and every
 leaf product of the plan is evaluated in FP32 with numpy, in plan order, on
 column-major buffers laid out exactly as the kernels would address them.
-Plans of the prepared (3xTF32) path also carry the prepare groups and, at
-depth >= 2, the deferred decode; both are executed as the kernels order them
-(prep_group_kernel: each output's terms in its own order, the first with its
-sign; decode_kernel: per target, old value plus the products in plan order).
+Plans of the prepared (3xTF32) path also carry the tree groups of the prepare
+pass and, at depth >= 2, the deferred decode; both are executed as the kernels
+order them (prep_tree_kernel: each mid's blocks, then each operand's mids, in
+their own order, the first term with its sign; decode_kernel: per target, old
+value plus the products in plan order).  Their deepest rounded operands are
+virtual (never written by the library): the simulator writes them into a
+fifth buffer from their definitions, like a materialisation job, so every
+leaf operand is evaluated twice -- from its terms and by the tree groups -- and
+the two must agree bit for bit.
 """
 
 from __future__ import annotations
@@ -14,7 +19,7 @@ from __future__ import annotations
 import numpy as np
 
 F32 = np.float32
-C_BUF, WS_BUF = 2, 3
+C_BUF, WS_BUF, VIRT_BUF = 2, 3, 4
 
 
 def _view(buf: np.ndarray, ref, rows: int, cols: int) -> np.ndarray:
@@ -36,22 +41,32 @@ def _signed_sum(xs, signs):
 
 
 def check_prep_groups(plan: dict) -> None:
-    """Structural rules of the prepare groups: every prepared operand sits in
-    exactly one group of its own shape, a group has at most 4 source blocks
-    and 8 outputs, each output's codes name its terms in order, and the
-    operands' hi/lo row ranges of the prepared region do not overlap."""
+    """Structural rules of the tree groups: every prepared operand sits in
+    exactly one segment of a group of its own shape; a group has at most 16
+    source blocks and 8 segments, a segment at most 4 mids and 8 operands;
+    each operand's codes name its mids in order and each mid's codes its
+    blocks in order; the operands' hi/lo row ranges of the prepared region do
+    not overlap."""
     prepared, groups = plan["prepared"], plan["prep_groups"]
     seen = []
     for g in groups:
-        assert 1 <= len(g["in"]) <= 4 and 1 <= len(g["ops"]) <= 8
-        assert len(g["expr"]) == len(g["ops"])
-        for j, codes in zip(g["ops"], g["expr"]):
-            op = prepared[j]
-            assert (op["rows"], op["cols"], op["transpose"]) == (g["rows"], g["cols"], g["transpose"])
-            assert len(codes) == len(op["terms"])
-            for code, (ref, coef) in zip(codes, op["terms"]):
-                assert g["in"][abs(code) - 1] == ref and (1 if code > 0 else -1) == coef
-            seen.append(j)
+        assert 1 <= len(g["in"]) <= 16 and 1 <= len(g["segs"]) <= 8
+        assert all(r[0] in (0, 1, 2, WS_BUF) for r in g["in"]), "a group reads a virtual block"
+        for sg in g["segs"]:
+            assert 1 <= len(sg["mids"]) <= 4 and 1 <= len(sg["ops"]) <= 8
+            assert len(sg["expr"]) == len(sg["ops"])
+            for j, codes in zip(sg["ops"], sg["expr"]):
+                op = prepared[j]
+                assert (op["rows"], op["cols"], op["transpose"]) == (g["rows"], g["cols"],
+                                                                     g["transpose"])
+                assert len(codes) == len(op["terms"])
+                for code, (mid_terms, coef) in zip(codes, op["terms"]):
+                    assert (1 if code > 0 else -1) == coef
+                    mid = sg["mids"][abs(code) - 1]
+                    assert len(mid) == len(mid_terms)
+                    for mc, (ref, c) in zip(mid, mid_terms):
+                        assert g["in"][abs(mc) - 1] == ref and (1 if mc > 0 else -1) == c
+                seen.append(j)
     assert sorted(seen) == list(range(len(prepared)))
     spans = sorted((op["hi_row"], op["hi_row"] + 2 * op["rows"]) for op in prepared)
     for (_, end), (begin, _) in zip(spans, spans[1:]):
@@ -61,9 +76,9 @@ def check_prep_groups(plan: dict) -> None:
 
 
 def _write_prepared(plan: dict, bufs) -> None:
-    """Evaluate every prepare group and store its operands in the prepared
-    region of the workspace as the kernels lay it out: operand j occupies
-    region rows [hi_row, hi_row + 2 * rows) (hi rows, then lo rows) of
+    """Evaluate every tree group and store its operands in the prepared region
+    of the workspace as the kernels lay it out: operand j occupies region rows
+    [hi_row, hi_row + 2 * rows) (hi rows, then lo rows) of
     ``prepared_row_len`` k values each, zero past its k extent.  Here the hi
     rows hold the FP32 value and the lo rows zero (the TF32 split itself is
     the GPU tests' business).  All groups of a launch read their sources
@@ -74,9 +89,12 @@ def _write_prepared(plan: dict, bufs) -> None:
         # (transposed into k-contiguous rows) is rows x cols, a right one cols x rows.
         shape = (g["rows"], g["cols"]) if g["transpose"] else (g["cols"], g["rows"])
         ins = [_view(bufs[r[0]], r, *shape).copy() for r in g["in"]]
-        for j, codes in zip(g["ops"], g["expr"]):
-            values[j] = _signed_sum([ins[abs(c) - 1] for c in codes],
-                                    [1 if c > 0 else -1 for c in codes])
+        for sg in g["segs"]:
+            mids = [_signed_sum([ins[abs(c) - 1] for c in m], [1 if c > 0 else -1 for c in m])
+                    for m in sg["mids"]]
+            for j, codes in zip(sg["ops"], sg["expr"]):
+                values[j] = _signed_sum([mids[abs(c) - 1] for c in codes],
+                                        [1 if c > 0 else -1 for c in codes])
     region = _prepared_region(plan, bufs)
     for j, op in enumerate(plan["prepared"]):
         rows_k = values[j] if op["transpose"] else values[j].T   # rows x k
@@ -112,8 +130,11 @@ def run_plan(plan: dict, a: np.ndarray, b: np.ndarray, c: np.ndarray,
             _view(buf, (0, 0, ld), rows, cols)[...] = x
         return buf
 
+    virt = plan.get("virtual", [])
+    vsize = max([v["out"][1] + (v["cols"] - 1) * v["out"][2] + v["rows"] for v in virt] + [1])
     bufs = [flat(a, m, k, lda), flat(b, k, n, ldb), flat(c, m, n, ldc),
-            np.full(max(plan["workspace_elements"], 1), np.nan, F32)]
+            np.full(max(plan["workspace_elements"], 1), np.nan, F32),
+            np.full(vsize, np.nan, F32)]
     for stage in plan["stages"]:
         for job in stage:
             rows, cols = job["rows"], job["cols"]
@@ -124,7 +145,17 @@ def run_plan(plan: dict, a: np.ndarray, b: np.ndarray, c: np.ndarray,
                     x = ins[abs(code) - 1] * F32(1 if code > 0 else -1)
                     acc = x.astype(F32) if acc is None else (acc + x).astype(F32)
                 _view(bufs[out_ref[0]], out_ref, rows, cols)[...] = acc
+    # Virtual blocks: written here from their definitions (the library never
+    # writes them; its prepare pass evaluates them inside the tree groups).
+    for v in virt:
+        assert v["out"][0] == VIRT_BUF
+        rows, cols = v["rows"], v["cols"]
+        terms = [(_view(bufs[r[0]], r, rows, cols), coef) for r, coef in v["terms"]]
+        assert all(r[0] != VIRT_BUF for r, _ in v["terms"]), "virtual block of virtual blocks"
+        _view(bufs[VIRT_BUF], v["out"], rows, cols)[...] = _signed_sum(
+            [x for x, _ in terms], [cf for _, cf in terms])
     prepared = bool(plan.get("prepared"))
+    assert prepared or not virt, "virtual blocks outside the prepared path"
     if prepared:
         check_prep_groups(plan)
         _write_prepared(plan, bufs)

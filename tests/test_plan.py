@@ -160,10 +160,14 @@ def test_prepared_plan_computes_gemm(built_lib, m, k, n, depth, basis, deferred)
 
 
 def test_prepare_groups_share_source_blocks(built_lib):
-    """At depth 2 the 98 prepared operands (49 left, 49 right) fold into 14
-    groups: the seven inner-level operands of one outer operand are sums of
-    its four quadrants, so each group reads 4 source blocks once -- 56 block
-    reads instead of the operands' 196 term reads."""
+    """At depth 2 the 98 prepared operands (49 left, 49 right) fold into one
+    tree group per side: the 16 sub-blocks of A's (B's) quadrants are read
+    once per tile, each outer product is a segment whose 4 mids are the
+    sub-blocks of its outer operand -- the operand the reference rounds
+    before splitting (prepare_child), evaluated in the same order and never
+    written to memory -- and its 7 inner operands are signed sums of those
+    mids.  There are no materialisation stages, and the workspace holds only
+    the prepared region and the deferred decode's product buffers."""
     import bag_b200 as bag
     bag.set_math_mode("3xtf32")
     try:
@@ -171,10 +175,17 @@ def test_prepare_groups_share_source_blocks(built_lib):
     finally:
         bag.set_math_mode("ffma")
     ops, groups = plan["prepared"], plan["prep_groups"]
-    assert len(ops) == 98
+    assert len(ops) == 98 and plan["stages"] == []
     assert sum(len(op["terms"]) for op in ops) == 196
-    assert len(groups) == 14 and all(len(g["ops"]) == 7 for g in groups)
-    assert sum(len(g["in"]) for g in groups) == 56
+    assert len(groups) == 2 and sorted(g["transpose"] for g in groups) == [False, True]
+    for g in groups:
+        assert len(g["in"]) == 16 and len(g["segs"]) == 7
+        assert all(len(sg["mids"]) == 4 and len(sg["ops"]) == 7 for sg in g["segs"])
+    # The four multi-term outer operands per side (M1, M2, M3, M6 / M7) stay virtual.
+    assert len(plan["virtual"]) == 8
+    region_rows = sum(2 * op["rows"] for op in ops)
+    decode = 49 * 32 * 32   # 49 product buffers of 32 x 32 (ld 32)
+    assert plan["workspace_elements"] <= region_rows * plan["prepared_row_len"] + decode + 64 * 50
 
 
 def test_ffma_plans_carry_no_prepared_operands(bag):
@@ -184,9 +195,9 @@ def test_ffma_plans_carry_no_prepared_operands(bag):
 
 
 def test_plan_sim_catches_a_corrupted_prepared_plan(built_lib):
-    """The checks above have teeth: a flipped sign in one prepare group, a
-    misrouted decode term, or a group output aimed at the wrong operand is
-    caught."""
+    """The checks above have teeth: a flipped sign in an operand's mids or in a
+    mid's blocks, two segment outputs swapped, a wrong virtual block or a
+    misrouted decode term is caught."""
     import copy
 
     import bag_b200 as bag
@@ -205,14 +216,26 @@ def test_plan_sim_catches_a_corrupted_prepared_plan(built_lib):
     assert O.rel_frobenius(run_plan(plan, a, b, c, m, k, m), ref) < 1e-5
 
     bad = copy.deepcopy(plan)
-    code = bad["prep_groups"][3]["expr"][2]
+    code = bad["prep_groups"][1]["segs"][3]["expr"][2]
     code[-1] = -code[-1]
     with pytest.raises(AssertionError):
         run_plan(bad, a, b, c, m, k, m)
 
     bad = copy.deepcopy(plan)
-    g = bad["prep_groups"][0]
-    g["ops"][0], g["ops"][1] = g["ops"][1], g["ops"][0]
+    mid = bad["prep_groups"][0]["segs"][2]["mids"][1]
+    mid[-1] = -mid[-1]
+    with pytest.raises(AssertionError):
+        run_plan(bad, a, b, c, m, k, m)
+
+    bad = copy.deepcopy(plan)
+    sg = bad["prep_groups"][0]["segs"][0]
+    sg["ops"][0], sg["ops"][1] = sg["ops"][1], sg["ops"][0]
+    with pytest.raises(AssertionError):
+        run_plan(bad, a, b, c, m, k, m)
+
+    bad = copy.deepcopy(plan)
+    term = bad["virtual"][2]["terms"][1]
+    term[1] = -term[1]
     with pytest.raises(AssertionError):
         run_plan(bad, a, b, c, m, k, m)
 
