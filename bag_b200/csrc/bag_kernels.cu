@@ -586,93 +586,6 @@ cudaError_t launch_leaf(const LeafPlan& plan, int config, bool vec, int batch, c
   }
 }
 
-// Deferred inverse transform.  A CTA (one warp per target) takes a
-// kDecodeRows-row slice of one column of the common m x n extent: it pulls
-// that slice of every product buffer -- and of every target when it
-// accumulates -- into shared memory with cp.async (about 65 KB in flight per
-// CTA, no registers held), then warp t adds its target's products in plan
-// order (lane l: rows 4l .. 4l+3 and 128+4l .. 128+4l+3, so each float4 read
-// of a warp is 512 contiguous bytes) and writes the slice once.
-constexpr int kDecodeRows = 256;
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
-                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
-               "l"(gmem), "r"(src_bytes)
-               : "memory");
-}
-
-__global__ void __launch_bounds__(kMaxDecodeTargets * 32) decode_kernel(
-    const __grid_constant__ DecodePlan plan) {
-  extern __shared__ __align__(16) float tile[];   // [np + nt][kDecodeRows]
-  const int slices = (plan.m + kDecodeRows - 1) / kDecodeRows;
-  const int col = int(blockIdx.x / slices), r0 = int(blockIdx.x % slices) * kDecodeRows;
-  const long long batch = blockIdx.y;
-  const int nin = plan.np + (plan.accumulate ? plan.nt : 0);
-  // Load: 16-byte pieces; rows past m are zero-filled (the source size of a
-  // piece counts only its rows below m, and is 0 past the end).
-  for (int q = threadIdx.x; q < nin * (kDecodeRows / 4); q += blockDim.x) {
-    const int j = q / (kDecodeRows / 4), r = r0 + (q % (kDecodeRows / 4)) * 4;
-    const Term& T = j < plan.np ? plan.in[j] : plan.out[j - plan.np];
-    const float* src = T.p + batch * T.bstride + (long long)col * T.ld + (r < plan.m ? r : 0);
-    const int bytes = r < plan.m ? 4 * min(4, plan.m - r) : 0;
-    cp_async16(tile + (long long)j * kDecodeRows + (r - r0), src, bytes);
-  }
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-  __syncthreads();
-  const int t = threadIdx.x / 32, lane = threadIdx.x % 32;
-  if (t >= plan.nt) return;
-  constexpr int kHalf = kDecodeRows / 2;
-  float acc[8];   // rows lane*4 + i (i < 4) and kHalf + lane*4 + (i - 4)
-  const float* own = tile + (long long)(plan.np + t) * kDecodeRows + lane * 4;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    acc[i] = plan.accumulate ? own[i] : 0.f;
-    acc[4 + i] = plan.accumulate ? own[kHalf + i] : 0.f;
-  }
-  for (int e = 0; e < plan.count[t]; ++e) {
-    const int code = plan.list[t][e];
-    const float* v = tile + (long long)((code > 0 ? code : -code) - 1) * kDecodeRows + lane * 4;
-    const float4 v0 = *reinterpret_cast<const float4*>(v);
-    const float4 v1 = *reinterpret_cast<const float4*>(v + kHalf);
-    const float s = code > 0 ? 1.f : -1.f;
-    acc[0] = fmaf(s, v0.x, acc[0]); acc[1] = fmaf(s, v0.y, acc[1]);
-    acc[2] = fmaf(s, v0.z, acc[2]); acc[3] = fmaf(s, v0.w, acc[3]);
-    acc[4] = fmaf(s, v1.x, acc[4]); acc[5] = fmaf(s, v1.y, acc[5]);
-    acc[6] = fmaf(s, v1.z, acc[6]); acc[7] = fmaf(s, v1.w, acc[7]);
-  }
-  const Term& T = plan.out[t];
-  float* column = const_cast<float*>(T.p) + batch * T.bstride + (long long)col * T.ld;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int r = r0 + h * kHalf + lane * 4;
-    float* dst = column + r;
-    const float* a = acc + 4 * h;
-    if (r + 3 < plan.m) {
-      *reinterpret_cast<float4*>(dst) = make_float4(a[0], a[1], a[2], a[3]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (r + i < plan.m) dst[i] = a[i];
-    }
-  }
-}
-
-cudaError_t launch_decode(const DecodePlan& plan, int batch, cudaStream_t stream) {
-  if (plan.np == 0 || plan.nt == 0 || plan.m == 0 || plan.n == 0 || batch == 0) return cudaSuccess;
-  const long long slices = (plan.m + kDecodeRows - 1) / kDecodeRows;
-  const long long blocks = slices * plan.n;
-  if (blocks > INT32_MAX) return cudaErrorInvalidValue;
-  const int nin = plan.np + (plan.accumulate ? plan.nt : 0);
-  const size_t smem = size_t(nin) * kDecodeRows * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(smem));
-  if (e != cudaSuccess) return e;
-  decode_kernel<<<dim3(unsigned(blocks), unsigned(batch)), kMaxDecodeTargets * 32, smem, stream>>>(
-      plan);
-  return cudaGetLastError();
-}
-
 cudaError_t launch_materialize(const MatPlan& plan, int batch, cudaStream_t stream, int sm_count) {
   if (plan.njobs == 0 || batch == 0) return cudaSuccess;
   const long long chunks = plan.chunk_begin[plan.njobs];

@@ -885,6 +885,86 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
   cluster_sync_all();
 }
 
+// ---- deferred inverse transform ---------------------------------------------
+// A CTA (one warp per target) takes a kDecodeRows-row slice of one column of
+// the common m x n extent.  Threads 0 .. nin-1 each bring that slice of one
+// product buffer (and, when accumulating, of one target) into shared memory
+// with one bulk copy (cp.async.bulk, completing on the CTA's mbarrier; a
+// slice is contiguous in the column-major blocks and a multiple of 16 bytes),
+// so staging costs a handful of instructions per CTA.  Then warp t adds its
+// target's products in plan order (lane l: rows 4l .. 4l+3 and 128+4l ..
+// 128+4l+3, so each float4 access of a warp covers 512 contiguous bytes) and
+// writes the slice once.  The wait is bounded like every wait here.
+constexpr int kDecodeRows = 256;
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, int bytes,
+                                          unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kMaxDecodeTargets * 32) decode_kernel(
+    const __grid_constant__ DecodePlan plan) {
+  extern __shared__ __align__(128) float slice[];   // [np + nt][kDecodeRows]
+  __shared__ unsigned long long bar;
+  __shared__ int abort;
+  const int slices = (plan.m + kDecodeRows - 1) / kDecodeRows;
+  const int col = int(blockIdx.x / slices), r0 = int(blockIdx.x % slices) * kDecodeRows;
+  const long long batch = blockIdx.y;
+  const int nin = plan.np + (plan.accumulate ? plan.nt : 0);
+  const int rows = min(kDecodeRows, plan.m - r0);   // a multiple of 4 (m % 4 == 0)
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_expect_tx(&bar, nin * rows * 4);
+  if (threadIdx.x < nin) {
+    const int j = threadIdx.x;
+    const Term& T = j < plan.np ? plan.in[j] : plan.out[j - plan.np];
+    bulk_load(slice + j * kDecodeRows, T.p + batch * T.bstride + (long long)col * T.ld + r0,
+              rows * 4, &bar);
+  }
+  if (!mbar_wait(abort, &bar, 0)) {
+    if (threadIdx.x < nin) mbar_drain(&bar, 0);   // no copy outlives the CTA
+    return;
+  }
+  const int t = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (t >= plan.nt) return;
+  constexpr int kHalf = kDecodeRows / 2;
+  float acc[8];   // rows lane*4 + i (i < 4) and kHalf + lane*4 + (i - 4)
+  const float* own = slice + (plan.np + t) * kDecodeRows + lane * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    acc[i] = plan.accumulate ? own[i] : 0.f;
+    acc[4 + i] = plan.accumulate ? own[kHalf + i] : 0.f;
+  }
+  for (int e = 0; e < plan.count[t]; ++e) {
+    const int code = plan.list[t][e];
+    const float* v = slice + ((code > 0 ? code : -code) - 1) * kDecodeRows + lane * 4;
+    const float4 v0 = *reinterpret_cast<const float4*>(v);
+    const float4 v1 = *reinterpret_cast<const float4*>(v + kHalf);
+    const float s = code > 0 ? 1.f : -1.f;
+    acc[0] = fmaf(s, v0.x, acc[0]); acc[1] = fmaf(s, v0.y, acc[1]);
+    acc[2] = fmaf(s, v0.z, acc[2]); acc[3] = fmaf(s, v0.w, acc[3]);
+    acc[4] = fmaf(s, v1.x, acc[4]); acc[5] = fmaf(s, v1.y, acc[5]);
+    acc[6] = fmaf(s, v1.z, acc[6]); acc[7] = fmaf(s, v1.w, acc[7]);
+  }
+  const Term& T = plan.out[t];
+  float* column = const_cast<float*>(T.p) + batch * T.bstride + (long long)col * T.ld + r0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = h * kHalf + lane * 4;
+    if (r < rows)
+      *reinterpret_cast<float4*>(column + r) =
+          make_float4(acc[4 * h], acc[4 * h + 1], acc[4 * h + 2], acc[4 * h + 3]);
+  }
+}
+
 // Self-test of the bounded wait the leaf kernels use: thread 0 waits on an
 // mbarrier that nothing arrives on, with a short limit; the wait must give
 // up, set this file's device error word and the CTA's abort flag, and the
@@ -1033,6 +1113,22 @@ cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* re
     return cudaErrorInvalidValue;
   return kind == kPrepLeafPair ? launch_pair(plan, maps, batch, stream)
                                : launch_bn<256>(plan, maps, batch, stream);
+}
+
+cudaError_t launch_decode(const DecodePlan& plan, int batch, cudaStream_t stream) {
+  if (plan.np == 0 || plan.nt == 0 || plan.m == 0 || plan.n == 0 || batch == 0) return cudaSuccess;
+  if (plan.m % 4) return cudaErrorInvalidValue;   // bulk copies move 16-byte multiples
+  const long long slices = (plan.m + kDecodeRows - 1) / kDecodeRows;
+  const long long blocks = slices * plan.n;
+  if (blocks > INT32_MAX) return cudaErrorInvalidValue;
+  const int nin = plan.np + (plan.accumulate ? plan.nt : 0);
+  const size_t smem = size_t(nin) * kDecodeRows * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(smem));
+  if (e != cudaSuccess) return e;
+  decode_kernel<<<dim3(unsigned(blocks), unsigned(batch)), kMaxDecodeTargets * 32, smem, stream>>>(
+      plan);
+  return cudaGetLastError();
 }
 
 cudaError_t run_wait_selftest(unsigned long long limit_ns, int* gave_up_device,

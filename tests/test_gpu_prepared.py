@@ -14,7 +14,6 @@ the prepared operands must not change when the prepare pass is restructured.
 from __future__ import annotations
 
 import ctypes
-import os
 
 import numpy as np
 import pytest
@@ -74,12 +73,15 @@ def test_prepared_region_is_bit_exact(bag, cuda, m, k, n, depth, basis):
     row_len = plan["prepared_row_len"]
     nrows = max(op["hi_row"] + 2 * op["rows"] for op in plan["prepared"])
     off = plan["prepared_region"][1]
-    region = np.empty((nrows, row_len), np.float32)
-    base = bag.lib().bag_workspace_data(ws.handle)
-    st = _cudart().cudaMemcpy(ctypes.c_void_p(region.ctypes.data),
-                              ctypes.c_void_p(base + 4 * off), ctypes.c_size_t(region.nbytes), 2)
+    # The whole workspace: at depth >= 3 mids read blocks rounded there first.
+    wsbuf = np.empty(plan["workspace_elements"], np.float32)
+    st = _cudart().cudaMemcpy(ctypes.c_void_p(wsbuf.ctypes.data),
+                              ctypes.c_void_p(bag.lib().bag_workspace_data(ws.handle)),
+                              ctypes.c_size_t(wsbuf.nbytes), 2)
     assert st == 0
-    bufs = [np.asfortranarray(a).ravel(order="F"), np.asfortranarray(b).ravel(order="F")]
+    region = wsbuf[off:off + nrows * row_len].reshape(nrows, row_len)
+    bufs = [np.asfortranarray(a).ravel(order="F"), np.asfortranarray(b).ravel(order="F"), None,
+            wsbuf]
     bad = []
     for j, op in enumerate(plan["prepared"]):
         shape = (op["rows"], op["cols"]) if op["transpose"] else (op["cols"], op["rows"])
