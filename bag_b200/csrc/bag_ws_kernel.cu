@@ -4,9 +4,12 @@
 // aligned (the fast signatures of bag_plan.h).  Each CTA of 384 threads owns a
 // 128 x 128 output tile of one product:
 //
-//  * 4 producer warps load the next k-tiles of every signed operand term with
-//    128-bit loads two tiles ahead, sum the terms in the reference's order
-//    (x + delta*y, bag.cuh:69-73), and store the transformed A tile (k-major)
+//  * 4 producer warps copy the raw k-tiles of every signed operand term
+//    several tiles ahead into a shared-memory ring with 16-byte cp.async (each
+//    thread its own chunks, so no barrier between producers; the prefetch
+//    distance is the ring depth, 5-7 tiles, not registers), then sum the
+//    terms in the reference's order (x + delta*y, bag.cuh:69-73), and store
+//    the transformed A tile (k-major)
 //    and B tile (in its natural K-contiguous layout, 16-byte chunks
 //    XOR-swizzled so both the stores and the consumers' column reads hit 32
 //    distinct banks) into a 4-stage shared-memory ring, then arrive on the
@@ -17,10 +20,10 @@
 //    sequential fmaf chain over k), arrive on the stage's "empty" mbarrier,
 //    and finally add coef*M into every target C block (128-bit red.global).
 //
-// Every mbarrier wait sleeps in try_wait (suspend-time hint) rather than
-// spinning, and is bounded: after kWaitLimitNs of wall time the thread sets
+// Every mbarrier wait polls try_wait (which waits in hardware for a short
+// system-defined time per call) and is bounded: after kWaitLimitNs of wall time the thread sets
 // g_device_error and leaves its loop, so a logic error cannot hang the GPU;
-// nothing is left in flight (producers use plain loads).
+// a producer that gives up first waits for its own copies in flight.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -35,7 +38,9 @@ namespace {
 
 constexpr int kBM = 128, kBN = 128, kBK = 8, kStages = 4;
 constexpr int kConsumers = 256, kProducers = 128, kThreads = kConsumers + kProducers;
-constexpr unsigned kSuspendNs = 1000000;                  // try_wait sleep hint (1 ms)
+// Raw operand ring of the producers (dynamic shared memory): per tile and
+// producer thread 2 float4 chunks per operand term.
+constexpr int kRawBytes = 144 * 1024;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull; // give up after 2 s
 
 struct WsSmem {
@@ -44,6 +49,10 @@ struct WsSmem {
   unsigned long long full[kStages];
   unsigned long long empty[kStages];
 };
+
+constexpr int kWsSmemBytes = (int(sizeof(WsSmem)) + 127) / 128 * 128;
+constexpr int kWsDynBytes = kWsSmemBytes + kRawBytes;
+static_assert(kWsDynBytes <= 227 * 1024, "shared memory per CTA");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -58,18 +67,18 @@ __device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// One try_wait; the thread may sleep up to `suspend_ns` for the phase to
-// complete, so a waiting warp does not spin on the issue slots of the
-// computing warps.
-__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity,
-                                              unsigned suspend_ns) {
+// One try_wait with the hardware's own (short) time limit.  A suspend-time
+// hint here compiled to sleeps whose wake-up came well after the stage was
+// ready: measured on B200, 3.4 sleeps per warp per k-tile and the FMA pipe
+// idle a third of the time.
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return done != 0;
 }
@@ -83,9 +92,9 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // Bounded wait for the phase of parity `parity`: gives up (error word set,
 // false) when the phase has not completed after kWaitLimitNs of wall time.
 __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity) {
-  if (mbar_try_wait(bar, parity, kSuspendNs)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_ns();
-  while (!mbar_try_wait(bar, parity, kSuspendNs)) {
+  while (!mbar_try_wait(bar, parity)) {
     if (global_ns() - start > kWaitLimitNs) {
       atomicOr(&g_device_error, 1u);
       return false;
@@ -113,11 +122,39 @@ __device__ __forceinline__ float4 signed_first(float4 v, float coef) {
   return coef < 0.f ? make_float4(-v.x, -v.y, -v.z, -v.w) : v;
 }
 
-// Producer: 128 threads.  Thread p stages A vectors (rows a_m..a_m+3 of
-// columns a_k and a_k+4) and B vectors (k-chunk b_kc of columns b_n and b_n+64).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Raw ring geometry for a signature: slots of 2 (NL + NR) float4 per
+// producer thread; the prefetch distance is one less than the slot count.
+template <int NL, int NR>
+struct RawRing {
+  static constexpr int kChunks = 2 * (NL + NR);
+  static constexpr int kSlotBytes = kChunks * kProducers * 16;
+  static constexpr int kSlots = (kRawBytes / kSlotBytes) < 8 ? (kRawBytes / kSlotBytes) : 8;
+  static constexpr int kAhead = kSlots - 1;
+  static_assert(kSlots >= 3, "raw ring too shallow");
+};
+
+// Producer: 128 threads.  Thread p copies A chunks (rows a_m..a_m+3 of
+// columns a_k and a_k+4) and B chunks (k-chunk b_kc of columns b_n and
+// b_n+64) of every term into its own slots of the raw ring, kAhead tiles
+// ahead, and later sums them into the stage ring.
 template <int NL, int NR>
 __device__ __forceinline__ void produce(const LeafPlan& plan, const Prod& P, int m0, int n0,
-                                        long long batch, WsSmem& sm, int p, int ktiles) {
+                                        long long batch, WsSmem& sm, float4* raw, int p,
+                                        int ktiles) {
+  using R = RawRing<NL, NR>;
   const int a_m = (p % 32) * 4, a_k = p / 32;
   const int b_n = p / 2, b_kc = p % 2;
   const long long lda = plan.terms[P.l0].ld, ldb = plan.terms[P.r0].ld;
@@ -138,115 +175,149 @@ __device__ __forceinline__ void produce(const LeafPlan& plan, const Prod& P, int
     cb[t] = T.coef;
   }
   // Clamped addresses: rows >= m and columns >= n are loaded but never stored.
-  long long oa = min(m0 + a_m, P.m - 4) + (long long)a_k * lda;
-  long long ob0 = b_kc * 4 + (long long)min(n0 + b_n, P.n - 1) * ldb;
-  long long ob1 = b_kc * 4 + (long long)min(n0 + b_n + 64, P.n - 1) * ldb;
-  const int kfull = P.k / kBK;
+  const long long oa = min(m0 + a_m, P.m - 4) + (long long)a_k * lda;
+  const long long ob0 = b_kc * 4 + (long long)min(n0 + b_n, P.n - 1) * ldb;
+  const long long ob1 = b_kc * 4 + (long long)min(n0 + b_n + 64, P.n - 1) * ldb;
 
-  float4 la[2][NL][2], lb[2][NR][2];
-  auto load = [&](float4 (&xa)[NL][2], float4 (&xb)[NR][2], int kt) {
-    if (kt < kfull) {
+  // Copy tile kt's chunks of this thread into slot kt % kSlots; chunks past k
+  // are zero-filled (k % 4 == 0 here), their source clamped to the tile start.
+  auto issue = [&](int kt) {
+    float4* slot = raw + (kt % R::kSlots) * R::kChunks * kProducers + p;
+    const int k0 = kt * kBK;
+    const bool a0 = k0 + a_k < P.k, a1 = k0 + a_k + 4 < P.k, bk = k0 + b_kc * 4 < P.k;
+    const long long oak0 = a0 ? oa + (long long)k0 * lda : oa;
+    const long long oak1 = a1 ? oa + (long long)(k0 + 4) * lda : oa;
+    const long long ok0 = bk ? ob0 + k0 : ob0, ok1 = bk ? ob1 + k0 : ob1;
 #pragma unroll
-      for (int t = 0; t < NL; ++t) {
-        xa[t][0] = ldg4(ba[t] + oa);
-        xa[t][1] = ldg4(ba[t] + oa + 4 * lda);
-      }
-#pragma unroll
-      for (int t = 0; t < NR; ++t) {
-        xb[t][0] = ldg4(bb[t] + ob0);
-        xb[t][1] = ldg4(bb[t] + ob1);
-      }
-    } else {   // the last, partial k-tile: zero beyond k (k % 4 == 0 here)
-      const int k0 = kt * kBK;
-      const bool a0 = k0 + a_k < P.k, a1 = k0 + a_k + 4 < P.k, bk = k0 + b_kc * 4 < P.k;
-      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int t = 0; t < NL; ++t) {
-        xa[t][0] = a0 ? ldg4(ba[t] + oa) : z;
-        xa[t][1] = a1 ? ldg4(ba[t] + oa + 4 * lda) : z;
-      }
-#pragma unroll
-      for (int t = 0; t < NR; ++t) {
-        xb[t][0] = bk ? ldg4(bb[t] + ob0) : z;
-        xb[t][1] = bk ? ldg4(bb[t] + ob1) : z;
-      }
+    for (int t = 0; t < NL; ++t) {
+      cp_async16(slot + (2 * t) * kProducers, ba[t] + oak0, a0 ? 16 : 0);
+      cp_async16(slot + (2 * t + 1) * kProducers, ba[t] + oak1, a1 ? 16 : 0);
     }
-    oa += kBK * lda;
-    ob0 += kBK;
-    ob1 += kBK;
+#pragma unroll
+    for (int t = 0; t < NR; ++t) {
+      cp_async16(slot + (2 * (NL + t)) * kProducers, bb[t] + ok0, bk ? 16 : 0);
+      cp_async16(slot + (2 * (NL + t) + 1) * kProducers, bb[t] + ok1, bk ? 16 : 0);
+    }
   };
-  auto store = [&](const float4 (&xa)[NL][2], const float4 (&xb)[NR][2], int s) {
+  // Sum slot kt's terms and store the transformed tiles into stage s.
+  auto store = [&](int kt, int s) {
+    const float4* slot = raw + (kt % R::kSlots) * R::kChunks * kProducers + p;
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
-      float4 v = signed_first(xa[0][q], ca[0]);
+      float4 v = signed_first(slot[q * kProducers], ca[0]);
 #pragma unroll
-      for (int t = 1; t < NL; ++t) v = add_signed(v, xa[t][q], ca[t]);
+      for (int t = 1; t < NL; ++t) v = add_signed(v, slot[(2 * t + q) * kProducers], ca[t]);
       *reinterpret_cast<float4*>(&sm.a[s][a_k + 4 * q][a_m]) = v;
     }
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
-      float4 v = signed_first(xb[0][q], cb[0]);
+      float4 v = signed_first(slot[(2 * NL + q) * kProducers], cb[0]);
 #pragma unroll
-      for (int t = 1; t < NR; ++t) v = add_signed(v, xb[t][q], cb[t]);
+      for (int t = 1; t < NR; ++t) v = add_signed(v, slot[(2 * (NL + t) + q) * kProducers], cb[t]);
       const int n = b_n + 64 * q;
       *reinterpret_cast<float4*>(&sm.b[s][n][(b_kc ^ ((n >> 2) & 1)) * 4]) = v;
     }
   };
-  // Publish tile kt from register buffer x: wait until consumers released the
-  // stage's previous use, store, arrive.  False when a wait timed out.
-  auto publish = [&](const float4 (&xa)[NL][2], const float4 (&xb)[NR][2], int kt) {
-    const int s = kt % kStages;
-    if (kt >= kStages && !mbar_wait(&sm.empty[s], ((kt / kStages) - 1) & 1)) return false;
-    store(xa, xb, s);
-    mbar_arrive(&sm.full[s]);
-    return true;
-  };
 
-  if (ktiles > 0) load(la[0], lb[0], 0);
-  if (ktiles > 1) load(la[1], lb[1], 1);
-  for (int kt = 0; kt < ktiles; kt += 2) {
-    if (!publish(la[0], lb[0], kt)) return;
-    if (kt + 2 < ktiles) load(la[0], lb[0], kt + 2);
-    if (kt + 1 < ktiles) {
-      if (!publish(la[1], lb[1], kt + 1)) return;
-      if (kt + 3 < ktiles) load(la[1], lb[1], kt + 3);
-    }
+  // Every iteration commits one group (empty past the last tile), so
+  // wait_group kAhead always means "tile kt has landed".
+#pragma unroll
+  for (int d = 0; d < R::kAhead; ++d) {
+    if (d < ktiles) issue(d);
+    cp_async_commit();
   }
+  for (int kt = 0; kt < ktiles; ++kt) {
+    // Slot (kt + kAhead) % kSlots held tile kt - 1, already summed.
+    if (kt + R::kAhead < ktiles) issue(kt + R::kAhead);
+    cp_async_commit();
+    cp_async_wait<R::kAhead>();
+    const int s = kt % kStages;
+    if (kt >= kStages && !mbar_wait(&sm.empty[s], ((kt / kStages) - 1) & 1)) {
+      cp_async_wait<0>();   // no copy outlives the CTA
+      return;
+    }
+    store(kt, s);
+    mbar_arrive(&sm.full[s]);
+  }
+  cp_async_wait<0>();
 }
 
 // Consumer: 256 threads in 8 warps (4 along M x 2 along N).  Thread rows are
-// wm + lane_m*4 + {0..3, 16..19}; columns wn + lane_n + 8c, c = 0..7.
+// wm + lane_m*4 + {0..3, 16..19}; columns wn + lane_n + 8c, c = 0..7.  The
+// fragment loads are software-pipelined: while the FFMA2s of step k run, the
+// A fragment of step k+1 (and, at the end of a 4-k group, the B fragments of
+// the next group; at the end of a stage, the first fragments of the next
+// stage) are already in flight, so a warp never starts a step waiting on
+// shared memory -- the eight consumer warps leave each stage barrier
+// together, and without this their load stalls coincide.  Every output is
+// still one sequential fmaf chain over k.
+__device__ __forceinline__ void load_b(const WsSmem& sm, int s, int kq, int col, int swz,
+                                       float4 (&b)[8]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    b[c] = *reinterpret_cast<const float4*>(&sm.b[s][col + 8 * c][(kq ^ swz) * 4]);
+}
+
+__device__ __forceinline__ void load_a(const WsSmem& sm, int s, int k, int am, float4& a0,
+                                       float4& a1) {
+  a0 = *reinterpret_cast<const float4*>(&sm.a[s][k][am]);
+  a1 = *reinterpret_cast<const float4*>(&sm.a[s][k][am + 16]);
+}
+
+template <int KK>
+__device__ __forceinline__ void ffma_step(const float4 (&b)[8], float4 a0, float4 a1,
+                                          float2 (&acc)[4][8]) {
+  const float2 ap[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w),
+                        make_float2(a1.x, a1.y), make_float2(a1.z, a1.w)};
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const float bv = KK == 0 ? b[c].x : KK == 1 ? b[c].y : KK == 2 ? b[c].z : b[c].w;
+    const float2 b2 = make_float2(bv, bv);
+#pragma unroll
+    for (int ip = 0; ip < 4; ++ip) acc[ip][c] = __ffma2_rn(ap[ip], b2, acc[ip][c]);
+  }
+}
+
 __device__ __forceinline__ bool consume(WsSmem& sm, int ctid, int ktiles, float2 (&acc)[4][8]) {
+  static_assert(kBK == 8, "two 4-k groups per stage");
   const int warp = ctid >> 5, lane = ctid & 31;
   const int lane_m = lane >> 3, lane_n = lane & 7;
   const int wm = (warp & 3) * 32, wn = (warp >> 2) * 64;
-  const int am = wm + lane_m * 4;
+  const int am = wm + lane_m * 4, col = wn + lane_n;
   const int swz = (lane_n >> 2) & 1;   // bit 2 of every column this thread reads
+  if (ktiles <= 0) return true;
+  float4 b0[8], b1[8];   // the current and the next 4-k group's B fragments
+  float4 a0, a1, n0, n1;
+  if (!mbar_wait(&sm.full[0], 0)) return false;
+  load_b(sm, 0, 0, col, swz, b0);
+  load_a(sm, 0, 0, am, a0, a1);
   for (int kt = 0; kt < ktiles; ++kt) {
     const int s = kt % kStages;
-    if (!mbar_wait(&sm.full[s], (kt / kStages) & 1)) return false;
-#pragma unroll
-    for (int kq = 0; kq < kBK / 4; ++kq) {
-      float4 bf[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        bf[c] = *reinterpret_cast<const float4*>(&sm.b[s][wn + lane_n + 8 * c][(kq ^ swz) * 4]);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const int k = kq * 4 + kk;
-        const float4 a0 = *reinterpret_cast<const float4*>(&sm.a[s][k][am]);
-        const float4 a1 = *reinterpret_cast<const float4*>(&sm.a[s][k][am + 16]);
-        const float2 ap[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w),
-                              make_float2(a1.x, a1.y), make_float2(a1.z, a1.w)};
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float bv = kk == 0 ? bf[c].x : kk == 1 ? bf[c].y : kk == 2 ? bf[c].z : bf[c].w;
-          const float2 b2 = make_float2(bv, bv);
-#pragma unroll
-          for (int ip = 0; ip < 4; ++ip) acc[ip][c] = __ffma2_rn(ap[ip], b2, acc[ip][c]);
-        }
-      }
+    // Group 0 (k 0..3) on b0; its last step also fetches group 1's B.
+    load_a(sm, s, 1, am, n0, n1);
+    ffma_step<0>(b0, a0, a1, acc);
+    load_a(sm, s, 2, am, a0, a1);
+    ffma_step<1>(b0, n0, n1, acc);
+    load_a(sm, s, 3, am, n0, n1);
+    ffma_step<2>(b0, a0, a1, acc);
+    load_b(sm, s, 1, col, swz, b1);
+    load_a(sm, s, 4, am, a0, a1);
+    ffma_step<3>(b0, n0, n1, acc);
+    // Group 1 (k 4..7) on b1; its last step fetches the next stage's first
+    // fragments once that stage has landed.
+    load_a(sm, s, 5, am, n0, n1);
+    ffma_step<0>(b1, a0, a1, acc);
+    load_a(sm, s, 6, am, a0, a1);
+    ffma_step<1>(b1, n0, n1, acc);
+    load_a(sm, s, 7, am, n0, n1);
+    ffma_step<2>(b1, a0, a1, acc);
+    if (kt + 1 < ktiles) {
+      const int s1 = (kt + 1) % kStages;
+      if (!mbar_wait(&sm.full[s1], ((kt + 1) / kStages) & 1)) return false;
+      load_b(sm, s1, 0, col, swz, b0);
+      load_a(sm, s1, 0, am, a0, a1);
     }
+    ffma_step<3>(b1, n0, n1, acc);
     mbar_arrive(&sm.empty[s]);
   }
   return true;
@@ -300,7 +371,11 @@ __device__ __forceinline__ void store_outputs(const LeafPlan& plan, const Prod& 
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 1) leaf_ws_kernel(const __grid_constant__ LeafPlan plan) {
-  __shared__ __align__(16) WsSmem sm;
+  // Dynamic shared memory: the stage ring and barriers, then the producers'
+  // raw ring (kRawBytes).
+  extern __shared__ __align__(16) unsigned char dyn[];
+  WsSmem& sm = *reinterpret_cast<WsSmem*>(dyn);
+  float4* raw = reinterpret_cast<float4*>(dyn + kWsSmemBytes);
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
@@ -323,13 +398,13 @@ __global__ void __launch_bounds__(kThreads, 1) leaf_ws_kernel(const __grid_const
   if (threadIdx.x >= kConsumers) {
     const int p = threadIdx.x - kConsumers;
     switch (P.sig) {
-      case kSig11: produce<1, 1>(plan, P, m0, n0, batch, sm, p, ktiles); break;
-      case kSig12: produce<1, 2>(plan, P, m0, n0, batch, sm, p, ktiles); break;
-      case kSig21: produce<2, 1>(plan, P, m0, n0, batch, sm, p, ktiles); break;
-      case kSig22: produce<2, 2>(plan, P, m0, n0, batch, sm, p, ktiles); break;
-      case kSig33: produce<3, 3>(plan, P, m0, n0, batch, sm, p, ktiles); break;
-      case kSig41: produce<4, 1>(plan, P, m0, n0, batch, sm, p, ktiles); break;
-      case kSig14: produce<1, 4>(plan, P, m0, n0, batch, sm, p, ktiles); break;
+      case kSig11: produce<1, 1>(plan, P, m0, n0, batch, sm, raw, p, ktiles); break;
+      case kSig12: produce<1, 2>(plan, P, m0, n0, batch, sm, raw, p, ktiles); break;
+      case kSig21: produce<2, 1>(plan, P, m0, n0, batch, sm, raw, p, ktiles); break;
+      case kSig22: produce<2, 2>(plan, P, m0, n0, batch, sm, raw, p, ktiles); break;
+      case kSig33: produce<3, 3>(plan, P, m0, n0, batch, sm, raw, p, ktiles); break;
+      case kSig41: produce<4, 1>(plan, P, m0, n0, batch, sm, raw, p, ktiles); break;
+      case kSig14: produce<1, 4>(plan, P, m0, n0, batch, sm, raw, p, ktiles); break;
       default: atomicOr(&g_device_error, 2u); break;   // the host never sends these here
     }
     return;
@@ -348,7 +423,10 @@ TileShape ws_tile_shape() { return {kBM, kBN}; }
 
 cudaError_t launch_leaf_ws(const LeafPlan& plan, int batch, cudaStream_t stream) {
   if (plan.nprod == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
-  leaf_ws_kernel<<<dim3(plan.ntiles, batch), kThreads, 0, stream>>>(plan);
+  const cudaError_t e =
+      cudaFuncSetAttribute(leaf_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsDynBytes);
+  if (e != cudaSuccess) return e;
+  leaf_ws_kernel<<<dim3(plan.ntiles, batch), kThreads, kWsDynBytes, stream>>>(plan);
   return cudaGetLastError();
 }
 
