@@ -1046,15 +1046,20 @@ def run_bag(args) -> None:
                                "leaf_tc_cfg3_traffic.txt"),
             }
             kname, kfile = kernels.get(leaf_kernel, kernels["tf32_fused"])
+            # The leaf launches are timed inside a long step (a >= 1 s soak, then
+            # the timed steps), so the denominator is the sustained figure; the
+            # burst one is reported beside it.
             roofline = {"bound": "tensor", "kernel": kname,
-                        "achieved": leaf_tflops, "peak": tf32 / 3.0, "unit": "TFLOP/s",
-                        "frac": leaf_tflops / (tf32 / 3.0),
+                        "achieved": leaf_tflops, "peak": sustained / 3.0, "unit": "TFLOP/s",
+                        "frac": leaf_tflops / (sustained / 3.0),
                         "traffic": read_traffic(kfile),
                         "prepare_and_materialise_ms": ms - leaf_ms,
-                        "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst, of measured) / 2 "
+                        "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured; "
+                                       "the kernel runs inside a long power-capped step) / 2 "
                                        "(dense TF32 = half the bf16 rate) / 3 (three MMAs per "
                                        "leaf product: hi*hi, hi*lo, lo*hi)",
-                        "frac_of_sustained": leaf_tflops / (sustained / 3.0),
+                        "peak_burst": tf32 / 3.0,
+                        "frac_of_burst": leaf_tflops / (tf32 / 3.0),
                         "leaf_ms": leaf_ms, "algorithmic_flops_per_launch": f_exec}
         else:
             roofline = {"bound": "compute", "kernel": "leaf_ws_kernel / leaf_gemm_kernel "
