@@ -22,6 +22,7 @@ from __future__ import annotations
 import ctypes
 import json
 import os
+import warnings
 from typing import NamedTuple, Optional
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -360,7 +361,20 @@ def sgemm(a, b, c, *, beta: float = 1.0, depth: int = 1, basis="minimal",
     _check(lib().bag_sgemm_ex(LAYOUT[la[0]], m, n, k, a.data_ptr(), la[1], b.data_ptr(), lb[1],
                               c.data_ptr(), lc[1], float(beta), _depth(depth), _basis(basis),
                               _stream_handle(stream), ws))
+    _warn_if_fused(workspace)
     return c
+
+
+def _warn_if_fused(workspace) -> None:
+    """Warn (once per call site) when a 3xTF32 call ran the fused-transform
+    tensor kernel although a workspace was given: that workspace was created
+    in FFMA mode and lacks the prepared operands of the fast path."""
+    if workspace is not None and int(lib().bag_get_math_mode()) == MATH["3xtf32"] and \
+            int(lib().bag_last_leaf_kernel()) == 1:
+        warnings.warn("bag_b200: this 3xTF32 call ran the fused-transform tensor kernel because "
+                      "its workspace was created in FFMA mode; create the workspace after "
+                      "set_math_mode('3xtf32') (size: workspace_bytes_for(..., math='3xtf32')) "
+                      "for the prepared-operand kernel", RuntimeWarning, stacklevel=3)
 
 
 def multi_grid(ngpus: int) -> tuple[int, int]:
@@ -434,6 +448,7 @@ def sgemm_batched(a, b, c, *, beta: float = 1.0, depth: int = 1, basis="minimal"
     _check(lib().bag_sgemm_batched(LAYOUT["row"], m, n, k, a.data_ptr(), k, m * k, b.data_ptr(), n,
                                    k * n, c.data_ptr(), n, m * n, batch, float(beta), _depth(depth),
                                    _basis(basis), _stream_handle(stream), ws))
+    _warn_if_fused(workspace)
     return c
 
 

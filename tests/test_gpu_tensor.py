@@ -317,3 +317,31 @@ def test_phase_events_split_a_prepared_call(tensor_mode):
     assert spans[2] > 0 and spans[3] > 0     # leaves, then the deferred decode
     with pytest.raises((ValueError, bag.BagError)):
         bag.profile_phase_events(ev[1], None)
+
+
+def test_fused_fallback_warns_and_prepared_path_does_not(bag, cuda):
+    """A 3xTF32 call whose workspace was created in FFMA mode runs the fused
+    kernel and says so; one created in 3xTF32 mode runs the pair kernel quietly."""
+    import warnings
+
+    import torch
+    n, depth = 2048, 1
+    g = torch.Generator(device="cuda").manual_seed(17)
+    a = torch.randn(n, n, device="cuda", generator=g)
+    b = torch.randn(n, n, device="cuda", generator=g)
+    c = torch.empty(n, n, device="cuda")
+    ws_ffma = bag.Workspace.for_problem(n, n, n, depth)    # FFMA mode: no prepared region
+    bag.set_math_mode("3xtf32")
+    try:
+        with pytest.warns(RuntimeWarning, match="fused-transform"):
+            bag.sgemm(a, b, c, beta=0.0, depth=depth, workspace=ws_ffma)
+        assert bag.last_leaf_kernel() == "tf32_fused"
+        ws = bag.Workspace.for_problem(n, n, n, depth)
+        with warnings.catch_warnings():
+            warnings.simplefilter("error")
+            bag.sgemm(a, b, c, beta=0.0, depth=depth, workspace=ws)
+        assert bag.last_leaf_kernel() == "tf32_pair"
+        torch.cuda.synchronize()
+    finally:
+        bag.set_math_mode("ffma")
+    assert bag.device_error() == 0
