@@ -16,10 +16,10 @@
 //    of stages; warp 0 also owns TMEM.
 //  * warp 1, lane 0: per stage four K-steps of three tcgen05.mma.kind::tf32
 //    (A_hi*B_hi + A_hi*B_lo + A_lo*B_hi, both operands by shared-memory
-//    descriptor) into one TMEM chunk accumulator -- a stage is one 32-long
-//    accumulation chunk, since the tensor core accumulates with
+//    descriptor) into one TMEM chunk accumulator -- kChunkStages stages form
+//    one accumulation chunk, since the tensor core accumulates with
 //    round-toward-zero (Ootomo & Yokota 2022, sec. 4) -- then commits the
-//    stage free and the chunk done.
+//    stage free and, at a chunk's end, the chunk done.
 //  * warps 2.. (fold; BN/64 per TMEM lane quadrant, 64 columns each): add each
 //    finished chunk into 64 FP32 running sums in registers (round-to-nearest),
 //    then add coef*sum into every target C block (red.global, coalesced along
@@ -48,6 +48,16 @@ __device__ unsigned int g_tc3_device_error = 0;
 namespace {
 
 constexpr int kStageK = 32;
+// Stages accumulated in TMEM per chunk before the fold warps add the chunk
+// into their FP32 running sums: 2 x 32 k = 64 k.  Longer chunks mean fewer
+// TMEM reads, adds and hand-offs per product (the fold is energy the
+// power-capped leaf launch pays for), but the tensor core's round-toward-zero
+// accumulation runs over the whole chunk, and its bias does not cancel on
+// same-signed data.  Measured on B200 (interleaved runs, one box each): cfg3
+// 32 -> 64 k +3.5%, rel-F 1.76e-6 -> 1.66e-6; 64 -> 128 k another +2.6%, but
+// cfg5 (U[0,1), 1024-long leaves) then reached 1.12e-6 against its bound of
+// 1.25 x 6.76e-7, so 64 k it is.
+constexpr int kChunkStages = 2;
 constexpr unsigned kSuspendNs = 1000000;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
@@ -490,8 +500,11 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
       bool ok = true;
       for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
         const TileCoord tc = tile_of<BN>(plan, item);
-        for (int s = 0; s < tc.stages; ++s, r.next(C::kStages), rc.next(C::kChunkBufs)) {
-          if (chunks >= C::kChunkBufs && !mbar_wait(sb.abort, &sb.chunk_empty[rc.idx], rc.phase ^ 1u)) {
+        for (int s = 0; s < tc.stages; ++s, r.next(C::kStages)) {
+          const bool first = s % kChunkStages == 0;
+          const bool last = s % kChunkStages == kChunkStages - 1 || s == tc.stages - 1;
+          if (first && chunks >= C::kChunkBufs &&
+              !mbar_wait(sb.abort, &sb.chunk_empty[rc.idx], rc.phase ^ 1u)) {
             ok = false;
             break;
           }
@@ -508,13 +521,16 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
             const uint64_t a_lo = sw128_desc(st + C::kABytes + 32 * j);
             const uint64_t b_hi = sw128_desc(st + 2 * C::kABytes + 32 * j);
             const uint64_t b_lo = sw128_desc(st + 2 * C::kABytes + C::kBBytes + 32 * j);
-            mma_ss<BN>(d, a_hi, b_hi, j > 0);
+            mma_ss<BN>(d, a_hi, b_hi, j > 0 || !first);
             mma_ss<BN>(d, a_hi, b_lo, true);
             mma_ss<BN>(d, a_lo, b_hi, true);
           }
           mma_commit(&sb.empty[r.idx]);
-          mma_commit(&sb.chunk_full[rc.idx]);
-          ++chunks;
+          if (last) {
+            mma_commit(&sb.chunk_full[rc.idx]);
+            ++chunks;
+            rc.next(C::kChunkBufs);
+          }
         }
       }
       // All issued MMAs must finish before TMEM is released.
@@ -533,7 +549,8 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
       float total[64];
 #pragma unroll
       for (int i = 0; i < 64; ++i) total[i] = 0.f;
-      for (int c = 0; c < tc.stages; ++c, rc.next(C::kChunkBufs)) {
+      const int nchunks = (tc.stages + kChunkStages - 1) / kChunkStages;
+      for (int c = 0; c < nchunks; ++c, rc.next(C::kChunkBufs)) {
         const bool w = mbar_wait(sb.abort, &sb.chunk_full[rc.idx], rc.phase);
         if (!__all_sync(0xffffffffu, w)) {   // tcgen05.ld below is warp-collective
           ok = false;
@@ -596,10 +613,11 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
 //    even CTA sets for both.  Warp 0 also allocates the pair's TMEM.
 //  * warp 1, lane 0 of the even CTA: the MMA thread: it waits for the full
 //    barrier, issues the stage's twelve MMAs into one of two 256-column TMEM
-//    chunk accumulators (a 32-k stage is one accumulation chunk), then
-//    commits to the stage's empty and the chunk's full barrier in both CTAs.
+//    chunk accumulators (kChunkStages 32-k stages form one accumulation chunk),
+//    then commits to the stage's empty barrier, and at a chunk's end to the
+//    chunk's full barrier, in both CTAs.
 //  * warps 2-17 (fold): TMEM lane quadrant warp % 4, 64 columns each; add
-//    each finished 32-k chunk into 64 FP32 running sums (round-to-nearest),
+//    each finished chunk into 64 FP32 running sums (round-to-nearest),
 //    release it to the even CTA's chunk_empty barrier, and per tile add
 //    coef * sum into every target C block (red.global, coalesced along the
 //    column).
@@ -781,8 +799,10 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
       bool ok = true;
       for (int p = 0; p < nparts && ok; ++p) {
         const TileCoord tc = pair_tile_of(plan, cid + p * ncl);
-        for (int s = 0; s < tc.stages; ++s, r.next(kStages), rc.next(kChunks)) {
-          if (chunks >= kChunks &&
+        for (int s = 0; s < tc.stages; ++s, r.next(kStages)) {
+          const bool first = s % kChunkStages == 0;
+          const bool last = s % kChunkStages == kChunkStages - 1 || s == tc.stages - 1;
+          if (first && chunks >= kChunks &&
               !mbar_wait(sb.abort, &sb.chunk_empty[rc.idx], rc.phase ^ 1u)) {
             ok = false;
             break;
@@ -800,15 +820,18 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
             const uint64_t a_lo = sw128_desc(st + kABytes + 32 * j);
             const uint64_t b_hi = sw128_desc(st + 2 * kABytes + 32 * j);
             const uint64_t b_lo = sw128_desc(st + 2 * kABytes + kBBytes + 32 * j);
-            mma_pair(d, a_hi, b_hi, j > 0);
+            mma_pair(d, a_hi, b_hi, j > 0 || !first);
             mma_pair(d, a_hi, b_lo, true);
             mma_pair(d, a_lo, b_hi, true);
           }
           mma_commit_pair(peer_addr(&sb.empty[r.idx], 0));
           mma_commit_pair(peer_addr(&sb.empty[r.idx], 1));
-          mma_commit_pair(peer_addr(&sb.chunk_full[rc.idx], 0));
-          mma_commit_pair(peer_addr(&sb.chunk_full[rc.idx], 1));
-          ++chunks;
+          if (last) {
+            mma_commit_pair(peer_addr(&sb.chunk_full[rc.idx], 0));
+            mma_commit_pair(peer_addr(&sb.chunk_full[rc.idx], 1));
+            ++chunks;
+            rc.next(kChunks);
+          }
         }
       }
       // All issued MMAs (which write both CTAs' TMEM and read both CTAs'
@@ -830,7 +853,8 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
       float total[64];
 #pragma unroll
       for (int i = 0; i < 64; ++i) total[i] = 0.f;
-      for (int c = 0; c < tc.stages; ++c, rc.next(kChunks)) {
+      const int nchunks = (tc.stages + kChunkStages - 1) / kChunkStages;
+      for (int c = 0; c < nchunks; ++c, rc.next(kChunks)) {
         const bool w = mbar_wait(sb.abort, &sb.chunk_full[rc.idx], rc.phase);
         if (!__all_sync(0xffffffffu, w)) {   // tcgen05.ld below is warp-collective
           ok = false;

@@ -65,7 +65,7 @@ enum { BAG_LAYOUT_COL_MAJOR = 0, BAG_LAYOUT_ROW_MAJOR = 1 };
 enum { BAG_DEPTH_AUTO = -1 };
 /* Leaf arithmetic (bag_set_math_mode).  FFMA: every output a sequential fmaf
  * chain, the reference's SIMT numerics.  3XTF32: tcgen05 tensor cores on
- * hi/lo TF32 splits (hi*hi + hi*lo + lo*hi) with 32-long K chunks summed in
+ * hi/lo TF32 splits (hi*hi + hi*lo + lo*hi) with 32- or 64-long K chunks summed in
  * FP32 -- error below an FP32 FFMA dot product's for K >= 1024; used where
  * bag_last_leaf_path says, FFMA elsewhere. */
 enum { BAG_MATH_FFMA = 0, BAG_MATH_3XTF32 = 1 };

@@ -177,7 +177,7 @@ def test_prepared_path_batched_and_accumulating(tensor_mode):
 
 # The two prepared-operand leaf kernels: 256 x 256 tiles on a cluster of two
 # SMs (tcgen05.mma.cta_group::2, the default) and 128 x 256 tiles on one SM
-# (BAG_B200_PREP_KERNEL=single).  Same operands, same 32-k chunk folding:
+# (BAG_B200_PREP_KERNEL=single).  Same operands, same chunk folding:
 # both within the FFMA bound, and close to each other.  Shapes cover ragged
 # M/N (partial pair tiles), K tails that are not a multiple of the 32-k
 # stage, fewer tiles than clusters, and batches.
