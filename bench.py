@@ -1041,7 +1041,7 @@ def run_bag(args) -> None:
             tf32 = peaks.get("bf16_tflops", 1590.0) / 2.0
             sustained = peaks.get("bf16_tflops_sustained", 1400.0) / 2.0
             # The workspace was created in 3xTF32 mode, so the call runs the
-            # prepare pass (prep_group_kernel), the leaf kernel on the prepared
+            # prepare pass (prep_tree_kernel), the leaf kernel on the prepared
             # operands and, at depth 2, the deferred decode; the leaf events
             # bracket the leaf launches only ("prepare_and_materialise_ms" is
             # the rest of the call).
@@ -1061,7 +1061,7 @@ def run_bag(args) -> None:
             roofline = {"bound": "tensor", "kernel": kname,
                         "achieved": leaf_tflops, "peak": sustained / 3.0, "unit": "TFLOP/s",
                         "frac": leaf_tflops / (sustained / 3.0),
-                        "traffic": read_traffic(kfile),
+                        "traffic": traffic_for(args, world, kfile),
                         "prepare_and_materialise_ms": ms - leaf_ms,
                         "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (of measured; "
                                        "the kernel runs inside a long power-capped step) / 2 "
@@ -1075,7 +1075,7 @@ def run_bag(args) -> None:
                                                       "(FP32 FFMA SIMT)",
                         "achieved": leaf_tflops, "peak": nominal, "unit": "TFLOP/s",
                         "frac": leaf_tflops / nominal,
-                        "traffic": read_traffic("leaf_gemm_cfg3_traffic.txt"),
+                        "traffic": traffic_for(args, world, "leaf_gemm_cfg3_traffic.txt"),
                         "peak_source": f"nominal FP32 FFMA {sms} SM x 128 lanes x 2 x "
                                        f"{max_mhz:.0f} MHz (MEASURED_PEAKS.json has no FP32 "
                                        f"SIMT figure)",
@@ -1183,6 +1183,15 @@ def measured_peaks() -> dict:
             return json.load(f)
     except (OSError, ValueError):
         return {}
+
+
+def traffic_for(args, world: int, name: str):
+    """The committed ncu traffic figure, which is per cfg3 leaf launch on one
+    GPU: reported for that workload only (null for the other configs and for
+    a rank's shard at N > 1, whose launches are smaller)."""
+    if getattr(args, "config", "cfg3") != "cfg3" or world != 1 or args.depth != 2:
+        return None
+    return read_traffic(name)
 
 
 def read_traffic(name: str):
