@@ -34,6 +34,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
 #include <cstring>
@@ -280,12 +281,21 @@ __device__ __forceinline__ float4 signed_add(float4 acc, float4 v, int code, boo
 // plan's codes), each output from the mids, splits it into TF32 hi/lo and
 // stores both.  Inputs past the block (rows or k) read as zero, so the
 // region's padding past an operand's k extent is written as zero.
+//
+// kIn bounds the inputs of every group of the launch: 16 at depth 2 (two CTAs
+// per SM), 4 at depth 1, where the smaller staging area and register file let
+// four CTAs share an SM -- twice the loads in flight for a pass whose CTAs
+// each move only 16 KB in and 56 KB out.
 constexpr int kTreeTile = 32;
 constexpr int kTreePitch = kTreeTile + 1;
 constexpr int kTreeThreads = 256;
-constexpr int kTreeSmemBytes = kTreeIn * kTreeTile * kTreePitch * 4;
+constexpr int kTreeSmallIn = 4;
 
-__global__ void __launch_bounds__(kTreeThreads, 2)
+template <int kIn>
+constexpr int tree_smem_bytes() { return kIn * kTreeTile * kTreePitch * 4; }
+
+template <int kIn>
+__global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 4 : 2)
     prep_tree_kernel(const __grid_constant__ PrepTreePlan plan) {
   extern __shared__ float staged[];                   // [input][k][row], pitch kTreePitch
   __shared__ float4 mids[kTreeMid][kTreeThreads];      // this thread's mids
@@ -302,14 +312,14 @@ __global__ void __launch_bounds__(kTreeThreads, 2)
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
 
   // Load every input's piece first (up to 16 loads in flight), then stage.
-  float4 v[kTreeIn];
+  float4 v[kIn];
   if (G.transpose) {
     // Left operand: element (r, k) at p + r + k * ld; rows 4 (t % 8) .. +3 of k
     // column t / 8 of the tile.
     const int rr = 4 * (t % 8), kk = t / 8;
     const int r = r0 + rr, k = k0 + kk;
 #pragma unroll
-    for (int u = 0; u < kTreeIn; ++u) {
+    for (int u = 0; u < kIn; ++u) {
       v[u] = zero;
       if (u < G.nin && k < G.cols) {
         const Term& T = G.in[u];
@@ -324,7 +334,7 @@ __global__ void __launch_bounds__(kTreeThreads, 2)
       }
     }
 #pragma unroll
-    for (int u = 0; u < kTreeIn; ++u) {
+    for (int u = 0; u < kIn; ++u) {
       if (u < G.nin) {
         float* s = staged + (u * kTreeTile + kk) * kTreePitch + rr;
         s[0] = v[u].x;
@@ -338,7 +348,7 @@ __global__ void __launch_bounds__(kTreeThreads, 2)
     // `row` of the tile.
     const int r = r0 + row, k = k0 + kc;
 #pragma unroll
-    for (int u = 0; u < kTreeIn; ++u) {
+    for (int u = 0; u < kIn; ++u) {
       v[u] = zero;
       if (u < G.nin && r < G.rows) {
         const Term& T = G.in[u];
@@ -353,7 +363,7 @@ __global__ void __launch_bounds__(kTreeThreads, 2)
       }
     }
 #pragma unroll
-    for (int u = 0; u < kTreeIn; ++u) {
+    for (int u = 0; u < kIn; ++u) {
       if (u < G.nin) {
         float* s = staged + (u * kTreeTile + kc) * kTreePitch + row;
         s[0] = v[u].x;
@@ -1114,14 +1124,25 @@ bool prep_pair_supported() { return prep_supported() && pair_clusters() > 0; }
 
 int prep_row_align() { return 64; }   // a multiple of the 32-k stage and the 32-k prepare tile
 
+template <int kIn>
+cudaError_t launch_prep_tree_in(const PrepTreePlan& plan, int batch, cudaStream_t stream) {
+  constexpr int smem = tree_smem_bytes<kIn>();
+  cudaError_t e = cudaFuncSetAttribute(prep_tree_kernel<kIn>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  prep_tree_kernel<kIn><<<dim3(unsigned(plan.ntiles), batch), kTreeThreads, smem, stream>>>(plan);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_prep_tree(const PrepTreePlan& plan, int batch, cudaStream_t stream) {
   if (plan.ngroups == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(prep_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kTreeSmemBytes);
-  if (e != cudaSuccess) return e;
-  prep_tree_kernel<<<dim3(unsigned(plan.ntiles), batch), kTreeThreads, kTreeSmemBytes, stream>>>(
-      plan);
-  return cudaGetLastError();
+  int nin = 0;
+  for (int g = 0; g < plan.ngroups; ++g) {
+    if (plan.group[g].nin < 0 || plan.group[g].nin > kTreeIn) return cudaErrorInvalidValue;
+    nin = std::max(nin, plan.group[g].nin);
+  }
+  return nin <= kTreeSmallIn ? launch_prep_tree_in<kTreeSmallIn>(plan, batch, stream)
+                             : launch_prep_tree_in<kTreeIn>(plan, batch, stream);
 }
 
 cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* region,

@@ -109,10 +109,6 @@ __device__ __forceinline__ const Prod& find_prod(const LeafPlan& plan, int item)
   return plan.prod[pid];
 }
 
-__device__ __forceinline__ float4 ldg4(const float* p) {
-  return __ldg(reinterpret_cast<const float4*>(p));
-}
-
 __device__ __forceinline__ float4 add_signed(float4 acc, float4 v, float coef) {
   return make_float4(fmaf(coef, v.x, acc.x), fmaf(coef, v.y, acc.y), fmaf(coef, v.z, acc.z),
                      fmaf(coef, v.w, acc.w));
