@@ -176,13 +176,19 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 
 // Tile load for a CTA pair: the copy lands in this CTA's shared memory and
 // completes on the mbarrier at `bar`, a shared::cluster address in either CTA
-// of the pair (.cta_group::2): a plain load into this CTA's own tile.
+// of the pair (.cta_group::2): a plain load into this CTA's own tile.  The
+// prepared operands are re-read by every tile that shares their block, so the
+// load asks L2 to keep them (evict_last); the product buffers the epilogue
+// writes are streamed (st.global.cs).  Measured on the cfg3 leaf launch: DRAM
+// reads 71.1 -> 68.5 GB.
 __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int x, int y,
                                                  int z, uint32_t bar) {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
   asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
       : "memory");
 }
 
@@ -277,28 +283,38 @@ __device__ __forceinline__ float4 signed_add(float4 acc, float4 v, int code, boo
 // pitch: conflict-free both for a left operand's loads along the rows and for
 // the threads' reads along k); a right operand (k contiguous in its source)
 // is loaded along k.  Then, segment by segment, the thread evaluates the
-// segment's mids from the inputs (kept in shared memory, indexed by the
-// plan's codes), each output from the mids, splits it into TF32 hi/lo and
-// stores both.  Inputs past the block (rows or k) read as zero, so the
-// region's padding past an operand's k extent is written as zero.
+// segment's mids from the inputs (the mids stay in the thread's registers,
+// picked by the plan's codes with selects), each output from the mids, splits
+// it into TF32 hi/lo and stores both.  Inputs past the block (rows or k) read
+// as zero, so the region's padding past an operand's k extent is written as
+// zero.
 //
-// kIn bounds the inputs of every group of the launch: 16 at depth 2 (two CTAs
-// per SM), 4 at depth 1, where the smaller staging area and register file let
-// four CTAs share an SM -- twice the loads in flight for a pass whose CTAs
-// each move only 16 KB in and 56 KB out.
+// kIn bounds the inputs of every group of the launch: 16 at depth 2, 4 at
+// depth 1.  Inputs are loaded eight at a time (eight 16-byte loads in flight
+// per thread), so the kernel fits three CTAs per SM at depth 2 (68 KB of
+// staging each) and five at depth 1: a CTA's stores (56 KB at depth 1, 392 KB
+// at depth 2) then overlap other CTAs' load phases.
 constexpr int kTreeTile = 32;
 constexpr int kTreePitch = kTreeTile + 1;
 constexpr int kTreeThreads = 256;
 constexpr int kTreeSmallIn = 4;
+constexpr int kTreeLoadBatch = 8;
 
 template <int kIn>
 constexpr int tree_smem_bytes() { return kIn * kTreeTile * kTreePitch * 4; }
 
+__device__ __forceinline__ float4 pick_mid(const float4 (&md)[kTreeMid], int i) {
+  float4 r = md[0];
+#pragma unroll
+  for (int j = 1; j < kTreeMid; ++j)
+    if (i == j) r = md[j];
+  return r;
+}
+
 template <int kIn>
-__global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 4 : 2)
+__global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 5 : 3)
     prep_tree_kernel(const __grid_constant__ PrepTreePlan plan) {
   extern __shared__ float staged[];                   // [input][k][row], pitch kTreePitch
-  __shared__ float4 mids[kTreeMid][kTreeThreads];      // this thread's mids
   const long long item = blockIdx.x;
   int gi = 0;
   while (gi + 1 < plan.ngroups && plan.group[gi + 1].tile_begin <= item) ++gi;
@@ -310,66 +326,72 @@ __global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 4 : 2)
   const int t = threadIdx.x;
   const int row = 4 * (t / 32) + (t % 32) / 8, kc = 4 * (t % 8);
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  constexpr int kBatch = kIn < kTreeLoadBatch ? kIn : kTreeLoadBatch;
 
-  // Load every input's piece first (up to 16 loads in flight), then stage.
-  float4 v[kIn];
-  if (G.transpose) {
-    // Left operand: element (r, k) at p + r + k * ld; rows 4 (t % 8) .. +3 of k
-    // column t / 8 of the tile.
-    const int rr = 4 * (t % 8), kk = t / 8;
-    const int r = r0 + rr, k = k0 + kk;
 #pragma unroll
-    for (int u = 0; u < kIn; ++u) {
-      v[u] = zero;
-      if (u < G.nin && k < G.cols) {
-        const Term& T = G.in[u];
-        const float* p = T.p + batch * T.bstride + r + (long long)k * T.ld;
-        if (r + 3 < G.rows) {
-          v[u] = load4(p);
-        } else {
-          if (r + 0 < G.rows) v[u].x = p[0];
-          if (r + 1 < G.rows) v[u].y = p[1];
-          if (r + 2 < G.rows) v[u].z = p[2];
+  for (int u0 = 0; u0 < kIn; u0 += kBatch) {
+    if (u0 >= G.nin) break;
+    float4 v[kBatch];
+    if (G.transpose) {
+      // Left operand: element (r, k) at p + r + k * ld; rows 4 (t % 8) .. +3
+      // of k column t / 8 of the tile.
+      const int rr = 4 * (t % 8), kk = t / 8;
+      const int r = r0 + rr, k = k0 + kk;
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int u = u0 + j;
+        v[j] = zero;
+        if (u < G.nin && k < G.cols) {
+          const Term& T = G.in[u];
+          const float* p = T.p + batch * T.bstride + r + (long long)k * T.ld;
+          if (r + 3 < G.rows) {
+            v[j] = load4(p);
+          } else {
+            if (r + 0 < G.rows) v[j].x = p[0];
+            if (r + 1 < G.rows) v[j].y = p[1];
+            if (r + 2 < G.rows) v[j].z = p[2];
+          }
         }
       }
-    }
 #pragma unroll
-    for (int u = 0; u < kIn; ++u) {
-      if (u < G.nin) {
-        float* s = staged + (u * kTreeTile + kk) * kTreePitch + rr;
-        s[0] = v[u].x;
-        s[1] = v[u].y;
-        s[2] = v[u].z;
-        s[3] = v[u].w;
-      }
-    }
-  } else {
-    // Right operand: element (k, r) at p + k + r * ld; k values kc .. +3 of row
-    // `row` of the tile.
-    const int r = r0 + row, k = k0 + kc;
-#pragma unroll
-    for (int u = 0; u < kIn; ++u) {
-      v[u] = zero;
-      if (u < G.nin && r < G.rows) {
-        const Term& T = G.in[u];
-        const float* p = T.p + batch * T.bstride + k + (long long)r * T.ld;
-        if (k + 3 < G.cols) {
-          v[u] = load4(p);
-        } else {
-          if (k + 0 < G.cols) v[u].x = p[0];
-          if (k + 1 < G.cols) v[u].y = p[1];
-          if (k + 2 < G.cols) v[u].z = p[2];
+      for (int j = 0; j < kBatch; ++j) {
+        if (u0 + j < G.nin) {
+          float* s = staged + ((u0 + j) * kTreeTile + kk) * kTreePitch + rr;
+          s[0] = v[j].x;
+          s[1] = v[j].y;
+          s[2] = v[j].z;
+          s[3] = v[j].w;
         }
       }
-    }
+    } else {
+      // Right operand: element (k, r) at p + k + r * ld; k values kc .. +3 of
+      // row `row` of the tile.
+      const int r = r0 + row, k = k0 + kc;
 #pragma unroll
-    for (int u = 0; u < kIn; ++u) {
-      if (u < G.nin) {
-        float* s = staged + (u * kTreeTile + kc) * kTreePitch + row;
-        s[0] = v[u].x;
-        s[kTreePitch] = v[u].y;
-        s[2 * kTreePitch] = v[u].z;
-        s[3 * kTreePitch] = v[u].w;
+      for (int j = 0; j < kBatch; ++j) {
+        const int u = u0 + j;
+        v[j] = zero;
+        if (u < G.nin && r < G.rows) {
+          const Term& T = G.in[u];
+          const float* p = T.p + batch * T.bstride + k + (long long)r * T.ld;
+          if (k + 3 < G.cols) {
+            v[j] = load4(p);
+          } else {
+            if (k + 0 < G.cols) v[j].x = p[0];
+            if (k + 1 < G.cols) v[j].y = p[1];
+            if (k + 2 < G.cols) v[j].z = p[2];
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        if (u0 + j < G.nin) {
+          float* s = staged + ((u0 + j) * kTreeTile + kc) * kTreePitch + row;
+          s[0] = v[j].x;
+          s[kTreePitch] = v[j].y;
+          s[2 * kTreePitch] = v[j].z;
+          s[3 * kTreePitch] = v[j].w;
+        }
       }
     }
   }
@@ -384,15 +406,18 @@ __global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 4 : 2)
   const long long ld = plan.row_len;
   for (int sg = 0; sg < G.nseg; ++sg) {
     const TreeSeg& S = G.seg[sg];
-    for (int i = 0; i < S.nmid; ++i) {
-      float4 m = zero;
+    float4 md[kTreeMid];
 #pragma unroll
-      for (int q = 0; q < kMaxOperandTerms; ++q) {
-        const int code = S.mid[i][q];
-        if (code == 0) break;
-        m = signed_add(m, input((code > 0 ? code : -code) - 1), code, q == 0);
+    for (int i = 0; i < kTreeMid; ++i) {
+      md[i] = zero;
+      if (i < S.nmid) {
+#pragma unroll
+        for (int q = 0; q < kMaxOperandTerms; ++q) {
+          const int code = S.mid[i][q];
+          if (code == 0) break;
+          md[i] = signed_add(md[i], input((code > 0 ? code : -code) - 1), code, q == 0);
+        }
       }
-      mids[i][t] = m;
     }
     for (int o = 0; o < S.nout; ++o) {
       float4 x = zero;
@@ -400,7 +425,7 @@ __global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 4 : 2)
       for (int q = 0; q < kMaxOperandTerms; ++q) {
         const int code = S.expr[o][q];
         if (code == 0) break;
-        x = signed_add(x, mids[(code > 0 ? code : -code) - 1][t], code, q == 0);
+        x = signed_add(x, pick_mid(md, (code > 0 ? code : -code) - 1), code, q == 0);
       }
       const float4 h = hi4(x);
       float* dst = region + (long long)(S.out_hi[o] + r) * ld + k0 + kc;
@@ -596,7 +621,7 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
             float* dst = base + (long long)col * T.ld;
             if (T.mode == kOutAtomic) atomicAdd(dst, coef * total[i]);
             else if (T.mode == kOutAdd) *dst += coef * total[i];
-            else *dst = coef * total[i];
+            else __stcs(dst, coef * total[i]);   // streamed: keep L2 for the operands
           }
         }
       }
@@ -900,7 +925,7 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
             float* dst = base + (long long)col * T.ld;
             if (T.mode == kOutAtomic) atomicAdd(dst, coef * total[i]);
             else if (T.mode == kOutAdd) *dst += coef * total[i];
-            else *dst = coef * total[i];
+            else __stcs(dst, coef * total[i]);   // streamed: keep L2 for the operands
           }
         }
       }
