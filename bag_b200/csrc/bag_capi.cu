@@ -16,6 +16,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdint>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -38,7 +39,24 @@ namespace bag_b200 {
 namespace {
 
 thread_local std::string g_last_error;
-thread_local int g_math_mode = BAG_MATH_FFMA;
+
+// The math mode every host thread starts in: FFMA (the reference's
+// sequential-fmaf numerics) unless the environment's BAG_B200_MATH says
+// "3xtf32", so a program written against the reference's headers takes the
+// tensor-core leaves without a code change.  Read once per process; a value
+// other than "ffma" or "3xtf32" is reported on stderr and FFMA kept.
+int process_default_math_mode() {
+  static const int mode = [] {
+    const char* env = std::getenv("BAG_B200_MATH");
+    if (!env || !*env || std::strcmp(env, "ffma") == 0) return int(BAG_MATH_FFMA);
+    if (std::strcmp(env, "3xtf32") == 0) return int(BAG_MATH_3XTF32);
+    std::fprintf(stderr, "bag_b200: BAG_B200_MATH=%s is not ffma or 3xtf32; using ffma\n", env);
+    return int(BAG_MATH_FFMA);
+  }();
+  return mode;
+}
+
+thread_local int g_math_mode = process_default_math_mode();
 thread_local int g_last_leaf_path = BAG_MATH_FFMA;
 // Leaf kernel of the last call's prepared-operand path (BAG_LEAF_KERNEL_*).
 thread_local int g_last_prep_kind = -1;

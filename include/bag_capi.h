@@ -181,7 +181,9 @@ unsigned long long bag_launch_count(void);
  * (a caller can check that a call allocated nothing). */
 unsigned long long bag_device_allocations(void);
 /* Math mode of later calls on this host thread (like cublasSetMathMode);
- * new, no reference counterpart. */
+ * new, no reference counterpart.  A thread starts in BAG_MATH_FFMA, or in
+ * BAG_MATH_3XTF32 when the process was started with BAG_B200_MATH=3xtf32 (a
+ * drop-in switch for programs that only call the reference's API). */
 bag_status bag_set_math_mode(int mode);
 int bag_get_math_mode(void);
 /* Leaf arithmetic the last call on this host thread used (BAG_MATH_*): 3XTF32

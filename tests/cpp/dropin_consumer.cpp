@@ -4,7 +4,11 @@
 // (benchmarks/cuda/bag.cu:51-101).  Built with a plain host compiler and
 // linked against libbag_b200.so; run on a GPU it checks C <- AB + C on
 // exactly representable inputs against an FP64 dot product at sampled
-// positions and exits non-zero on failure.
+// positions and exits non-zero on failure.  An optional argument sets n (a
+// multiple of 256; default 256); after each matmul case the consumer prints
+// the leaf arithmetic the library reports (bag_last_leaf_path, the one name
+// it uses beyond the reference's), so a run under BAG_B200_MATH=3xtf32 can
+// show the tensor-core leaves were taken without a code change.
 #include <bag/cuda/bag.cuh>
 
 #include <cmath>
@@ -42,8 +46,12 @@ bool check(const std::vector<float>& a, const std::vector<float>& b, const std::
 
 }  // namespace
 
-int main() try {
-  const int n = 256;
+int main(int argc, char** argv) try {
+  const int n = argc > 1 ? std::atoi(argv[1]) : 256;
+  if (n <= 0 || n % 256) {
+    std::fprintf(stderr, "n must be a positive multiple of 256\n");
+    return 2;
+  }
   const size_t count = size_t(n) * n;
   std::vector<float> a(count), b(count), c0(count), c(count);
   for (size_t i = 0; i < count; ++i) {
@@ -67,6 +75,8 @@ int main() try {
       strassen_cuda::checked(cudaStreamSynchronize(caller));
       strassen_cuda::checked(cudaMemcpy(c.data(), dc.p, count * 4, cudaMemcpyDeviceToHost));
       ok = check(a, b, c0, c, n, 3, basis == bag_cuda::Basis::Full ? "bag_full" : "bag_minimal") && ok;
+      std::printf("depth=%d leaf_path=%s\n", depth,
+                  bag_last_leaf_path() == BAG_MATH_3XTF32 ? "3xtf32" : "ffma");
     }
   }
   strassen_cuda::Workspace workers;

@@ -162,3 +162,26 @@ def test_device_allocation_counter_without_a_gpu():
     bag.workspace_bytes_for(4096, 4096, 4096, 2, math="3xtf32")
     bag.plan_dump(256, 256, 256, 256, 256, 256, 2)
     assert bag.device_allocations() == before   # sizing and planning allocate nothing
+
+
+@pytest.mark.parametrize("value,want,warns", [(None, "ffma", False), ("ffma", "ffma", False),
+                                              ("3xtf32", "3xtf32", False),
+                                              ("tf32", "ffma", True)])
+def test_math_mode_default_from_environment(value, want, warns):
+    """BAG_B200_MATH sets the mode every host thread starts in (the main thread
+    and a new one alike); an unknown value keeps FFMA and says so on stderr."""
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = {k: v for k, v in os.environ.items() if k != "BAG_B200_MATH"}
+    if value is not None:
+        env["BAG_B200_MATH"] = value
+    prog = ("import threading, bag_b200 as bag\n"
+            "seen = []\n"
+            "t = threading.Thread(target=lambda: seen.append(bag.get_math_mode()))\n"
+            "t.start(); t.join()\n"
+            "print(bag.get_math_mode(), seen[0])\n")
+    r = subprocess.run([sys.executable, "-c", prog], cwd=root, env=env, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.split() == [want, want]
+    assert ("BAG_B200_MATH" in r.stderr) == warns

@@ -82,3 +82,22 @@ def test_consumer_runs_on_gpu(built_lib, cuda):
     print(out.stdout)
     assert out.returncode == 0, out.stdout + out.stderr
     assert "DROPIN OK" in out.stdout
+
+
+@pytest.mark.gpu
+def test_consumer_takes_tensor_leaves_from_environment(built_lib, cuda):
+    """BAG_B200_MATH=3xtf32 switches a program that only calls the reference's
+    API: at n = 2048 its depth-1 leaves (K = 1024) run on the tensor cores, its
+    depth-2 leaves (K = 512) stay on FFMA, and every result passes the check."""
+    exe = build_consumer(built_lib)
+    env = dict(os.environ, BAG_B200_MATH="3xtf32")
+    out = subprocess.run([exe, "2048"], capture_output=True, text=True, timeout=300, env=env)
+    print(out.stdout)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert "DROPIN OK" in out.stdout
+    paths = [line.split() for line in out.stdout.splitlines() if line.startswith("depth=")]
+    assert sorted(paths) == [["depth=1", "leaf_path=3xtf32"]] * 2 + [["depth=2", "leaf_path=ffma"]] * 2
+    plain = subprocess.run([exe, "2048"], capture_output=True, text=True, timeout=300,
+                           env={k: v for k, v in os.environ.items() if k != "BAG_B200_MATH"})
+    assert plain.returncode == 0, plain.stdout + plain.stderr
+    assert "leaf_path=3xtf32" not in plain.stdout
