@@ -740,7 +740,8 @@ int choose_tile(const std::vector<HostLeaf>& leaves, int sm_count, bool vec) {
   };
   if (all_fast && tiles_for(kTileWS) >= sm_count) return kTileWS;
   if (tiles_for(kTileTall) >= 2LL * sm_count) return kTileTall;
-  return tiles_for(kTileLarge) >= 2LL * sm_count ? kTileLarge : kTileSmall;
+  if (tiles_for(kTileLarge) >= 2LL * sm_count) return kTileLarge;
+  return tiles_for(kTileSmall) >= 2LL * sm_count ? kTileSmall : kTileMicro;
 }
 
 // The compiled main loop for a product (kSigGeneric when none applies).

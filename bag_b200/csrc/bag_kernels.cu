@@ -548,6 +548,12 @@ using CfgTall = Cfg<256, 128, 8, 16, 8, 1, true, false>;    // 256 threads, 1 CT
 using CfgLarge1 = Cfg<128, 128, 8, 8, 8, 1, true, true>;    // 256 threads, 1 CTA/SM, FFMA2
 using CfgHalf = Cfg<128, 64, 8, 8, 8, 2, true, true>;       // 128 threads, 2 CTAs/SM, FFMA2
 using CfgTallS = Cfg<256, 128, 8, 16, 8, 1, false, true>;   // Tall, single-buffered, FFMA2
+// Tiny problems (cfg1: 7 leaves of 256^3 make 28 tiles of 128 x 128, 112 of
+// 64 x 64): 448 CTAs of two warps spread over every SM; each output is still
+// one sequential fmaf chain, so the results do not depend on the tile.  16-k
+// steps: measured on cfg1 the leaf phase takes 29.5 us with 8, 25.5 with 16,
+// 32.3 with 32 (the 64-k-long step holds too few CTAs' loads in flight).
+using CfgMicro = Cfg<32, 32, 16, 4, 4, 8, true, false>;     // 64 threads
 
 template <class C>
 cudaError_t launch_cfg(const LeafPlan& plan, bool vec, int batch, cudaStream_t stream) {
@@ -567,6 +573,7 @@ TileShape leaf_tile_shape(int config) {
     case kTileLarge1: return {CfgLarge1::BM, CfgLarge1::BN};
     case kTileHalf: return {CfgHalf::BM, CfgHalf::BN};
     case kTileTallS: return {CfgTallS::BM, CfgTallS::BN};
+    case kTileMicro: return {CfgMicro::BM, CfgMicro::BN};
     case kTileWS: return ws_tile_shape();
     default: return {CfgLarge::BM, CfgLarge::BN};
   }
@@ -581,6 +588,7 @@ cudaError_t launch_leaf(const LeafPlan& plan, int config, bool vec, int batch, c
     case kTileLarge1: return launch_cfg<CfgLarge1>(plan, vec, batch, stream);
     case kTileHalf: return launch_cfg<CfgHalf>(plan, vec, batch, stream);
     case kTileTallS: return launch_cfg<CfgTallS>(plan, vec, batch, stream);
+    case kTileMicro: return launch_cfg<CfgMicro>(plan, vec, batch, stream);
     case kTileWS: return launch_leaf_ws(plan, batch, stream);
     default: return launch_cfg<CfgLarge>(plan, vec, batch, stream);
   }

@@ -16,7 +16,8 @@ enum : int {
   kTileHalf = 5,    // 128 x 64 CTA tile, 128 threads, 8 x 8 per thread, 2 CTAs/SM
   kTileTallS = 6,   // Tall with single-buffered register fragments
   kTileWS = 7,      // warp-specialised 128 x 128 kernel (bag_ws_kernel.cu), fast signatures only
-  kTileCount = 8,
+  kTileMicro = 8,   // 32 x 32 CTA tile, 64 threads, 4 x 4 FFMA per thread, for tiny grids
+  kTileCount = 9,
 };
 
 struct TileShape {
