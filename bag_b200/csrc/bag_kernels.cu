@@ -551,8 +551,8 @@ using CfgTallS = Cfg<256, 128, 8, 16, 8, 1, false, true>;   // Tall, single-buff
 // Tiny problems (cfg1: 7 leaves of 256^3 make 28 tiles of 128 x 128, 112 of
 // 64 x 64): 448 CTAs of two warps spread over every SM; each output is still
 // one sequential fmaf chain, so the results do not depend on the tile.  16-k
-// steps: measured on cfg1 the leaf phase takes 29.5 us with 8, 25.5 with 16,
-// 32.3 with 32 (the 64-k-long step holds too few CTAs' loads in flight).
+// steps: measured on cfg1 the leaf phase takes 29.5 us with 8-k steps, 25.5
+// with 16, 32.3 with 32.
 using CfgMicro = Cfg<32, 32, 16, 4, 4, 8, true, false>;     // 64 threads
 
 template <class C>
