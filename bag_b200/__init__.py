@@ -273,10 +273,16 @@ def _torch():
     return torch
 
 
-def _stream_handle(stream=None) -> Optional[int]:
+def _stream_handle(stream=None, device: Optional[int] = None) -> Optional[int]:
+    """The raw cudaStream_t of `stream`, else torch's current stream on `device`
+    (the current device when None) -- read without building a Stream object,
+    which costs more than the rest of a small call's Python work."""
+    if stream is not None:
+        return stream.cuda_stream
     torch = _torch()
-    s = torch.cuda.current_stream() if stream is None else stream
-    return s.cuda_stream
+    if device is None:
+        device = torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(device)
 
 
 def _layout_of(t) -> Optional[tuple[str, int]]:
@@ -360,7 +366,7 @@ def sgemm(a, b, c, *, beta: float = 1.0, depth: int = 1, basis="minimal",
     ws = workspace.handle if workspace is not None else None
     _check(lib().bag_sgemm_ex(LAYOUT[la[0]], m, n, k, a.data_ptr(), la[1], b.data_ptr(), lb[1],
                               c.data_ptr(), lc[1], float(beta), _depth(depth), _basis(basis),
-                              _stream_handle(stream), ws))
+                              _stream_handle(stream, c.get_device()), ws))
     _warn_if_fused(workspace)
     return c
 
@@ -369,8 +375,8 @@ def _warn_if_fused(workspace) -> None:
     """Warn (once per call site) when a 3xTF32 call ran the fused-transform
     tensor kernel although a workspace was given: that workspace was created
     in FFMA mode and lacks the prepared operands of the fast path."""
-    if workspace is not None and int(lib().bag_get_math_mode()) == MATH["3xtf32"] and \
-            int(lib().bag_last_leaf_kernel()) == 1:
+    # Kernel id 1 (the fused-transform tensor kernel) runs only in 3xTF32 mode.
+    if workspace is not None and int(lib().bag_last_leaf_kernel()) == 1:
         warnings.warn("bag_b200: this 3xTF32 call ran the fused-transform tensor kernel because "
                       "its workspace was created in FFMA mode; create the workspace after "
                       "set_math_mode('3xtf32') (size: workspace_bytes_for(..., math='3xtf32')) "
@@ -447,7 +453,7 @@ def sgemm_batched(a, b, c, *, beta: float = 1.0, depth: int = 1, basis="minimal"
     ws = workspace.handle if workspace is not None else None
     _check(lib().bag_sgemm_batched(LAYOUT["row"], m, n, k, a.data_ptr(), k, m * k, b.data_ptr(), n,
                                    k * n, c.data_ptr(), n, m * n, batch, float(beta), _depth(depth),
-                                   _basis(basis), _stream_handle(stream), ws))
+                                   _basis(basis), _stream_handle(stream, c.get_device()), ws))
     _warn_if_fused(workspace)
     return c
 

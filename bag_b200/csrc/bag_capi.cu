@@ -1061,6 +1061,51 @@ void check_device_workspace(const bag_workspace* ws) {
   if (ws->device != dev) fail(BAG_ERR_WORKSPACE, "workspace belongs to another device");
 }
 
+// Plans of recent calls, per host thread.  A plan holds absolute addresses
+// and depends on nothing but the key's fields (the problem with every pointer,
+// leading dimension and stride, beta, the math mode, the workspace and its
+// size, the device), so a call equal in all of them reuses the plan as it was
+// built and skips the two or three host-side builds.  Executing a plan leaves
+// it unchanged (splitting long FFMA chains is idempotent).  A freed and
+// reallocated buffer at the same address is the same operand to a plan.
+struct PlanKey {
+  GemmDesc g;
+  float beta;
+  int mode;
+  const bag_workspace* ws;
+  const float* ws_data;
+  size_t ws_elements;
+  int device;
+  bool operator==(const PlanKey& o) const {
+    return g.m == o.g.m && g.n == o.g.n && g.k == o.g.k && g.a == o.g.a && g.lda == o.g.lda &&
+           g.sa == o.g.sa && g.b == o.g.b && g.ldb == o.g.ldb && g.sb == o.g.sb && g.c == o.g.c &&
+           g.ldc == o.g.ldc && g.sc == o.g.sc && g.batch == o.g.batch && g.depth == o.g.depth &&
+           g.basis == o.g.basis && beta == o.beta && mode == o.mode && ws == o.ws &&
+           ws_data == o.ws_data && ws_elements == o.ws_elements && device == o.device;
+  }
+};
+constexpr size_t kPlanCacheSize = 8;
+struct CachedPlan {
+  PlanKey key;
+  Builder plan;
+};
+thread_local std::vector<CachedPlan> g_plan_cache;   // most recent last
+
+Builder* cached_plan(const PlanKey& key) {
+  for (size_t i = g_plan_cache.size(); i-- > 0;) {
+    if (g_plan_cache[i].key == key) {
+      if (i + 1 != g_plan_cache.size()) std::swap(g_plan_cache[i], g_plan_cache.back());
+      return &g_plan_cache.back().plan;
+    }
+  }
+  return nullptr;
+}
+
+void remember_plan(const PlanKey& key, Builder&& plan) {
+  if (g_plan_cache.size() == kPlanCacheSize) g_plan_cache.erase(g_plan_cache.begin());
+  g_plan_cache.push_back(CachedPlan{key, std::move(plan)});
+}
+
 void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
   if (g.m < 0 || g.n < 0 || g.k < 0) fail(BAG_ERR_SHAPE, "negative extent");
   g.depth = resolve_depth(g.depth, g.m, g.n, g.k);
@@ -1080,6 +1125,16 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
   };
   if (g.k == 0) {
     if (beta == 0.f) zero_c();
+    return;
+  }
+  const std::vector<TcSource> sources = {{g.a, g.lda, g.sa, g.m, g.k}, {g.b, g.ldb, g.sb, g.k, g.n}};
+  int device = 0;
+  cuda_check(cudaGetDevice(&device), "cudaGetDevice");
+  PlanKey key{g, beta, g_math_mode, ws, ws ? ws->data : nullptr, ws ? ws->elements : 0, device};
+  if (Builder* hit = cached_plan(key)) {
+    if (ws) check_device_workspace(ws);
+    if (beta == 0.f && !hit->decode.on) zero_c();
+    execute_plan(*hit, g.batch, stream, sources);
     return;
   }
   // 3xTF32 mode prepares the leaf operands when the workspace was sized for
@@ -1113,8 +1168,8 @@ void run_gemm(GemmDesc g, float beta, cudaStream_t stream, bag_workspace* ws) {
     if (B.decode.on) B.decode.overwrite = true;
     else zero_c();
   }
-  const std::vector<TcSource> sources = {{g.a, g.lda, g.sa, g.m, g.k}, {g.b, g.ldb, g.sb, g.k, g.n}};
   execute_plan(B, g.batch, stream, sources);
+  remember_plan(key, std::move(B));
 }
 
 GemmDesc make_desc(int layout, int m, int n, int k, const float* a, long long lda, long long sa,

@@ -718,11 +718,15 @@ def run_bag(args) -> None:
         host0 = time.time()
         t_start.record()
         for i in range(args.steps):
+            # The library's profiling hooks are set before the step's start
+            # event: with a flush between steps, the step's events time the
+            # call alone.
             if flush is not None:
                 flush.fill_(float(i))
-                step_events[i][0].record()
             bag.profile_events(*pairs[i])
             bag.profile_phase_events(phases[i][1], phases[i][2])
+            if flush is not None:
+                step_events[i][0].record()
             phases[i][0].record()
             step()
             if flush is not None:
