@@ -89,6 +89,7 @@ SIGNATURES = {
     "bag_get_math_mode": (_I, []),
     "bag_last_leaf_path": (_I, []),
     "bag_last_leaf_kernel": (_I, []),
+    "bag_last_prepare_table": (_I, []),
     "bag_selftest_bounded_wait": (_I, [ctypes.c_ulonglong, ctypes.POINTER(_I)]),
     "bag_multi_grid": (_I, [_I, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "bag_multi_workspace_create": (_I, [_I, ctypes.POINTER(_I), _I, _I, _I, _I, _I, _I,
@@ -222,8 +223,15 @@ def last_leaf_kernel() -> str:
     """Leaf kernel the last call on this thread ran: "ffma", "tf32_fused"
     (transforms in the tensor kernel's prologue), "tf32_single" (prepared
     operands, 128 x 256 tiles per SM) or "tf32_pair" (prepared operands,
-    256 x 128 tiles per cluster of two SMs)."""
+    256 x 256 tiles per cluster of two SMs)."""
     return LEAF_KERNELS[int(lib().bag_last_leaf_kernel())]
+
+
+def last_prepare_table() -> int:
+    """Prepare kernel of the last call: 1 Minimal, 2 Full, 3 Classic, 4 Winograd
+    for a basis whose operand expressions are compiled in, 0 for the
+    plan-reading kernel, -1 when the last call prepared nothing."""
+    return int(lib().bag_last_prepare_table())
 
 
 def selftest_bounded_wait(limit_ns: int = 1_000_000) -> bool:

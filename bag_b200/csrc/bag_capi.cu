@@ -790,7 +790,7 @@ int prep_leaf_kind() {
 }
 
 void run_prepared(Builder& B, int batch, cudaStream_t stream) {
-  const int tile = 32;   // prep_tree_kernel's tile: 32 rows x 32 k
+  static_assert(kPrepTreeK <= 64 && 64 % kPrepTreeK == 0, "rows are padded to 64 k");
   const std::vector<Builder::TreeGroupHost>& groups = B.trees;
   for (size_t g0 = 0; g0 < groups.size(); g0 += kMaxTreeGroups) {
     PrepTreePlan pp;
@@ -823,7 +823,8 @@ void run_prepared(Builder& B, int batch, cudaStream_t stream) {
         }
       }
       G.tile_begin = tiles;
-      tiles += (long long)((hg.rows + tile - 1) / tile) * (B.prep_row_len / tile);
+      tiles += (long long)((hg.rows + kPrepTreeRows - 1) / kPrepTreeRows) *
+               (B.prep_row_len / kPrepTreeK);
     }
     pp.ntiles = tiles;
     if (tiles > INT32_MAX) fail(BAG_ERR_SHAPE, "problem too large");
@@ -1708,6 +1709,8 @@ int bag_last_leaf_kernel(void) {
   if (g_last_prep_kind == kPrepLeafSingle) return BAG_LEAF_KERNEL_TF32_SINGLE;
   return BAG_LEAF_KERNEL_TF32_FUSED;
 }
+
+int bag_last_prepare_table(void) { return g_last_prep_kind >= 0 ? last_tree_expr_table() : -1; }
 
 bag_status bag_device_error(unsigned* code) {
   return guarded([&] {

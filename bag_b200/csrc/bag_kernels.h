@@ -69,8 +69,16 @@ enum : int { kPrepLeafSingle = 0, kPrepLeafPair = 1 };
 bool prep_supported();
 bool prep_pair_supported();
 int prep_row_align();
+// prep_tree_kernel's tile: rows x k of every operand of a tree group per CTA.
+constexpr int kPrepTreeRows = 16;
+constexpr int kPrepTreeK = 64;
+// Compiled-in operand expression tables of the tree prepare (4 bases x 2
+// sides); last_tree_expr_table() is the last launch's basis (1 Minimal,
+// 2 Full, 3 Classic, 4 Winograd; 0 = the plan-reading kernel).
+constexpr int kTreeExprCount = 8;
+int last_tree_expr_table();
 TileShape prep_tile_shape(int kind);
-cudaError_t launch_prep_tree(const PrepTreePlan& plan, int batch, cudaStream_t stream);
+cudaError_t launch_prep_tree(PrepTreePlan& plan, int batch, cudaStream_t stream);  // sets group[].table
 cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* region,
                              long long row_len, long long rows, long long region_bstride,
                              int batch, cudaStream_t stream);

@@ -123,6 +123,7 @@ struct TreeSeg {
 struct TreeGroup {
   int rows, cols;
   int transpose, nin, nseg;
+  int table;                                      // 1: segments hold the launch's compiled-in tables
   Term in[kTreeIn];                               // coef unused
   TreeSeg seg[kTreeSeg];
   long long tile_begin;                           // first work item of the group

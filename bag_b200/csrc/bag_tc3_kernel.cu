@@ -36,6 +36,8 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
+#include <utility>
 #include <cstdint>
 #include <cstring>
 
@@ -276,32 +278,42 @@ __device__ __forceinline__ float4 signed_add(float4 acc, float4 v, int code, boo
                      fmaf(c, v.w, acc.w));
 }
 
-// One CTA (256 threads) writes a 32-row x 32-k tile of every operand of a
-// tree group.  Thread t owns row 4 (t / 32) + (t % 32) / 8 of the tile and its
-// k values 4 (t % 8) .. +3, so a warp's store covers 4 rows x 128 contiguous
-// bytes.  Every input's tile is staged in shared memory as [k][row] (a 33-float
-// pitch: conflict-free both for a left operand's loads along the rows and for
-// the threads' reads along k); a right operand (k contiguous in its source)
-// is loaded along k.  Then, segment by segment, the thread evaluates the
-// segment's mids from the inputs (the mids stay in the thread's registers,
-// picked by the plan's codes with selects), each output from the mids, splits
-// it into TF32 hi/lo and stores both.  Inputs past the block (rows or k) read
-// as zero, so the region's padding past an operand's k extent is written as
-// zero.
+// One CTA (256 threads) writes a 16-row x 64-k tile of every operand of a
+// tree group.  Thread t owns row t / 16 of the tile and its k values
+// 4 (t % 16) .. +3, so a warp's store covers 2 rows x 256 contiguous bytes of
+// a plane.  Every input's tile is staged in shared memory in that same
+// [row][k] layout (pitch 68 floats: 16-byte aligned rows, and a warp's
+// 16-byte reads of 2 rows x 256 bytes take the minimum four wavefronts), so
+// the thread reads each input as one float4.  A right operand (k contiguous
+// in its source) is loaded in that layout; a left operand (rows contiguous)
+// is loaded as 4 rows x 1 k per thread (a warp reads 8 columns x 64 bytes)
+// and transposed on its way into shared memory.  Then, segment by segment,
+// the thread evaluates the segment's mids from the inputs (the mids stay in
+// the thread's registers, picked by the plan's codes with selects), each
+// output from the mids, splits it into TF32 hi/lo and stores both.  Inputs
+// past the block (rows or k) read as zero, so the region's padding past an
+// operand's k extent is written as zero.
+//
+// The tile shape is the measured one: on B200, stores of 98 planes in this
+// pattern ran at 6.89 TB/s against 5.47 for 32 x 32 tiles (a warp writing
+// 4 rows x 128 bytes), and 16-row column segments of a column-major source
+// read at 6.09 TB/s against 5.12 for 32-row ones.
 //
 // kIn bounds the inputs of every group of the launch: 16 at depth 2, 4 at
 // depth 1.  Inputs are loaded eight at a time (eight 16-byte loads in flight
-// per thread), so the kernel fits three CTAs per SM at depth 2 (68 KB of
-// staging each) and five at depth 1: a CTA's stores (56 KB at depth 1, 392 KB
-// at depth 2) then overlap other CTAs' load phases.
-constexpr int kTreeTile = 32;
-constexpr int kTreePitch = kTreeTile + 1;
+// per thread), three CTAs per SM at depth 2 (70 KB of staging each) and five
+// at depth 1.
+constexpr int kTreeRows = kPrepTreeRows;   // 16
+constexpr int kTreeK = kPrepTreeK;         // 64
+constexpr int kTreePitch = kTreeK + 4;
 constexpr int kTreeThreads = 256;
 constexpr int kTreeSmallIn = 4;
 constexpr int kTreeLoadBatch = 8;
+thread_local int g_last_tree_table = -1;   // host side: the last launch's basis pair (0 = none)
+static_assert(kTreeRows * kTreeK == 4 * kTreeThreads, "one float4 per thread per input");
 
 template <int kIn>
-constexpr int tree_smem_bytes() { return kIn * kTreeTile * kTreePitch * 4; }
+constexpr int tree_smem_bytes() { return kIn * kTreeRows * kTreePitch * 4; }
 
 __device__ __forceinline__ float4 pick_mid(const float4 (&md)[kTreeMid], int i) {
   float4 r = md[0];
@@ -311,20 +323,87 @@ __device__ __forceinline__ float4 pick_mid(const float4 (&md)[kTreeMid], int i) 
   return r;
 }
 
-template <int kIn>
+// The operand expressions of a tree group are one basis's inner transform,
+// the same in every segment: 7 operands, each a signed sum of up to 4 of the
+// segment's 4 mids (1-based, sign = subtract, 0 = end), in evaluation order;
+// left operands (transposed groups) and right ones have their own table.  A
+// launch with groups that hold one basis's pair of tables runs a kernel with
+// the pair compiled in (kP = 1 Minimal, 2 Full, 3 Classic, 4 Winograd): in
+// those groups (TreeGroup::table, set by the host after comparing every
+// segment with its side's table) the mids stay in registers with fixed
+// indices and an operand costs its arithmetic alone; other groups of the
+// launch (peeled strips of ragged shapes) read their terms from the plan.
+struct TreeExprTable {
+  signed char e[7][4];
+};
+constexpr TreeExprTable kTreeExprTables[kTreeExprCount] = {
+    {{{1, 2, 0, 0}, {2, -3, 0, 0}, {1, -3, 2, 0}, {4, 0, 0, 0}, {1, 0, 0, 0}, {1, -3, 2, -4},
+      {3, 0, 0, 0}}},                                                    // Minimal, left
+    {{{1, 2, 0, 0}, {2, -3, 0, 0}, {1, -3, 2, 0}, {4, 0, 0, 0}, {3, 0, 0, 0}, {1, 0, 0, 0},
+      {1, -3, 2, -4}}},                                                  // Minimal, right
+    {{{1, 0, 0, 0}, {2, 0, 0, 0}, {3, 0, 0, 0}, {4, 0, 0, 0}, {3, -2, 0, 0}, {3, -4, 0, 0},
+      {1, -3, 0, 0}}},                                                   // Full, left
+    {{{1, 0, 0, 0}, {2, 0, 0, 0}, {3, 0, 0, 0}, {4, 0, 0, 0}, {1, -3, 0, 0}, {3, -2, 0, 0},
+      {3, -4, 0, 0}}},                                                   // Full, right
+    {{{1, 2, 0, 0}, {3, 4, 0, 0}, {1, -3, 0, 0}, {4, -2, 0, 0}, {3, 0, 0, 0}, {2, 0, 0, 0},
+      {3, 2, 0, 0}}},                                                    // Classic, left
+    {{{1, 0, 0, 0}, {2, 0, 0, 0}, {1, 3, 0, 0}, {4, 2, 0, 0}, {3, -2, 0, 0}, {4, -1, 0, 0},
+      {1, 2, 0, 0}}},                                                    // Classic, right
+    {{{1, 0, 0, 0}, {2, 0, 0, 0}, {2, -3, -4, 1}, {4, 0, 0, 0}, {3, 4, 0, 0}, {3, 4, -1, 0},
+      {1, -3, 0, 0}}},                                                   // Winograd, left
+    {{{1, 0, 0, 0}, {2, 0, 0, 0}, {3, 0, 0, 0}, {3, -4, 1, -2}, {4, -1, 0, 0}, {3, -4, 1, 0},
+      {3, -4, 0, 0}}},                                                   // Winograd, right
+};
+
+template <int kX, int O, int Q>
+__device__ __forceinline__ float4 table_term(const float4 (&md)[kTreeMid], float4 x) {
+  constexpr int code = kTreeExprTables[kX - 1].e[O][Q];
+  if constexpr (code == 0) {
+    return x;
+  } else {
+    constexpr int idx = (code > 0 ? code : -code) - 1;
+    static_assert(idx < kTreeMid, "table names a mid past the segment's four");
+    return signed_add(x, md[idx], code, Q == 0);
+  }
+}
+
+// Operand O of the table: its terms in order (the rounding of signed_add).
+template <int kX, int O>
+__device__ __forceinline__ float4 table_operand(const float4 (&md)[kTreeMid]) {
+  float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+  x = table_term<kX, O, 0>(md, x);
+  x = table_term<kX, O, 1>(md, x);
+  x = table_term<kX, O, 2>(md, x);
+  return table_term<kX, O, 3>(md, x);
+}
+
+__device__ __forceinline__ void store_hi_lo(float* dst, long long plane, float4 x) {
+  const float4 h = hi4(x);
+  *reinterpret_cast<float4*>(dst) = h;
+  *reinterpret_cast<float4*>(dst + plane) = lo4(x, h);
+}
+
+template <int kX, int... O>
+__device__ __forceinline__ void table_operands(const float4 (&md)[kTreeMid], const TreeSeg& S,
+                                               float* base, long long ld, long long plane,
+                                               std::integer_sequence<int, O...>) {
+  (store_hi_lo(base + (long long)S.out_hi[O] * ld, plane, table_operand<kX, O>(md)), ...);
+}
+
+template <int kIn, int kP>
 __global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 5 : 3)
     prep_tree_kernel(const __grid_constant__ PrepTreePlan plan) {
-  extern __shared__ float staged[];                   // [input][k][row], pitch kTreePitch
+  extern __shared__ __align__(16) float staged[];     // [input][row][k], pitch kTreePitch
   const long long item = blockIdx.x;
   int gi = 0;
   while (gi + 1 < plan.ngroups && plan.group[gi + 1].tile_begin <= item) ++gi;
   const TreeGroup& G = plan.group[gi];
   const long long local = item - G.tile_begin;
-  const int ktiles = plan.row_len / kTreeTile;
-  const int r0 = int(local / ktiles) * kTreeTile, k0 = int(local % ktiles) * kTreeTile;
+  const int ktiles = plan.row_len / kTreeK;
+  const int r0 = int(local / ktiles) * kTreeRows, k0 = int(local % ktiles) * kTreeK;
   const long long batch = blockIdx.y;
   const int t = threadIdx.x;
-  const int row = 4 * (t / 32) + (t % 32) / 8, kc = 4 * (t % 8);
+  const int row = t / (kTreeK / 4), kc = 4 * (t % (kTreeK / 4));
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   constexpr int kBatch = kIn < kTreeLoadBatch ? kIn : kTreeLoadBatch;
 
@@ -333,9 +412,9 @@ __global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 5 : 3)
     if (u0 >= G.nin) break;
     float4 v[kBatch];
     if (G.transpose) {
-      // Left operand: element (r, k) at p + r + k * ld; rows 4 (t % 8) .. +3
-      // of k column t / 8 of the tile.
-      const int rr = 4 * (t % 8), kk = t / 8;
+      // Left operand: element (r, k) at p + r + k * ld; rows 4 (t % 4) .. +3
+      // of k column t / 4 of the tile.
+      const int rr = 4 * (t % (kTreeRows / 4)), kk = t / (kTreeRows / 4);
       const int r = r0 + rr, k = k0 + kk;
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
@@ -356,16 +435,16 @@ __global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 5 : 3)
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
         if (u0 + j < G.nin) {
-          float* s = staged + ((u0 + j) * kTreeTile + kk) * kTreePitch + rr;
+          float* s = staged + ((u0 + j) * kTreeRows + rr) * kTreePitch + kk;
           s[0] = v[j].x;
-          s[1] = v[j].y;
-          s[2] = v[j].z;
-          s[3] = v[j].w;
+          s[kTreePitch] = v[j].y;
+          s[2 * kTreePitch] = v[j].z;
+          s[3 * kTreePitch] = v[j].w;
         }
       }
     } else {
       // Right operand: element (k, r) at p + k + r * ld; k values kc .. +3 of
-      // row `row` of the tile.
+      // row `row` of the tile, the layout the thread computes in.
       const int r = r0 + row, k = k0 + kc;
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
@@ -384,23 +463,17 @@ __global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 5 : 3)
         }
       }
 #pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        if (u0 + j < G.nin) {
-          float* s = staged + ((u0 + j) * kTreeTile + kc) * kTreePitch + row;
-          s[0] = v[j].x;
-          s[kTreePitch] = v[j].y;
-          s[2 * kTreePitch] = v[j].z;
-          s[3 * kTreePitch] = v[j].w;
-        }
-      }
+      for (int j = 0; j < kBatch; ++j)
+        if (u0 + j < G.nin)
+          *reinterpret_cast<float4*>(staged + ((u0 + j) * kTreeRows + row) * kTreePitch + kc) =
+              v[j];
     }
   }
   __syncthreads();
   const int r = r0 + row;
   if (r >= G.rows) return;
   auto input = [&](int u) {
-    const float* s = staged + (u * kTreeTile + kc) * kTreePitch + row;
-    return make_float4(s[0], s[kTreePitch], s[2 * kTreePitch], s[3 * kTreePitch]);
+    return *reinterpret_cast<const float4*>(staged + (u * kTreeRows + row) * kTreePitch + kc);
   };
   float* region = plan.region + batch * plan.region_bstride;
   const long long ld = plan.row_len;
@@ -419,18 +492,30 @@ __global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 5 : 3)
         }
       }
     }
-    for (int o = 0; o < S.nout; ++o) {
-      float4 x = zero;
-#pragma unroll
-      for (int q = 0; q < kMaxOperandTerms; ++q) {
-        const int code = S.expr[o][q];
-        if (code == 0) break;
-        x = signed_add(x, pick_mid(md, (code > 0 ? code : -code) - 1), code, q == 0);
+    bool tabled = false;
+    if constexpr (kP > 0) {
+      if (G.table) {
+        float* base = region + (long long)r * ld + k0 + kc;
+        const long long plane = (long long)G.rows * ld;
+        if (G.transpose)
+          table_operands<2 * kP - 1>(md, S, base, ld, plane, std::make_integer_sequence<int, 7>{});
+        else
+          table_operands<2 * kP>(md, S, base, ld, plane, std::make_integer_sequence<int, 7>{});
+        tabled = true;
       }
-      const float4 h = hi4(x);
-      float* dst = region + (long long)(S.out_hi[o] + r) * ld + k0 + kc;
-      *reinterpret_cast<float4*>(dst) = h;
-      *reinterpret_cast<float4*>(dst + (long long)G.rows * ld) = lo4(x, h);
+    }
+    if (!tabled) {
+      for (int o = 0; o < S.nout; ++o) {
+        float4 x = zero;
+#pragma unroll
+        for (int q = 0; q < kMaxOperandTerms; ++q) {
+          const int code = S.expr[o][q];
+          if (code == 0) break;
+          x = signed_add(x, pick_mid(md, (code > 0 ? code : -code) - 1), code, q == 0);
+        }
+        store_hi_lo(region + (long long)(S.out_hi[o] + r) * ld + k0 + kc, (long long)G.rows * ld,
+                    x);
+      }
     }
   }
 }
@@ -1147,28 +1232,75 @@ bool prep_supported() { return encode_fn() != nullptr; }
 
 bool prep_pair_supported() { return prep_supported() && pair_clusters() > 0; }
 
-int prep_row_align() { return 64; }   // a multiple of the 32-k stage and the 32-k prepare tile
+int prep_row_align() { return 64; }   // a multiple of the 32-k stage and the 64-k prepare tile
 
-template <int kIn>
-cudaError_t launch_prep_tree_in(const PrepTreePlan& plan, int batch, cudaStream_t stream) {
+template <int kIn, int kP>
+cudaError_t launch_prep_tree_kp(const PrepTreePlan& plan, int batch, cudaStream_t stream) {
   constexpr int smem = tree_smem_bytes<kIn>();
-  cudaError_t e = cudaFuncSetAttribute(prep_tree_kernel<kIn>,
+  cudaError_t e = cudaFuncSetAttribute(prep_tree_kernel<kIn, kP>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  prep_tree_kernel<kIn><<<dim3(unsigned(plan.ntiles), batch), kTreeThreads, smem, stream>>>(plan);
+  prep_tree_kernel<kIn, kP>
+      <<<dim3(unsigned(plan.ntiles), batch), kTreeThreads, smem, stream>>>(plan);
   return cudaGetLastError();
 }
 
-cudaError_t launch_prep_tree(const PrepTreePlan& plan, int batch, cudaStream_t stream) {
+template <int kIn, int... P>
+cudaError_t launch_prep_tree_in(const PrepTreePlan& plan, int kp, int batch, cudaStream_t stream,
+                                std::integer_sequence<int, P...>) {
+  cudaError_t e = cudaErrorInvalidValue;
+  ((kp == P ? (e = launch_prep_tree_kp<kIn, P>(plan, batch, stream), true) : false) || ...);
+  return e;
+}
+
+// Whether every segment of group G holds basis p's table for G's side (left
+// operands the first table of the pair, right ones the second).
+bool group_holds_pair(const TreeGroup& G, int p) {
+  const TreeExprTable& T = kTreeExprTables[G.transpose ? 2 * p - 2 : 2 * p - 1];
+  bool all = G.nseg > 0;
+  for (int sg = 0; sg < G.nseg && all; ++sg) {
+    const TreeSeg& S = G.seg[sg];
+    all = S.nout == 7 && S.nmid >= 0 && S.nmid <= kTreeMid;
+    for (int o = 0; o < 7 && all; ++o)
+      for (int q = 0; q < kMaxOperandTerms && all; ++q) {
+        const int want = q < 4 ? T.e[o][q] : 0;
+        const int code = S.expr[o][q];
+        all = code == want && (code == 0 || std::abs(code) <= S.nmid);
+        if (code == 0) break;
+      }
+  }
+  return all;
+}
+
+// The basis whose tables the launch's groups hold (1..4; the first that any
+// group holds), with TreeGroup::table set on those groups; 0 when none does.
+int mark_tree_tables(PrepTreePlan& plan) {
+  for (int p = 1; 2 * p <= kTreeExprCount; ++p) {
+    int held = 0;
+    for (int g = 0; g < plan.ngroups; ++g) {
+      plan.group[g].table = group_holds_pair(plan.group[g], p) ? 1 : 0;
+      held += plan.group[g].table;
+    }
+    if (held) return p;
+  }
+  return 0;
+}
+
+cudaError_t launch_prep_tree(PrepTreePlan& plan, int batch, cudaStream_t stream) {
   if (plan.ngroups == 0 || plan.ntiles == 0 || batch == 0) return cudaSuccess;
   int nin = 0;
   for (int g = 0; g < plan.ngroups; ++g) {
     if (plan.group[g].nin < 0 || plan.group[g].nin > kTreeIn) return cudaErrorInvalidValue;
     nin = std::max(nin, plan.group[g].nin);
   }
-  return nin <= kTreeSmallIn ? launch_prep_tree_in<kTreeSmallIn>(plan, batch, stream)
-                             : launch_prep_tree_in<kTreeIn>(plan, batch, stream);
+  const int kp = mark_tree_tables(plan);
+  g_last_tree_table = kp;
+  constexpr auto pairs = std::make_integer_sequence<int, kTreeExprCount / 2 + 1>{};
+  return nin <= kTreeSmallIn ? launch_prep_tree_in<kTreeSmallIn>(plan, kp, batch, stream, pairs)
+                             : launch_prep_tree_in<kTreeIn>(plan, kp, batch, stream, pairs);
 }
+
+int last_tree_expr_table() { return g_last_tree_table; }
 
 cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* region,
                              long long row_len, long long rows, long long region_bstride,

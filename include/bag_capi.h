@@ -194,7 +194,7 @@ int bag_last_leaf_path(void);
 /* Leaf kernel the last call on this host thread ran: the FFMA kernels; the
  * 3xTF32 kernel with the basis transforms fused into its prologue (no
  * prepared-operand workspace); or, on prepared operands, 128 x 256 tiles on
- * one SM or 256 x 128 tiles on a cluster of two SMs.  New; diagnostic. */
+ * one SM or 256 x 256 tiles on a cluster of two SMs.  New; diagnostic. */
 enum {
   BAG_LEAF_KERNEL_FFMA = 0,
   BAG_LEAF_KERNEL_TF32_FUSED = 1,
@@ -202,6 +202,12 @@ enum {
   BAG_LEAF_KERNEL_TF32_PAIR = 3
 };
 int bag_last_leaf_kernel(void);
+/* Prepare kernel of the last call on this host thread: 1 Minimal, 2 Full,
+ * 3 Classic, 4 Winograd when every operand expression matched that basis's
+ * compiled-in tables (left and right operands), 0 for the kernel that reads
+ * the expressions from the plan, -1 when the last call prepared nothing.
+ * New; diagnostic. */
+int bag_last_prepare_table(void);
 
 /* Reads and clears the device error word (synchronous): non-zero when a
  * bounded in-kernel wait gave up instead of hanging (1) or a product reached a

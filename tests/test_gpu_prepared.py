@@ -8,7 +8,9 @@ source blocks, evaluated in FP32 in order (the first term with its sign, then
 one rounding per further term -- the reference's order, bag.cuh:69-73 and
 124-135), then split hi = rn_tf32(x), lo = rn_tf32(x - hi) with round to
 nearest, ties to even, on the 10-bit TF32 mantissa.  The comparison is exact:
-the prepared operands must not change when the prepare pass is restructured.
+the prepared operands must not change when the prepare pass is restructured,
+and the kernels with compiled-in basis expressions must write the same bits
+as the one that reads them from the plan.
 """
 
 from __future__ import annotations
@@ -47,7 +49,9 @@ def _signed_sum(xs, signs):
 
 
 CASES = [(256, 4096, 192, 2, "minimal"), (100, 4096, 72, 2, "minimal"),
-         (128, 2048, 128, 1, "full"), (96, 4096, 64, 2, "winograd"), (64, 8192, 64, 3, "minimal")]
+         (128, 2048, 128, 1, "full"), (96, 4096, 64, 2, "winograd"), (64, 8192, 64, 3, "minimal"),
+         (128, 4096, 96, 2, "classic"), (128, 2048, 64, 1, "classic"), (256, 4096, 256, 2, "full"),
+         (64, 2048, 128, 1, "winograd"), (96, 2048, 96, 1, "minimal")]
 
 
 @pytest.mark.parametrize("m,k,n,depth,basis", CASES)
@@ -67,6 +71,7 @@ def test_prepared_region_is_bit_exact(bag, cuda, m, k, n, depth, basis):
         bag.sgemm(ta, tb, tc, beta=0.0, depth=depth, basis=basis, workspace=ws)
         torch.cuda.synchronize()
         assert bag.last_leaf_kernel() in ("tf32_pair", "tf32_single")
+        table = bag.last_prepare_table()
     finally:
         bag.set_math_mode("ffma")
     assert plan["prepared"] and plan["prepared_region"][0] == 3
@@ -99,6 +104,10 @@ def test_prepared_region_is_bit_exact(bag, cuda, m, k, n, depth, basis):
         if not ok:
             bad.append(j)
     assert not bad, f"{len(bad)} of {len(plan['prepared'])} prepared operands differ, e.g. {bad[:5]}"
+    # Depths 1 and 2 of every basis run the kernel with the basis's operand
+    # expressions compiled in; the region above is the same bit for bit.
+    if depth <= 2:
+        assert table == {"minimal": 1, "full": 2, "classic": 3, "winograd": 4}[basis], table
     exact = a.astype(np.float64) @ b.astype(np.float64)
     got = tc.cpu().numpy()
     # The product on those operands: 3xTF32 at this depth is ~1.3e-6 (N(0,1)).
