@@ -544,7 +544,10 @@ struct Builder {
     if (leaves.empty() || leaves.size() > size_t(kMaxDecodeProducts)) return;
     size_t outs = 0;
     for (const HostLeaf& l : leaves) outs += l.out.size();
-    if (outs < 3 * leaves.size()) return;   // a store + a pass pays from ~3 targets a product
+    // Measured on B200: the atomic epilogue slows the leaf kernel more than
+    // a store and a pass cost, from depth 1 up (one level: ~1.7 targets a
+    // product; cfg5's leaves 5.1 -> 3.9 ms).
+    if (outs < leaves.size()) return;
     const int m = leaves[0].m, n = leaves[0].n;
     std::vector<View> targets;
     for (const HostLeaf& l : leaves) {

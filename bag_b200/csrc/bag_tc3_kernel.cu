@@ -1030,16 +1030,19 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
 }
 
 // ---- deferred inverse transform ---------------------------------------------
-// A CTA (one warp per target) takes a kDecodeRows-row slice of one column of
-// the common m x n extent.  Threads 0 .. nin-1 each bring that slice of one
-// product buffer (and, when accumulating, of one target) into shared memory
-// with one bulk copy (cp.async.bulk, completing on the CTA's mbarrier; a
-// slice is contiguous in the column-major blocks and a multiple of 16 bytes),
-// so staging costs a handful of instructions per CTA.  Then warp t adds its
-// target's products in plan order (lane l: rows 4l .. 4l+3 and 128+4l ..
+// A CTA (16 warps) takes a slice of plan.rows rows of one column of the
+// common m x n extent: 256 rows per warp of each target, so with few targets
+// (4 at depth 1) the slice grows to 1024 rows and every warp still works.
+// Threads 0 .. nin-1 each bring that slice of one product buffer (and, when
+// accumulating, of one target) into shared memory with one bulk copy
+// (cp.async.bulk, completing on the CTA's mbarrier; a slice is contiguous in
+// the column-major blocks and a multiple of 16 bytes), so staging costs a
+// handful of instructions per CTA.  Then warp w adds target w / W's products
+// in plan order over its 256 rows (lane l: rows 4l .. 4l+3 and 128+4l ..
 // 128+4l+3, so each float4 access of a warp covers 512 contiguous bytes) and
-// writes the slice once.  The wait is bounded like every wait here.
-constexpr int kDecodeRows = 256;
+// writes them once.  The wait is bounded like every wait here.
+constexpr int kDecodeWarpRows = 256;
+constexpr int kDecodeMaxSmem = 96 * 1024;
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, int bytes,
                                           unsigned long long* bar) {
@@ -1050,16 +1053,21 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, int bytes,
       : "memory");
 }
 
-__global__ void __launch_bounds__(kMaxDecodeTargets * 32) decode_kernel(
+// Three CTAs per SM (65 KB of staging each at cfg3 with beta 1): at most 40
+// registers a thread; with 48 only two fit, and the cfg3 pass took 1.5x.
+// kPer warps per target (a power of two); the slice is kPer x 256 rows.
+template <int kPer>
+__global__ void __launch_bounds__(kMaxDecodeTargets * 32, 3) decode_kernel(
     const __grid_constant__ DecodePlan plan) {
-  extern __shared__ __align__(128) float slice[];   // [np + nt][kDecodeRows]
+  extern __shared__ __align__(128) float slice[];   // [np + nt][span]
   __shared__ unsigned long long bar;
   __shared__ int abort;
-  const int slices = (plan.m + kDecodeRows - 1) / kDecodeRows;
-  const int col = int(blockIdx.x / slices), r0 = int(blockIdx.x % slices) * kDecodeRows;
+  constexpr int span = kPer * kDecodeWarpRows, per_target = kPer;
+  const int slices = (plan.m + span - 1) / span;
+  const int col = int(blockIdx.x / slices), r0 = int(blockIdx.x % slices) * span;
   const long long batch = blockIdx.y;
   const int nin = plan.np + (plan.accumulate ? plan.nt : 0);
-  const int rows = min(kDecodeRows, plan.m - r0);   // a multiple of 4 (m % 4 == 0)
+  const int rows = min(span, plan.m - r0);   // a multiple of 4 (m % 4 == 0)
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     abort = 0;
@@ -1070,18 +1078,19 @@ __global__ void __launch_bounds__(kMaxDecodeTargets * 32) decode_kernel(
   if (threadIdx.x < nin) {
     const int j = threadIdx.x;
     const Term& T = j < plan.np ? plan.in[j] : plan.out[j - plan.np];
-    bulk_load(slice + j * kDecodeRows, T.p + batch * T.bstride + (long long)col * T.ld + r0,
-              rows * 4, &bar);
+    bulk_load(slice + j * span, T.p + batch * T.bstride + (long long)col * T.ld + r0, rows * 4,
+              &bar);
   }
   if (!mbar_wait(abort, &bar, 0)) {
     if (threadIdx.x < nin) mbar_drain(&bar, 0);   // no copy outlives the CTA
     return;
   }
-  const int t = threadIdx.x / 32, lane = threadIdx.x % 32;
-  if (t >= plan.nt) return;
-  constexpr int kHalf = kDecodeRows / 2;
-  float acc[8];   // rows lane*4 + i (i < 4) and kHalf + lane*4 + (i - 4)
-  const float* own = slice + (plan.np + t) * kDecodeRows + lane * 4;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int t = warp / per_target, sub = (warp % per_target) * kDecodeWarpRows;
+  if (t >= plan.nt || sub >= rows) return;
+  constexpr int kHalf = kDecodeWarpRows / 2;
+  float acc[8];   // rows sub + lane*4 + i (i < 4) and sub + kHalf + lane*4 + (i - 4)
+  const float* own = slice + (plan.np + t) * span + sub + lane * 4;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     acc[i] = plan.accumulate ? own[i] : 0.f;
@@ -1089,7 +1098,7 @@ __global__ void __launch_bounds__(kMaxDecodeTargets * 32) decode_kernel(
   }
   for (int e = 0; e < plan.count[t]; ++e) {
     const int code = plan.list[t][e];
-    const float* v = slice + ((code > 0 ? code : -code) - 1) * kDecodeRows + lane * 4;
+    const float* v = slice + ((code > 0 ? code : -code) - 1) * span + sub + lane * 4;
     const float4 v0 = *reinterpret_cast<const float4*>(v);
     const float4 v1 = *reinterpret_cast<const float4*>(v + kHalf);
     const float s = code > 0 ? 1.f : -1.f;
@@ -1099,11 +1108,11 @@ __global__ void __launch_bounds__(kMaxDecodeTargets * 32) decode_kernel(
     acc[6] = fmaf(s, v1.z, acc[6]); acc[7] = fmaf(s, v1.w, acc[7]);
   }
   const Term& T = plan.out[t];
-  float* column = const_cast<float*>(T.p) + batch * T.bstride + (long long)col * T.ld + r0;
+  float* column = const_cast<float*>(T.p) + batch * T.bstride + (long long)col * T.ld + r0 + sub;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int r = h * kHalf + lane * 4;
-    if (r < rows)
+    if (sub + r < rows)
       *reinterpret_cast<float4*>(column + r) =
           make_float4(acc[4 * h], acc[4 * h + 1], acc[4 * h + 2], acc[4 * h + 3]);
   }
@@ -1317,20 +1326,41 @@ cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* re
                                : launch_bn<256>(plan, maps, batch, stream);
 }
 
-cudaError_t launch_decode(const DecodePlan& plan, int batch, cudaStream_t stream) {
-  if (plan.np == 0 || plan.nt == 0 || plan.m == 0 || plan.n == 0 || batch == 0) return cudaSuccess;
-  if (plan.m % 4) return cudaErrorInvalidValue;   // bulk copies move 16-byte multiples
-  const long long slices = (plan.m + kDecodeRows - 1) / kDecodeRows;
+cudaError_t launch_decode(const DecodePlan& plan_in, int batch, cudaStream_t stream) {
+  if (plan_in.np == 0 || plan_in.nt == 0 || plan_in.m == 0 || plan_in.n == 0 || batch == 0)
+    return cudaSuccess;
+  if (plan_in.m % 4) return cudaErrorInvalidValue;   // bulk copies move 16-byte multiples
+  if (plan_in.nt > kMaxDecodeTargets || plan_in.np > kMaxDecodeProducts)
+    return cudaErrorInvalidValue;
+  DecodePlan plan = plan_in;
+  const int nin = plan.np + (plan.accumulate ? plan.nt : 0);
+  // Warps per target: a power of two keeping all 16 warps busy, a slice no
+  // longer than the blocks need, and its staging within the shared-memory
+  // budget.
+  int per_target = 1;
+  while (2 * per_target * plan.nt <= kMaxDecodeTargets) per_target *= 2;
+  while (per_target > 1 && ((per_target / 2) * kDecodeWarpRows >= plan.m ||
+                            size_t(nin) * per_target * kDecodeWarpRows * 4 > kDecodeMaxSmem))
+    per_target /= 2;
+  plan.rows = per_target * kDecodeWarpRows;
+  const long long slices = (plan.m + plan.rows - 1) / plan.rows;
   const long long blocks = slices * plan.n;
   if (blocks > INT32_MAX) return cudaErrorInvalidValue;
-  const int nin = plan.np + (plan.accumulate ? plan.nt : 0);
-  const size_t smem = size_t(nin) * kDecodeRows * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(smem));
-  if (e != cudaSuccess) return e;
-  decode_kernel<<<dim3(unsigned(blocks), unsigned(batch)), kMaxDecodeTargets * 32, smem, stream>>>(
-      plan);
-  return cudaGetLastError();
+  const size_t smem = size_t(nin) * plan.rows * sizeof(float);
+  auto go = [&](auto kernel) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(smem));
+    if (e != cudaSuccess) return e;
+    kernel<<<dim3(unsigned(blocks), unsigned(batch)), kMaxDecodeTargets * 32, smem, stream>>>(plan);
+    return cudaGetLastError();
+  };
+  switch (per_target) {
+    case 1: return go(decode_kernel<1>);
+    case 2: return go(decode_kernel<2>);
+    case 4: return go(decode_kernel<4>);
+    case 8: return go(decode_kernel<8>);
+    default: return go(decode_kernel<16>);
+  }
 }
 
 cudaError_t run_wait_selftest(unsigned long long limit_ns, int* gave_up_device,

@@ -125,11 +125,12 @@ def test_winograd_plan_has_the_15_addition_structure(built_lib):
 # Prepared (3xTF32) plans: leaves need K >= 1024, so these keep M and N small
 # and K long.  (m, k, n, depth, basis, deferred decode expected)
 PREPARED = [
-    (64, 2048, 64, 1, "minimal", False),    # depth 1: products update C directly
-    (64, 4096, 64, 2, "minimal", True),     # 49 products, 16 targets: deferred decode
+    (64, 2048, 64, 1, "minimal", True),     # depth 1: 7 products, 4 targets: deferred decode
+    (64, 2048, 64, 1, "classic", True),
+    (64, 4096, 64, 2, "minimal", True),     # 49 products, 16 targets
     (64, 4096, 48, 2, "full", True),
     (64, 4096, 64, 2, "winograd", True),
-    (64, 4096, 64, 2, "classic", False),    # 144 updates / 49 products < 3: direct
+    (64, 4096, 64, 2, "classic", True),
     (77, 4096, 61, 2, "minimal", False),    # peeled M/N strips: leaf shapes differ
     (32, 8192, 32, 3, "minimal", False),    # 343 products: above the decode's 64
 ]
