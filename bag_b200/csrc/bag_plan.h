@@ -165,7 +165,6 @@ constexpr int kMaxDecodeTargets = 16;
 struct DecodePlan {
   int np, nt, m, n;
   int accumulate;                  // 1: out[t] += sum; 0: out[t] = sum
-  int rows;                        // rows per CTA slice (256 x warps per target; set at launch)
   Term in[kMaxDecodeProducts];     // M_p (coef unused)
   Term out[kMaxDecodeTargets];     // C blocks (coef unused)
   // Per target, its products in plan order: +-(p + 1); count[t] of them.

@@ -1030,7 +1030,7 @@ __global__ void __launch_bounds__(pairk::kThreads, 1)
 }
 
 // ---- deferred inverse transform ---------------------------------------------
-// A CTA (16 warps) takes a slice of plan.rows rows of one column of the
+// A CTA (16 warps) takes a slice of kPer x 256 rows of one column of the
 // common m x n extent: 256 rows per warp of each target, so with few targets
 // (4 at depth 1) the slice grows to 1024 rows and every warp still works.
 // Threads 0 .. nin-1 each bring that slice of one product buffer (and, when
@@ -1326,13 +1326,11 @@ cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* re
                                : launch_bn<256>(plan, maps, batch, stream);
 }
 
-cudaError_t launch_decode(const DecodePlan& plan_in, int batch, cudaStream_t stream) {
-  if (plan_in.np == 0 || plan_in.nt == 0 || plan_in.m == 0 || plan_in.n == 0 || batch == 0)
+cudaError_t launch_decode(const DecodePlan& plan, int batch, cudaStream_t stream) {
+  if (plan.np == 0 || plan.nt == 0 || plan.m == 0 || plan.n == 0 || batch == 0)
     return cudaSuccess;
-  if (plan_in.m % 4) return cudaErrorInvalidValue;   // bulk copies move 16-byte multiples
-  if (plan_in.nt > kMaxDecodeTargets || plan_in.np > kMaxDecodeProducts)
-    return cudaErrorInvalidValue;
-  DecodePlan plan = plan_in;
+  if (plan.m % 4) return cudaErrorInvalidValue;   // bulk copies move 16-byte multiples
+  if (plan.nt > kMaxDecodeTargets || plan.np > kMaxDecodeProducts) return cudaErrorInvalidValue;
   const int nin = plan.np + (plan.accumulate ? plan.nt : 0);
   // Warps per target: a power of two keeping all 16 warps busy, a slice no
   // longer than the blocks need, and its staging within the shared-memory
@@ -1342,11 +1340,11 @@ cudaError_t launch_decode(const DecodePlan& plan_in, int batch, cudaStream_t str
   while (per_target > 1 && ((per_target / 2) * kDecodeWarpRows >= plan.m ||
                             size_t(nin) * per_target * kDecodeWarpRows * 4 > kDecodeMaxSmem))
     per_target /= 2;
-  plan.rows = per_target * kDecodeWarpRows;
-  const long long slices = (plan.m + plan.rows - 1) / plan.rows;
+  const int span = per_target * kDecodeWarpRows;
+  const long long slices = (plan.m + span - 1) / span;
   const long long blocks = slices * plan.n;
   if (blocks > INT32_MAX) return cudaErrorInvalidValue;
-  const size_t smem = size_t(nin) * plan.rows * sizeof(float);
+  const size_t smem = size_t(nin) * span * sizeof(float);
   auto go = [&](auto kernel) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          int(smem));
