@@ -68,17 +68,21 @@ thread_local int g_last_prep_kind = -1;
 constexpr int kTcMinK = 1024;
 
 // BAG_DEPTH_AUTO: the depth is chosen from the shape and this thread's math
-// mode.  Measured on B200 (square N(0,1) problems, effective TFLOP/s):
-// 3xTF32 is best with leaves of at least 8192 (N=4096: d0 193, d1 177;
-// N=8192: d0 231, d1 229; N=16384: d0 207, d1 231, d2 224 -- a 16384-long K
-// panel no longer fits L2), FFMA one level deeper per doubling from 2048
-// (N=4096: d1 49, d2 53; N=8192: d2 58, d3 55; N=16384: d2 60, d3 63).
+// mode.  Measured on B200 (N(0,1) inputs, effective TFLOP/s, depths 0/1/2/3):
+// 3xTF32 -- 2048^3: 148/144; 4096^3: 187/205/189; 8192^3: 227/252/247/137;
+// 16384^3: 218/238/266/203; 8192x4096x16384 (m x n x k): 220/239/230/154;
+// 10000^3: 212/239/233 -- so no recursion below 4096, at least one level
+// from 4096, and further levels while the leaves stay >= 4096 (shorter leaves
+// pay the prepare and decode passes for less saved work).  FFMA one level
+// deeper per doubling from 2048 (N=4096: d1 49, d2 53; N=8192: d2 58, d3 55;
+// N=16384: d2 60, d3 63).
 int resolve_depth(int depth, int m, int n, int k) {
   if (depth != BAG_DEPTH_AUTO) return depth;
   const int s = std::min(m, std::min(n, k));
   if (g_math_mode == BAG_MATH_3XTF32) {
-    int d = 0;
-    while (d < 3 && (s >> (d + 1)) >= 8192) ++d;
+    if (s < 4096) return 0;
+    int d = 1;
+    while (d < 3 && (s >> (d + 1)) >= 4096) ++d;
     return d;
   }
   return s >= 16384 ? 3 : s >= 2048 ? 2 : s >= 1024 ? 1 : 0;

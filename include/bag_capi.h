@@ -60,8 +60,9 @@ enum {
 enum { BAG_LAYOUT_COL_MAJOR = 0, BAG_LAYOUT_ROW_MAJOR = 1 };
 /* `depth` of bag_sgemm_ex / _batched / _noalloc, bag_workspace_create_ex and
  * bag_plan_dump: choose the recursion depth from the shape and the calling
- * thread's math mode (3XTF32: leaves of at least 8192; FFMA: depth 3 from
- * 16384, 2 from 2048, 1 from 1024).  New; the reference takes explicit levels. */
+ * thread's math mode (3XTF32: none below 4096, at least one level from 4096,
+ * more while the leaves stay >= 4096; FFMA: depth 3 from 16384, 2 from 2048,
+ * 1 from 1024).  New; the reference takes explicit levels. */
 enum { BAG_DEPTH_AUTO = -1 };
 /* Leaf arithmetic (bag_set_math_mode).  FFMA: every output a sequential fmaf
  * chain, the reference's SIMT numerics.  3XTF32: tcgen05 tensor cores on

@@ -95,8 +95,9 @@ def test_plan_workspace_alignment(bag):
                 assert ref[0] == 3 and ref[1] % 64 == 0 and ref[2] % 4 == 0
 
 
-@pytest.mark.parametrize("mode,n,leaf", [("3xtf32", 4096, 4096), ("3xtf32", 8192, 8192),
-                                         ("3xtf32", 16384, 8192), ("3xtf32", 32768, 8192),
+@pytest.mark.parametrize("mode,n,leaf", [("3xtf32", 2048, 2048), ("3xtf32", 4096, 2048),
+                                         ("3xtf32", 8192, 4096), ("3xtf32", 10000, 5000),
+                                         ("3xtf32", 16384, 4096), ("3xtf32", 32768, 4096),
                                          ("ffma", 4096, 1024), ("ffma", 8192, 2048),
                                          ("ffma", 16384, 2048), ("ffma", 512, 512)])
 def test_auto_depth_follows_the_measured_policy(built_lib, mode, n, leaf):
@@ -107,7 +108,7 @@ def test_auto_depth_follows_the_measured_policy(built_lib, mode, n, leaf):
     finally:
         bag.set_math_mode("ffma")
     assert {l["m"] for l in pl["leaves"]} == {leaf}
-    depth = (n // leaf).bit_length() - 1
+    depth = round(n / leaf).bit_length() - 1
     assert len(pl["leaves"]) == 7 ** depth
 
 
