@@ -796,11 +796,14 @@ int prep_leaf_kind() {
   return prep_pair_supported() ? kPrepLeafPair : kPrepLeafSingle;
 }
 
-void run_prepared(Builder& B, int batch, cudaStream_t stream) {
+// The prepare pass's launches: up to kMaxTreeGroups tree groups each.
+std::vector<PrepTreePlan> tree_plans(const Builder& B) {
   static_assert(kPrepTreeK <= 64 && 64 % kPrepTreeK == 0, "rows are padded to 64 k");
   const std::vector<Builder::TreeGroupHost>& groups = B.trees;
+  std::vector<PrepTreePlan> plans;
   for (size_t g0 = 0; g0 < groups.size(); g0 += kMaxTreeGroups) {
-    PrepTreePlan pp;
+    plans.emplace_back();
+    PrepTreePlan& pp = plans.back();
     std::memset(&pp, 0, sizeof(pp));
     pp.row_len = B.prep_row_len;
     pp.region = const_cast<float*>(B.prep_region.p);
@@ -835,6 +838,12 @@ void run_prepared(Builder& B, int batch, cudaStream_t stream) {
     }
     pp.ntiles = tiles;
     if (tiles > INT32_MAX) fail(BAG_ERR_SHAPE, "problem too large");
+  }
+  return plans;
+}
+
+void run_prepared(Builder& B, int batch, cudaStream_t stream) {
+  for (PrepTreePlan& pp : tree_plans(B)) {
     cuda_check(launch_prep_tree(pp, batch, stream), "prepare launch");
     ++g_launches;
   }
@@ -1367,6 +1376,21 @@ std::string dump_plan(int m, int n, int k, long long lda, long long ldb, long lo
       s += std::string(t ? "," : "") + "[" + ref(vb.def[t].v) + "," +
            std::to_string(int(vb.def[t].coef)) + "]";
     s += "]}";
+  }
+  s += "]";
+  // Per prepare launch: the compiled-in basis tables its kernel would use
+  // (1 Minimal .. 4 Winograd, 0 none) and which of its groups take them --
+  // computed by the function the launcher calls.
+  s += ",\"prepare_tables\":[";
+  if (!B.trees.empty()) {
+    std::vector<PrepTreePlan> plans = tree_plans(B);
+    for (size_t i = 0; i < plans.size(); ++i) {
+      const int p = mark_tree_tables(plans[i]);
+      s += std::string(i ? "," : "") + "{\"basis_tables\":" + std::to_string(p) + ",\"groups\":[";
+      for (int gi = 0; gi < plans[i].ngroups; ++gi)
+        s += std::string(gi ? "," : "") + std::to_string(plans[i].group[gi].table);
+      s += "]}";
+    }
   }
   s += "]";
   s += ",\"prepared_region\":" + (B.prep_region.p ? ref(B.prep_region) : std::string("null"));

@@ -77,6 +77,10 @@ constexpr int kPrepTreeK = 64;
 // 2 Full, 3 Classic, 4 Winograd; 0 = the plan-reading kernel).
 constexpr int kTreeExprCount = 8;
 int last_tree_expr_table();
+// Flags the groups of `plan` whose segments hold one basis's compiled-in
+// tables (TreeGroup::table) and returns that basis (1..4), 0 when none does;
+// launch_prep_tree calls it, plan dumps report it.
+int mark_tree_tables(PrepTreePlan& plan);
 TileShape prep_tile_shape(int kind);
 cudaError_t launch_prep_tree(PrepTreePlan& plan, int batch, cudaStream_t stream);  // sets group[].table
 cudaError_t launch_leaf_prep(const PrepLeafPlan& plan, int kind, const float* region,

@@ -245,3 +245,44 @@ def test_plan_sim_catches_a_corrupted_prepared_plan(built_lib):
     term = bad["decode"]["terms"][10][0]
     term[0] = (term[0] + 1) % len(bad["decode"]["target_refs"])
     assert O.rel_frobenius(run_plan(bad, a, b, c, m, k, m), ref) > 1e-2
+
+
+@pytest.mark.parametrize("m,k,n,depth,basis,table", [
+    (2048, 2048, 2048, 1, "minimal", 1), (4096, 4096, 4096, 2, "minimal", 1),
+    (2048, 2048, 2048, 1, "full", 2), (4096, 4096, 4096, 2, "full", 2),
+    (2048, 2048, 2048, 1, "classic", 3), (4096, 4096, 4096, 2, "classic", 3),
+    (2048, 2048, 2048, 1, "winograd", 4), (4096, 4096, 4096, 2, "winograd", 4),
+    (64, 8192, 64, 3, "minimal", 1)])
+def test_prepare_launch_takes_the_compiled_in_tables(built_lib, m, k, n, depth, basis, table):
+    """The prepare kernel has each basis's operand expressions compiled in
+    (bag_tc3_kernel.cu) and takes them only when every segment the plan
+    builder produced matches; this pins the builder's expression order to
+    those tables, so a change to either shows here instead of as a silent
+    fall back to the plan-reading kernel."""
+    import bag_b200 as bag
+    bag.set_math_mode("3xtf32")
+    try:
+        plan = bag.plan_dump(m, n, k, m, k, m, depth, basis)
+    finally:
+        bag.set_math_mode("ffma")
+    launches = plan["prepare_tables"]
+    assert launches and all(l["basis_tables"] == table for l in launches)
+    assert all(all(launch["groups"]) for launch in launches)
+
+
+def test_ragged_prepare_keeps_the_tables_for_the_main_groups(built_lib):
+    """Peeled strips of a ragged shape are single-input groups: they read
+    their terms from the plan inside the same launch, the main groups keep
+    the compiled-in tables."""
+    import bag_b200 as bag
+    bag.set_math_mode("3xtf32")
+    try:
+        plan = bag.plan_dump(100, 72, 4096, 100, 4096, 100, 2, "minimal")
+    finally:
+        bag.set_math_mode("ffma")
+    (launch,) = plan["prepare_tables"]
+    assert launch["basis_tables"] == 1
+    groups = plan["prep_groups"]
+    assert len(launch["groups"]) == len(groups)
+    for flag, g in zip(launch["groups"], groups):
+        assert flag == (1 if len(g["in"]) > 1 else 0)
