@@ -390,6 +390,65 @@ __device__ __forceinline__ void table_operands(const float4 (&md)[kTreeMid], con
   (store_hi_lo(base + (long long)S.out_hi[O] * ld, plane, table_operand<kX, O>(md)), ...);
 }
 
+// The operands of one tile from its staged inputs ([input][row][k], pitch
+// kTreePitch): per segment, the mids in registers, then each operand split
+// into TF32 hi/lo and stored (rows past the group's are skipped).
+template <int kP>
+__device__ __forceinline__ void tree_operands(const PrepTreePlan& plan, const TreeGroup& G,
+                                              const float* staged, int r0, int k0,
+                                              long long batch, int t) {
+  const int row = t / (kTreeK / 4), kc = 4 * (t % (kTreeK / 4));
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int r = r0 + row;
+  if (r >= G.rows) return;
+  auto input = [&](int u) {
+    return *reinterpret_cast<const float4*>(staged + (u * kTreeRows + row) * kTreePitch + kc);
+  };
+  float* region = plan.region + batch * plan.region_bstride;
+  const long long ld = plan.row_len;
+  for (int sg = 0; sg < G.nseg; ++sg) {
+    const TreeSeg& S = G.seg[sg];
+    float4 md[kTreeMid];
+#pragma unroll
+    for (int i = 0; i < kTreeMid; ++i) {
+      md[i] = zero;
+      if (i < S.nmid) {
+#pragma unroll
+        for (int q = 0; q < kMaxOperandTerms; ++q) {
+          const int code = S.mid[i][q];
+          if (code == 0) break;
+          md[i] = signed_add(md[i], input((code > 0 ? code : -code) - 1), code, q == 0);
+        }
+      }
+    }
+    bool tabled = false;
+    if constexpr (kP > 0) {
+      if (G.table) {
+        float* base = region + (long long)r * ld + k0 + kc;
+        const long long plane = (long long)G.rows * ld;
+        if (G.transpose)
+          table_operands<2 * kP - 1>(md, S, base, ld, plane, std::make_integer_sequence<int, 7>{});
+        else
+          table_operands<2 * kP>(md, S, base, ld, plane, std::make_integer_sequence<int, 7>{});
+        tabled = true;
+      }
+    }
+    if (!tabled) {
+      for (int o = 0; o < S.nout; ++o) {
+        float4 x = zero;
+#pragma unroll
+        for (int q = 0; q < kMaxOperandTerms; ++q) {
+          const int code = S.expr[o][q];
+          if (code == 0) break;
+          x = signed_add(x, pick_mid(md, (code > 0 ? code : -code) - 1), code, q == 0);
+        }
+        store_hi_lo(region + (long long)(S.out_hi[o] + r) * ld + k0 + kc, (long long)G.rows * ld,
+                    x);
+      }
+    }
+  }
+}
+
 template <int kIn, int kP>
 __global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 5 : 3)
     prep_tree_kernel(const __grid_constant__ PrepTreePlan plan) {
@@ -470,54 +529,7 @@ __global__ void __launch_bounds__(kTreeThreads, kIn <= kTreeSmallIn ? 5 : 3)
     }
   }
   __syncthreads();
-  const int r = r0 + row;
-  if (r >= G.rows) return;
-  auto input = [&](int u) {
-    return *reinterpret_cast<const float4*>(staged + (u * kTreeRows + row) * kTreePitch + kc);
-  };
-  float* region = plan.region + batch * plan.region_bstride;
-  const long long ld = plan.row_len;
-  for (int sg = 0; sg < G.nseg; ++sg) {
-    const TreeSeg& S = G.seg[sg];
-    float4 md[kTreeMid];
-#pragma unroll
-    for (int i = 0; i < kTreeMid; ++i) {
-      md[i] = zero;
-      if (i < S.nmid) {
-#pragma unroll
-        for (int q = 0; q < kMaxOperandTerms; ++q) {
-          const int code = S.mid[i][q];
-          if (code == 0) break;
-          md[i] = signed_add(md[i], input((code > 0 ? code : -code) - 1), code, q == 0);
-        }
-      }
-    }
-    bool tabled = false;
-    if constexpr (kP > 0) {
-      if (G.table) {
-        float* base = region + (long long)r * ld + k0 + kc;
-        const long long plane = (long long)G.rows * ld;
-        if (G.transpose)
-          table_operands<2 * kP - 1>(md, S, base, ld, plane, std::make_integer_sequence<int, 7>{});
-        else
-          table_operands<2 * kP>(md, S, base, ld, plane, std::make_integer_sequence<int, 7>{});
-        tabled = true;
-      }
-    }
-    if (!tabled) {
-      for (int o = 0; o < S.nout; ++o) {
-        float4 x = zero;
-#pragma unroll
-        for (int q = 0; q < kMaxOperandTerms; ++q) {
-          const int code = S.expr[o][q];
-          if (code == 0) break;
-          x = signed_add(x, pick_mid(md, (code > 0 ? code : -code) - 1), code, q == 0);
-        }
-        store_hi_lo(region + (long long)(S.out_hi[o] + r) * ld + k0 + kc, (long long)G.rows * ld,
-                    x);
-      }
-    }
-  }
+  tree_operands<kP>(plan, G, staged, r0, k0, batch, t);
 }
 
 // ---- leaf products on prepared operands -------------------------------------
