@@ -238,30 +238,35 @@ def test_bounded_wait_gives_up_and_context_survives(tensor_mode):
         bag.selftest_bounded_wait(0)
 
 
-# Deferred inverse transform (depth 2, one leaf shape): products store into
-# their own buffers and one pass adds them into C -- accumulating (beta 1) or
-# overwriting without zeroing C first (beta 0, C starts as garbage here).
-@pytest.mark.parametrize("m,n,beta", [(2048, 2048, 0.0), (2048, 2048, 1.0), (2064, 1040, 1.0),
-                                      (1040, 2064, 0.0)])
-def test_deferred_decode(tensor_mode, m, n, beta):
+# Deferred inverse transform (one leaf shape): products store into their own
+# buffers and one pass adds them into C -- accumulating (beta 1) or
+# overwriting without zeroing C first (beta 0, C starts as garbage here).  At
+# depth 1 (4 target blocks) a CTA slice is 512 or 1024 rows; the shapes below
+# give a block shorter than one slice (500 rows), a last slice of 8 rows
+# (520) and whole 1024-row slices.
+@pytest.mark.parametrize("m,n,depth,beta", [
+    (2048, 2048, 2, 0.0), (2048, 2048, 2, 1.0), (2064, 1040, 2, 1.0), (1040, 2064, 2, 0.0),
+    (2048, 2048, 1, 0.0), (2048, 2048, 1, 1.0), (2000, 1000, 1, 0.0), (2064, 1040, 1, 1.0),
+    (1040, 2064, 1, 0.0)])
+def test_deferred_decode(tensor_mode, m, n, depth, beta):
     import torch
     bag = tensor_mode
-    k = 4096
-    assert bag.plan_dump(n, m, k, n, k, n, depth=2)["decode"]["deferred"]
+    k = 2048 * depth
+    assert bag.plan_dump(n, m, k, n, k, n, depth=depth)["decode"]["deferred"]
     g = torch.Generator(device="cuda").manual_seed(17)
     a = torch.randn(m, k, device="cuda", generator=g)
     b = torch.randn(k, n, device="cuda", generator=g)
     c0 = torch.randn(m, n, device="cuda", generator=g) if beta else torch.full((m, n), float("nan"), device="cuda")
-    ws = bag.Workspace.for_problem(n, m, k, 2)
+    ws = bag.Workspace.for_problem(n, m, k, depth)
     c = c0.clone()
-    bag.sgemm(a, b, c, beta=beta, depth=2, workspace=ws)
+    bag.sgemm(a, b, c, beta=beta, depth=depth, workspace=ws)
     torch.cuda.synchronize()
     assert bag.last_leaf_kernel() == "tf32_pair" and bag.device_error() == 0
     exact = a.double() @ b.double() + (c0.double() if beta else 0.0)
     assert float((c.double() - exact).norm() / exact.norm()) <= 2e-6
     # Deterministic: the pass adds the products in plan order.
     c2 = c0.clone()
-    bag.sgemm(a, b, c2, beta=beta, depth=2, workspace=ws)
+    bag.sgemm(a, b, c2, beta=beta, depth=depth, workspace=ws)
     torch.cuda.synchronize()
     assert torch.equal(c, c2)
 
