@@ -93,3 +93,15 @@ def test_profile_calls_runs_one_case_without_rounds(cuda, tmp_path, capsys):
 def test_profile_calls_needs_one_case():
     with pytest.raises(SystemExit):
         D.parse(["--profile-calls", "1"])
+
+
+def test_depth_sweep_arguments():
+    """The depth-sweep tool (measurement behind BAG_DEPTH_AUTO) parses square
+    and rectangular shapes and rejects malformed ones, without a GPU."""
+    from bag_b200 import depth_sweep as D
+    args = D.parse_args(["--shapes", "4096,8192x4096x16384", "--depths", "1,2"])
+    assert args.shapes == [(4096, 4096, 4096), (8192, 4096, 16384)]
+    assert args.depths == [1, 2] and args.math == "3xtf32"
+    for bad in ("0", "8x8", "axb", "8x8x-8"):
+        with pytest.raises(ValueError):
+            D.parse_shape(bad)
